@@ -1,0 +1,42 @@
+"""Plan -> sm_100a kernel sources.
+
+``generate`` walks the fused plan in order and dispatches on ``Kernel.kind``
+exactly like the reference backend (``tensorjit/backends/cuda_backend.py:437-456``):
+elementwise/copy -> vectorised grid-stride kernel, row -> staged row kernel,
+reduce -> row kernel with one stage, matmul -> tcgen05 GEMM (bf16/f16) or the
+SIMT GEMM (everything else).
+"""
+from __future__ import annotations
+
+from ..plan import PProgram
+from .common import KernelSource
+from .ewise import gen_elementwise
+from .gemm import gen_gemm_simt, gen_gemm_tc, tc_eligible
+from .row import gen_row
+
+
+def generate(plan: PProgram, tiles: dict | None = None, prefix: str = "tj") -> list[KernelSource]:
+    out: list[KernelSource] = []
+    for idx, k in enumerate(plan.kernels):
+        sym = f"{prefix}_{k.kind}_{idx}"
+        if k.kind in ("elementwise", "copy"):
+            ks = gen_elementwise(k, sym)
+        elif k.kind == "row":
+            ks = gen_row(k, k.stages, tuple(k.rows), int(k.n), sym)
+        elif k.kind == "reduce":
+            x = k.anchor.inputs[0]
+            ks = gen_row(k, [k], tuple(x.shape[:-1]), int(x.shape[-1]) if x.shape else 1, sym)
+        elif k.kind == "matmul":
+            if tc_eligible(k):
+                ks = gen_gemm_tc(k, sym, idx, (tiles or {}).get(idx))
+            else:
+                ks = gen_gemm_simt(k, sym)
+        else:
+            raise NotImplementedError(f"kernel kind {k.kind!r} is not supported by the b200 backend")
+        ks.info["kind"] = k.kind
+        ks.info["index"] = idx
+        out.append(ks)
+    return out
+
+
+__all__ = ["generate", "KernelSource"]

@@ -1,0 +1,208 @@
+"""Shared pieces of the sm_100a code generator: op expressions, C types,
+kernel-source records and index arithmetic.
+
+The generator emits one small CUDA translation unit per plan kernel: a
+parameter-block struct, the kernel entry point, and the fused pointwise DAG
+written out as straight-line f32 code.  The heavy lifting (vector memory
+access, reductions, the tcgen05 GEMM pipeline) lives in the hand-written
+headers under ``csrc/kernels``; the generated part only binds sizes, strides
+and the DAG as compile-time constants.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Optional
+
+from ..plan import PKernel, PNode
+
+CTYPE = {"f32": "float", "f16": "__half", "bf16": "__nv_bfloat16", "i32": "int"}
+ITEM = {"f32": 4, "f16": 2, "bf16": 2, "i32": 4}
+NUM_SMS = 148
+
+# CUDA expression per op (tensorjit/backends/common.py:65-88).  The helper
+# functions are defined in csrc/kernels/tj_common.cuh with the same formulas.
+EXPR = {
+    "neg": "(-{0})",
+    "exp": "expf({0})",
+    "log": "logf({0})",
+    "sqrt": "sqrtf({0})",
+    "rsqrt": "tj_rsqrt({0})",
+    "tanh": "tanhf({0})",
+    "relu": "tj_relu({0})",
+    "sigmoid": "tj_sigmoid({0})",
+    "gelu": "tj_gelu({0})",
+    "silu": "tj_silu({0})",
+    "abs": "fabsf({0})",
+    "add": "({0} + {1})",
+    "sub": "({0} - {1})",
+    "mul": "({0} * {1})",
+    "div": "({0} / {1})",
+    "pow": "powf({0}, {1})",
+    "maximum": "fmaxf({0}, {1})",
+    "minimum": "fminf({0}, {1})",
+    "where": "tj_where({0}, {1}, {2})",
+}
+
+
+def literal(v: float) -> str:
+    """f32 literal for a scalar constant (``common.py:113-119``)."""
+    v = float(v)
+    if v != v:
+        return "__int_as_float(0x7fffffff)"
+    if v == float("inf"):
+        return "__int_as_float(0x7f800000)"
+    if v == float("-inf"):
+        return "__int_as_float(0xff800000)"
+    return f"{v!r}f"
+
+
+def is_scalar_const(n: PNode) -> bool:
+    return n.op == "const" and n.shape == ()
+
+
+def expr(node: PNode, operand: dict[int, str]) -> str:
+    """Expression of one elementwise node given operand names (scalar consts inline)."""
+    args = []
+    for i in node.inputs:
+        if is_scalar_const(i):
+            args.append(literal(i.attrs["value"]))
+        elif i.op == "const":
+            args.append(literal(i.attrs["value"]))   # shaped const: every element has the value
+        else:
+            args.append(operand[i.id])
+    if node.op in ("transpose", "broadcast_to"):
+        return args[0]
+    return EXPR[node.op].format(*args)
+
+
+@dataclass
+class TMapSpec:
+    arg: int                  # index into the kernel's argument list
+    dtype: str                # plan dtype
+    dims: list[int]           # innermost first (elements)
+    strides: list[int]        # bytes, dims 1..rank-1
+    box: list[int]
+    swizzle: int              # CUtensorMapSwizzle
+    param_offset: int = 0
+    l2_promotion: int = 2     # CU_TENSOR_MAP_L2_PROMOTION_L2_128B
+
+
+TMAP_DTYPE = {"f16": 6, "f32": 7, "bf16": 9}
+
+
+@dataclass
+class KernelSource:
+    symbol: str
+    family: str                         # ewise | copy | row | gemm_simt | gemm_tc
+    source: str
+    grid: tuple
+    block: tuple
+    args: list                          # list of ("node", PNode) | ("status", None)
+    smem: int = 0
+    cluster: tuple = (1, 1, 1)
+    tmaps: list = field(default_factory=list)
+    param_bytes: int = 0
+    info: dict = field(default_factory=dict)
+
+    def finalize_params(self) -> None:
+        """Lay the parameter block out exactly as nvcc lays out the generated struct:
+        pointers first, then 64-byte aligned CUtensorMaps."""
+        n = len(self.args)
+        if self.tmaps:
+            off = (8 * n + 63) // 64 * 64
+            for t in self.tmaps:
+                t.param_offset = off
+                off += 128
+            self.param_bytes = off
+        else:
+            self.param_bytes = 8 * n
+
+
+def params_struct(nptr: int, ntmap: int) -> str:
+    lines = ["struct Params {", f"  void* p[{max(nptr, 1)}];"]
+    if ntmap:
+        lines.append(f"  CUtensorMap tm[{ntmap}];")
+    lines.append("};")
+    return "\n".join(lines)
+
+
+def prod(xs) -> int:
+    return math.prod(xs) if xs else 1
+
+
+def coalesce(shape: tuple, stride_sets: list[tuple]) -> tuple[tuple, list[tuple]]:
+    """Merge adjacent iteration dims whenever every operand's strides allow it
+    (``stride[d] == stride[d+1] * shape[d+1]``), and drop size-1 dims.  Fewer
+    dims means cheaper index decomposition in the generated loops."""
+    dims = [(s, [st[d] for st in stride_sets]) for d, s in enumerate(shape) if s != 1]
+    if not dims:
+        return (), [() for _ in stride_sets]
+    out = [dims[0]]
+    for s, sts in dims[1:]:
+        ps, psts = out[-1]
+        if all(a == b * s for a, b in zip(psts, sts)):
+            out[-1] = (ps * s, sts)
+        else:
+            out.append((s, sts))
+    new_shape = tuple(s for s, _ in out)
+    new_strides = [tuple(sts[i] for _, sts in out) for i in range(len(stride_sets))]
+    return new_shape, new_strides
+
+
+def offset_expr(idx_vars: list[str], strides: tuple) -> str:
+    terms = []
+    for v, s in zip(idx_vars, strides):
+        if s == 0:
+            continue
+        terms.append(v if s == 1 else f"{v} * {s}L")
+    return " + ".join(terms) if terms else "0L"
+
+
+def decompose_stmts(linear: str, shape: tuple, prefix: str) -> tuple[list[str], list[str]]:
+    """Split a linear index over ``shape`` into per-dim indices (compile-time divisors)."""
+    stmts, names = [], []
+    rem = linear
+    cs = []
+    acc = 1
+    for s in reversed(shape):
+        cs.append(acc)
+        acc *= s
+    cs = list(reversed(cs))
+    for d, (s, st) in enumerate(zip(shape, cs)):
+        name = f"{prefix}{d}"
+        names.append(name)
+        if d == 0 and len(shape) > 1:
+            stmts.append(f"const long {name} = ({rem}) / {st}L;")
+            stmts.append(f"const long {prefix}r{d} = ({rem}) - {name} * {st}L;")
+            rem = f"{prefix}r{d}"
+        elif d == len(shape) - 1:
+            stmts.append(f"const long {name} = {rem};")
+        else:
+            stmts.append(f"const long {name} = ({rem}) / {st}L;")
+            stmts.append(f"const long {prefix}r{d} = ({rem}) - {name} * {st}L;")
+            rem = f"{prefix}r{d}"
+    return stmts, names
+
+
+HEADER = '#include "tj_common.cuh"\n'
+
+
+def node_var(n: PNode) -> str:
+    return f"v{n.id}"
+
+
+def kernel_io(k: PKernel) -> tuple[list[PNode], list[PNode]]:
+    return list(k.inputs), list(k.outputs)
+
+
+def pick_vec(dtypes: list[str]) -> int:
+    """Elements per 16-byte access for the widest dtype among the operands."""
+    return 16 // max(ITEM[d] for d in dtypes)
+
+
+def find_consumer(n: PNode, nodes: list[PNode]) -> Optional[PNode]:
+    for c in nodes:
+        if any(i is n for i in c.inputs):
+            return c
+    return None

@@ -1,0 +1,349 @@
+"""Matmul kernels with the fused pointwise epilogue.
+
+Plan semantics (``tensorjit/backends/cuda_backend.py:299-429``, C twin
+``c_backend.py:186-304``): ``C[b,i,j] = sum_k A[b,i,k] * B[b,k,j]`` (``B[b,j,k]``
+when ``trans_b``), batch dims broadcast with stride 0 (``cuda_backend.py:330-340``),
+accumulate in f32, then evaluate every epilogue node per output element in f32
+and store each escaping node in its dtype.
+
+Two implementations:
+
+* ``tc``   bf16/f16 operands: the persistent tcgen05 kernel of
+  ``csrc/kernels/gemm_sm100.cuh`` (TMA -> 128B-swizzled smem -> tcgen05.mma ->
+  TMEM -> epilogue).  Needs K % 8 == 0 (16-byte TMA row pitch) and, for an
+  N-major B, N % 8 == 0.
+* ``simt`` every other case (f32 operands, odd pitches, K == 0): a 64x64 tile,
+  4x4 register micro-tile FFMA kernel with bounds checks, f32 accumulate.
+"""
+from __future__ import annotations
+
+import os
+
+from ..plan import PKernel, PNode, access_strides, contiguous_strides, first_consumer
+from .common import (CTYPE, HEADER, ITEM, NUM_SMS, TMAP_DTYPE, KernelSource, TMapSpec, decompose_stmts, expr,
+                     offset_expr, params_struct, prod)
+
+
+def _mm_dims(k: PKernel):
+    mm = k.anchor
+    a, b = mm.inputs
+    tb = bool(mm.attrs.get("trans_b"))
+    M, K = a.shape[-2], a.shape[-1]
+    N = b.shape[-2] if tb else b.shape[-1]
+    out_shape = tuple(mm.shape)
+    return mm, a, b, tb, M, N, K, out_shape
+
+
+def _batch_strides(t: PNode, batch_shape: tuple) -> tuple:
+    """Per-batch-dim stride of operand ``t`` in units of whole matrices (0 = broadcast)."""
+    mshape = t.shape[:-2]
+    cs = contiguous_strides(mshape) if mshape else ()
+    pad = len(batch_shape) - len(mshape)
+    st = [0] * pad
+    for d in range(len(mshape)):
+        st.append(0 if mshape[d] == 1 and batch_shape[pad + d] != 1 else cs[d])
+    return tuple(st)
+
+
+def tc_eligible(k: PKernel) -> bool:
+    mm, a, b, tb, M, N, K, _ = _mm_dims(k)
+    if os.environ.get("TENSORJIT_B200_NO_TCGEN05") == "1":
+        return False
+    if a.dtype not in ("bf16", "f16") or b.dtype != a.dtype:
+        return False
+    if K < 8 or K % 8 != 0 or M == 0 or N == 0:
+        return False
+    if not tb and N % 8 != 0:
+        return False
+    return True
+
+
+# ---------------------------------------------------------------------------
+# epilogue generator (shared by both GEMM implementations)
+# ---------------------------------------------------------------------------
+class Epilogue:
+    """Emits the per-element epilogue of a matmul kernel: load epilogue inputs at
+    (batch, i, j), evaluate the DAG, store every escaping node."""
+
+    def __init__(self, k: PKernel, in_index: dict[int, int], out_index: dict[int, int]):
+        self.k = k
+        mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
+        self.mm, self.M, self.N, self.out_shape = mm, M, N, out_shape
+        self.batch_shape = out_shape[:-2]
+        self.epi_nodes = [n for n in k.nodes if n is not mm]
+        self.epi_inputs = [n for n in k.inputs if n is not a and n is not b]
+        self.in_index, self.out_index = in_index, out_index
+        self.strides = {}
+        for n in self.epi_inputs:
+            c = first_consumer(n, self.epi_nodes, self.epi_nodes[0] if self.epi_nodes else mm)
+            self.strides[n.id] = access_strides(n, c, out_shape)
+        self.dtype_out = {o.id: o.dtype for o in k.outputs}
+
+    def vec_ok(self) -> bool:
+        """8-column vector path: every epilogue operand unit-stride or broadcast along j,
+        every other stride and N a multiple of 8, no i32."""
+        if self.N % 8 != 0:
+            return False
+        for n in self.epi_inputs:
+            st = self.strides[n.id]
+            if st[-1] not in (0, 1) or any(s % 8 != 0 for s in st[:-1]) or n.dtype == "i32":
+                return False
+        return all(d in ("bf16", "f16", "f32") for d in self.dtype_out.values())
+
+    def batch_index_lines(self, bvar: str) -> tuple[list[str], list[str]]:
+        if not self.batch_shape:
+            return [], []
+        return decompose_stmts(bvar, self.batch_shape, "eb")
+
+    def offset(self, n: PNode, bidx: list[str], ivar: str, jvar: str) -> str:
+        return offset_expr(bidx + [ivar, jvar], self.strides[n.id])
+
+    def out_offset(self, bidx: list[str], ivar: str, jvar: str) -> str:
+        return offset_expr(bidx + [ivar, jvar], contiguous_strides(self.out_shape))
+
+    def compute_lines(self, acc: str, val: dict[int, str]) -> tuple[list[str], dict[int, str]]:
+        """f32 evaluation of the DAG given the accumulator and loaded operands."""
+        m = dict(val)
+        m[self.mm.id] = acc
+        lines = []
+        for n in self.epi_nodes:
+            lines.append(f"const float e{n.id} = {expr(n, m)};")
+            m[n.id] = f"e{n.id}"
+        return lines, m
+
+    def chunk32_function(self) -> str:
+        """``epilogue(prm, b, i, j0, acc[32])`` for the tcgen05 kernel (one row, 32 columns)."""
+        L = ["  template <class P>",
+             "  static __device__ __forceinline__ void epilogue(const P& prm, long b, long i, long j0, const float (&acc)[32]) {",
+             f"    if (i >= {self.M}L) return;"]
+        L += ["    " + s for s in self._ptr_lines()]
+        bl, bidx = self.batch_index_lines("b")
+        L += ["    " + s for s in bl]
+        if self.vec_ok():
+            L.append("    #pragma unroll")
+            L.append("    for (int c = 0; c < 32; c += 8) {")
+            L.append("      const long j = j0 + c;")
+            L.append(f"      if (j >= {self.N}L) break;")
+            val = {}
+            for n in self.epi_inputs:
+                st = self.strides[n.id]
+                idx = self.in_index[n.id]
+                off = self.offset(n, bidx, "i", "j")
+                if st[-1] == 1:
+                    L.append(f"      float x{n.id}[8]; tj_load_vec(in{idx} + ({off}), x{n.id});")
+                    val[n.id] = f"x{n.id}[u]"
+                else:
+                    L.append(f"      const float x{n.id} = tj_f32(in{idx}[{off}]);")
+                    val[n.id] = f"x{n.id}"
+            outs = self.k.outputs
+            for j, o in enumerate(outs):
+                L.append(f"      float o{j}[8];")
+            L.append("      #pragma unroll")
+            L.append("      for (int u = 0; u < 8; ++u) {")
+            comp, m = self.compute_lines("acc[c + u]", val)
+            L += ["        " + s for s in comp]
+            for j, o in enumerate(outs):
+                L.append(f"        o{j}[u] = {m[o.id]};")
+            L.append("      }")
+            off = self.out_offset(bidx, "i", "j")
+            for j, o in enumerate(outs):
+                oi = self.out_index[o.id]
+                if o.dtype == "f32":
+                    L.append(f"      tj_store_vec(out{oi} + ({off}), o{j}); tj_store_vec(out{oi} + ({off}) + 4, o{j} + 4);")
+                else:
+                    L.append(f"      tj_store_vec(out{oi} + ({off}), o{j});")
+            L.append("    }")
+        else:
+            L.append("    #pragma unroll 4")
+            L.append("    for (int c = 0; c < 32; ++c) {")
+            L.append("      const long j = j0 + c;")
+            L.append(f"      if (j >= {self.N}L) break;")
+            L += ["      " + s for s in self.scalar_element_lines(bidx, "i", "j", "acc[c]")]
+            L.append("    }")
+        L.append("  }")
+        return "\n".join(L)
+
+    def _ptr_lines(self) -> list[str]:
+        L = []
+        for n in self.epi_inputs:
+            idx = self.in_index[n.id]
+            L.append(f"const {CTYPE[n.dtype]}* __restrict__ in{idx} = (const {CTYPE[n.dtype]}*)prm.p[{idx}];")
+        for o in self.k.outputs:
+            oi = self.out_index[o.id]
+            L.append(f"{CTYPE[o.dtype]}* __restrict__ out{oi} = ({CTYPE[o.dtype]}*)prm.p[{oi}];")
+        return L
+
+    def scalar_element_lines(self, bidx: list[str], ivar: str, jvar: str, acc: str) -> list[str]:
+        L = []
+        val = {}
+        for n in self.epi_inputs:
+            idx = self.in_index[n.id]
+            L.append(f"const float x{n.id} = tj_f32(in{idx}[{self.offset(n, bidx, ivar, jvar)}]);")
+            val[n.id] = f"x{n.id}"
+        comp, m = self.compute_lines(acc, val)
+        L += comp
+        off = self.out_offset(bidx, ivar, jvar)
+        for o in self.k.outputs:
+            oi = self.out_index[o.id]
+            L.append(f"out{oi}[{off}] = tj_from<{CTYPE[o.dtype]}>({m[o.id]});")
+        return L
+
+
+# ---------------------------------------------------------------------------
+# tcgen05 kernel
+# ---------------------------------------------------------------------------
+def choose_tile(M: int, N: int, batch: int, b_mn_major: bool, override: dict | None = None) -> tuple[int, int, int]:
+    """(BN, STAGES, GROUP_M): largest N tile that still gives every SM work."""
+    if override:
+        return override["BN"], override["STAGES"], override.get("GROUP_M", 16)
+    m_tiles = (M + 127) // 128
+    cands = [256, 128, 64] if not b_mn_major else [256, 128, 64]
+    BN = 64
+    for bn in cands:
+        if N < bn and bn > 64 and N <= bn // 2:
+            continue
+        tiles = batch * m_tiles * ((N + bn - 1) // bn)
+        if tiles >= NUM_SMS or bn == 64:
+            BN = bn
+            break
+    if N <= 32 and not b_mn_major:
+        BN = 32
+    stage_bytes = 128 * 64 * 2 + BN * 64 * 2
+    STAGES = max(2, min(8, (200 * 1024) // stage_bytes))
+    return BN, STAGES, 16
+
+
+def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = None) -> KernelSource:
+    mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
+    batch_shape = out_shape[:-2]
+    batch = prod(batch_shape)
+    ins, outs = list(k.inputs), list(k.outputs)
+    in_index = {n.id: j for j, n in enumerate(ins)}
+    out_index = {o.id: len(ins) + j for j, o in enumerate(outs)}
+    nptr = len(ins) + len(outs) + 1          # + status word
+    status_idx = nptr - 1
+    epi = Epilogue(k, in_index, out_index)
+    b_mn = not tb
+    BN, STAGES, GROUP_M = choose_tile(M, N, batch, b_mn, tile)
+    a_bs = _batch_strides(a, batch_shape)
+    b_bs = _batch_strides(b, batch_shape)
+    a_mats = prod(a.shape[:-2])
+    b_mats = prod(b.shape[:-2])
+    bl, bidx = decompose_stmts("b", batch_shape, "bb") if batch_shape else ([], [])
+    L = [HEADER, '#include "gemm_sm100.cuh"', params_struct(nptr, 2)]
+    L.append("struct Cfg {")
+    L.append(f"  static constexpr int BN = {BN}, STAGES = {STAGES}, M = {M}, N = {N}, K = {K}, GROUP_M = {GROUP_M};")
+    L.append(f"  static constexpr long BATCH = {batch}L;")
+    L.append(f"  static constexpr bool BF16 = {'true' if a.dtype == 'bf16' else 'false'}, B_MN_MAJOR = {'true' if b_mn else 'false'};")
+    L.append("  static __device__ __forceinline__ void batch_map(long b, long& ab, long& bb_) {")
+    L += ["    " + s for s in bl]
+    L.append(f"    ab = {offset_expr(bidx, a_bs) if batch_shape else '0L'};")
+    L.append(f"    bb_ = {offset_expr(bidx, b_bs) if batch_shape else '0L'};")
+    L.append("  }")
+    L.append(epi.chunk32_function())
+    L.append("};")
+    smem = 1024 + STAGES * (128 * 64 * 2 + BN * 64 * 2) + (2 * STAGES + 6) * 8 + 16
+    L.append(f'extern "C" __global__ void __launch_bounds__(192, 1) {symbol}(const __grid_constant__ Params prm) {{')
+    L.append(f"  tjg::gemm_sm100<Cfg>(prm, (int*)prm.p[{status_idx}], {kernel_id});")
+    L.append("}")
+    m_tiles = (M + 127) // 128
+    n_tiles = (N + BN - 1) // BN
+    num_tiles = batch * m_tiles * n_tiles
+    grid = min(num_tiles, NUM_SMS)
+    esz = ITEM[a.dtype]
+    tmA = TMapSpec(arg=in_index[a.id], dtype=a.dtype, dims=[K, a_mats * M], strides=[K * esz], box=[64, 128],
+                   swizzle=3)
+    if tb:
+        tmB = TMapSpec(arg=in_index[b.id], dtype=b.dtype, dims=[K, b_mats * N], strides=[K * esz], box=[64, BN],
+                       swizzle=3)
+    else:
+        tmB = TMapSpec(arg=in_index[b.id], dtype=b.dtype, dims=[N, K, b_mats], strides=[N * esz, K * N * esz],
+                       box=[64, 64, 1], swizzle=3)
+    args = [("node", n) for n in ins] + [("node", o) for o in outs] + [("status", None)]
+    ks = KernelSource(symbol, "gemm_tc", "\n".join(L), (grid, 1, 1), (192, 1, 1), args, smem=smem,
+                      tmaps=[tmA, tmB],
+                      info={"M": M, "N": N, "K": K, "batch": batch, "BN": BN, "stages": STAGES,
+                            "flops": 2.0 * batch * M * N * K, "tiles": num_tiles,
+                            "bytes": sum(n.nbytes for n in ins) + sum(o.nbytes for o in outs)})
+    ks.finalize_params()
+    return ks
+
+
+# ---------------------------------------------------------------------------
+# SIMT fallback
+# ---------------------------------------------------------------------------
+def gen_gemm_simt(k: PKernel, symbol: str) -> KernelSource:
+    mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
+    batch_shape = out_shape[:-2]
+    batch = prod(batch_shape)
+    ins, outs = list(k.inputs), list(k.outputs)
+    in_index = {n.id: j for j, n in enumerate(ins)}
+    out_index = {o.id: len(ins) + j for j, o in enumerate(outs)}
+    epi = Epilogue(k, in_index, out_index)
+    a_bs = _batch_strides(a, batch_shape)
+    b_bs = _batch_strides(b, batch_shape)
+    ia, ib = in_index[a.id], in_index[b.id]
+    BM_, BN_, BK_ = 64, 64, 16
+    L = [HEADER, params_struct(len(ins) + len(outs), 0)]
+    L.append(f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{')
+    L.append(f"  const {CTYPE[a.dtype]}* __restrict__ A = (const {CTYPE[a.dtype]}*)prm.p[{ia}];")
+    L.append(f"  const {CTYPE[b.dtype]}* __restrict__ B = (const {CTYPE[b.dtype]}*)prm.p[{ib}];")
+    L += ["  " + s for s in epi._ptr_lines()]
+    L.append("  const long bz = blockIdx.z;")
+    bl, bidx = decompose_stmts("bz", batch_shape, "bb") if batch_shape else ([], [])
+    L += ["  " + s for s in bl]
+    L.append(f"  const long aoff = ({offset_expr(bidx, a_bs) if batch_shape else '0L'}) * {M * K}L;")
+    L.append(f"  const long boff = ({offset_expr(bidx, b_bs) if batch_shape else '0L'}) * {N * K}L;")
+    L.append(f"  __shared__ float As[{BK_}][{BM_} + 4];")
+    L.append(f"  __shared__ float Bs[{BK_}][{BN_} + 4];")
+    L.append(f"  const int tid = threadIdx.x, tr = tid / 16, tc = tid % 16;")
+    L.append(f"  const long i0 = (long)blockIdx.y * {BM_}, j0 = (long)blockIdx.x * {BN_};")
+    L.append("  float acc[4][4];")
+    L.append("  #pragma unroll")
+    L.append("  for (int x = 0; x < 4; ++x) for (int y = 0; y < 4; ++y) acc[x][y] = 0.0f;")
+    L.append(f"  for (long k0 = 0; k0 < {K}L; k0 += {BK_}) {{")
+    L.append(f"    for (int t = tid; t < {BM_ * BK_}; t += 256) {{")
+    L.append(f"      const int r = t / {BK_}, c = t % {BK_};")
+    L.append("      const long gi = i0 + r, gk = k0 + c;")
+    L.append(f"      As[c][r] = (gi < {M}L && gk < {K}L) ? tj_f32(A[aoff + gi * {K}L + gk]) : 0.0f;")
+    L.append("    }")
+    L.append(f"    for (int t = tid; t < {BK_ * BN_}; t += 256) {{")
+    if tb:
+        L.append(f"      const int c = t / {BN_}, r = t % {BN_};")
+        L.append("      const long gk = k0 + c, gj = j0 + r;")
+        L.append(f"      Bs[c][r] = (gk < {K}L && gj < {N}L) ? tj_f32(B[boff + gj * {K}L + gk]) : 0.0f;")
+    else:
+        L.append(f"      const int r = t / {BN_}, c = t % {BN_};")
+        L.append("      const long gk = k0 + r, gj = j0 + c;")
+        L.append(f"      Bs[r][c] = (gk < {K}L && gj < {N}L) ? tj_f32(B[boff + gk * {N}L + gj]) : 0.0f;")
+    L.append("    }")
+    L.append("    __syncthreads();")
+    L.append("    #pragma unroll")
+    L.append(f"    for (int kk = 0; kk < {BK_}; ++kk) {{")
+    L.append("      float av[4], bv[4];")
+    L.append("      #pragma unroll")
+    L.append("      for (int x = 0; x < 4; ++x) av[x] = As[kk][tr * 4 + x];")
+    L.append("      #pragma unroll")
+    L.append("      for (int y = 0; y < 4; ++y) bv[y] = Bs[kk][tc * 4 + y];")
+    L.append("      #pragma unroll")
+    L.append("      for (int x = 0; x < 4; ++x) for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(av[x], bv[y], acc[x][y]);")
+    L.append("    }")
+    L.append("    __syncthreads();")
+    L.append("  }")
+    L.append("  #pragma unroll")
+    L.append("  for (int x = 0; x < 4; ++x) {")
+    L.append("    #pragma unroll")
+    L.append("    for (int y = 0; y < 4; ++y) {")
+    L.append("      const long i = i0 + tr * 4 + x, j = j0 + tc * 4 + y;")
+    L.append(f"      if (i < {M}L && j < {N}L) {{")
+    L += ["        " + s for s in epi.scalar_element_lines(bidx, "i", "j", "acc[x][y]")]
+    L.append("      }")
+    L.append("    }")
+    L.append("  }")
+    L.append("}")
+    grid = ((N + BN_ - 1) // BN_, (M + BM_ - 1) // BM_, batch) if M and N and batch else (0, 1, 1)
+    ks = KernelSource(symbol, "gemm_simt", "\n".join(L), grid, (256, 1, 1), [("node", n) for n in ins + outs],
+                      info={"M": M, "N": N, "K": K, "batch": batch, "flops": 2.0 * batch * M * N * K,
+                            "bytes": sum(n.nbytes for n in ins) + sum(o.nbytes for o in outs)})
+    ks.finalize_params()
+    return ks

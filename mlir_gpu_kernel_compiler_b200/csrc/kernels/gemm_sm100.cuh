@@ -1,0 +1,370 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a with a fused pointwise epilogue.
+//
+//   C[b, i, j] = sum_k A[b, i, k] * B[b, k, j]   (B stored [N,K] K-major, or [K,N] N-major)
+//   then the plan's epilogue DAG on the f32 accumulator, stored in the output dtype.
+//
+// Plan semantics: tensorjit/backends/cuda_backend.py:299-429 (matmul + _epilogue_lines).
+//
+// Roles (192 threads, one CTA per SM, tiles handed out round-robin):
+//   warp 0      TMA producer: A tile [128 x 64] and B tile [BN x 64] per stage into
+//               128B-swizzled shared memory, completion tracked by mbarrier tx bytes.
+//   warp 1      TMEM allocator + MMA issuer: one elected lane issues
+//               tcgen05.mma.cta_group::1.kind::f16 (128 x BN x 16) four times per stage
+//               into a TMEM accumulator; tcgen05.commit frees the smem stage, and
+//               a final commit per tile signals the epilogue.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (lane = output row),
+//               generated epilogue functor (bias / GELU / residual ...), 16-byte stores.
+// The accumulator is double-buffered in TMEM (2 x BN columns), so the epilogue of
+// tile t overlaps the main loop of tile t+1.
+//
+// Every wait is bounded: after TJ_WAIT_NS of no progress the waiting thread raises
+// a CTA-wide abort flag and writes the device status word; all roles then drain
+// their in-flight copies / MMAs (again bounded), TMEM is freed, and the kernel
+// returns.  No trap, no unbounded spin.
+//
+// No TMA multicast is used anywhere (loads are plain per-CTA tiled copies).
+#pragma once
+#include <cuda.h>
+
+#include "tj_common.cuh"
+
+#ifndef TJ_WAIT_NS
+#define TJ_WAIT_NS 4000000000ull  // 4 s without progress = failure
+#endif
+
+namespace tjg {
+
+TJ_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+TJ_DEV void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+TJ_DEV void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+TJ_DEV void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+TJ_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on phase `parity` of `bar`.  Returns false on abort / timeout.
+TJ_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status, int where,
+                      uint64_t budget_ns = TJ_WAIT_NS) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = tj_globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (tj_globaltimer() - t0 > budget_ns) {
+        *abort_flag = 1;
+        tj_report(status, TJ_STATUS_WAIT_TIMEOUT, where);
+        return false;
+      }
+    }
+  }
+}
+
+TJ_DEV void tma_prefetch(const CUtensorMap* m) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+TJ_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+TJ_DEV void tma_load_3d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// UMMA shared-memory matrix descriptor, 128-byte swizzle (sm100 descriptor version 1).
+TJ_DEV uint64_t desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with f32 accumulation.
+constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((a_mn_major ? 1u : 0u) << 15) |
+         ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+TJ_DEV void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+TJ_DEV void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+TJ_DEV void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols) : "memory");
+}
+TJ_DEV void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
+TJ_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+TJ_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+TJ_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 lanes x 32 consecutive f32 columns: thread `lane` receives its row's 32 values.
+TJ_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+  // the wait names every destination register so no use can be scheduled before it
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+                 "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]),
+                 "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Grouped raster over (m, n) tiles inside one batch: GROUP_M m-tiles share the
+// same B columns while the whole group sweeps N, so concurrently running CTAs
+// reuse A and B tiles through L2.
+TJ_DEV void tile_coords(long t, int m_tiles, int n_tiles, int group_m, long& b, int& mt, int& nt) {
+  const long per_batch = static_cast<long>(m_tiles) * n_tiles;
+  b = t / per_batch;
+  const long r = t - b * per_batch;
+  const long per_group = static_cast<long>(group_m) * n_tiles;
+  const int g = static_cast<int>(r / per_group);
+  const int first_m = g * group_m;
+  const int gsize = min(m_tiles - first_m, group_m);
+  const int in_g = static_cast<int>(r - static_cast<long>(g) * per_group);
+  mt = first_m + in_g % gsize;
+  nt = in_g / gsize;
+}
+
+// Cfg provides:
+//   static constexpr int BN, STAGES, M, N, K, GROUP_M; static constexpr long BATCH;
+//   static constexpr bool BF16, B_MN_MAJOR;
+//   static __device__ void batch_map(long b, long& a_batch, long& b_batch);
+//   template <class P> static __device__ void epilogue(const P& prm, long b, long i, long j0, const float (&acc)[32]);
+template <class Cfg, class P>
+__device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel_id) {
+  constexpr int BM = 128, BK = 64;
+  constexpr int BN = Cfg::BN, STAGES = Cfg::STAGES;
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr int m_tiles = (Cfg::M + BM - 1) / BM;
+  constexpr int n_tiles = (Cfg::N + BN - 1) / BN;
+  constexpr int k_blocks = (Cfg::K + BK - 1) / BK;
+  constexpr long num_tiles = Cfg::BATCH * m_tiles * n_tiles;
+  constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+  constexpr uint32_t IDESC = idesc_f16(Cfg::BF16, BM, BN, false, Cfg::B_MN_MAJOR);
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  static_assert(!Cfg::B_MN_MAJOR || BN % 64 == 0, "N-major B needs BN multiple of 64");
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B-swizzle atoms
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + 2;
+  uint64_t* drain = bars + 2 * STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const CUtensorMap* tmA = &prm.tm[0];
+  const CUtensorMap* tmB = &prm.tm[1];
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&tfull[b]), 1);
+      mbar_init(smem_u32(&tempty[b]), 128);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch(tmA);
+    tma_prefetch(tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_phase[STAGES];
+      bool pending[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) pending[s] = false;
+      bool ok = true;
+      for (long t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        long b;
+        int mt, nt;
+        tile_coords(t, m_tiles, n_tiles, Cfg::GROUP_M, b, mt, nt);
+        long ab, bb;
+        Cfg::batch_map(b, ab, bb);
+        const int a_row = static_cast<int>(ab * Cfg::M + static_cast<long>(mt) * BM);
+        const int n0 = nt * BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, status, kernel_id * 16 + 1)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[stage]);
+          mbar_expect_tx(fb, STAGE_BYTES);
+          tma_load_2d(smem_u32(sA + stage * A_BYTES), tmA, fb, kb * BK, a_row);
+          if constexpr (!Cfg::B_MN_MAJOR) {
+            tma_load_2d(smem_u32(sB + stage * B_BYTES), tmB, fb, kb * BK, static_cast<int>(bb * Cfg::N + n0));
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_3d(smem_u32(sB + stage * B_BYTES + c * (BK * 128)), tmB, fb, n0 + 64 * c, kb * BK,
+                          static_cast<int>(bb));
+          }
+          pending[stage] = true;
+          issued_phase[stage] = phase;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // abort: let every copy this thread issued land before shared memory is released
+        for (int s = 0; s < STAGES; ++s)
+          if (pending[s]) {
+            volatile int no_abort = 0;
+            mbar_wait(smem_u32(&full[s]), issued_phase[s], &no_abort, status, kernel_id * 16 + 5, 200000000ull);
+          }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (long t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+        const int buf = it & 1;
+        if (!mbar_wait(smem_u32(&tempty[buf]), ((it >> 1) & 1) ^ 1u, abort_flag, status, kernel_id * 16 + 2)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, status, kernel_id * 16 + 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = desc_sw128(a0 + kk * 32, 16, 1024);
+            uint64_t bd;
+            if constexpr (!Cfg::B_MN_MAJOR)
+              bd = desc_sw128(b0 + kk * 32, 16, 1024);
+            else
+              bd = desc_sw128(b0 + kk * 16 * 128, BK * 128, 1024);
+            umma_f16(d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(smem_u32(&empty[stage]));
+          issued_any = true;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit(smem_u32(&tfull[buf]));
+      }
+      if (!ok && issued_any) {
+        // abort: wait for the MMAs already issued before TMEM / smem go away
+        umma_commit(smem_u32(drain));
+        volatile int no_abort = 0;
+        mbar_wait(smem_u32(drain), 0, &no_abort, status, kernel_id * 16 + 6, 200000000ull);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2..5 ----------------
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    int it = 0;
+    for (long t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+      long b;
+      int mt, nt;
+      tile_coords(t, m_tiles, n_tiles, Cfg::GROUP_M, b, mt, nt);
+      const int buf = it & 1;
+      const bool ok = mbar_wait(smem_u32(&tfull[buf]), (it >> 1) & 1, abort_flag, status, kernel_id * 16 + 4);
+      if (!__all_sync(0xffffffffu, ok)) break;  // the warp leaves together: tcgen05.ld is warp-collective
+      tc_fence_after();
+      const long i = static_cast<long>(mt) * BM + q * 32 + lane;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float acc[32];
+        tmem_ld32(tbase + c * 32, acc);
+        Cfg::epilogue(prm, b, i, static_cast<long>(nt) * BN + c * 32, acc);
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&tempty[buf]));
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+template <int BN, int STAGES>
+constexpr int gemm_smem_bytes() {
+  return 1024 + STAGES * (128 * 64 * 2 + BN * 64 * 2) + (2 * STAGES + 6) * 8 + 16;
+}
+
+}  // namespace tjg

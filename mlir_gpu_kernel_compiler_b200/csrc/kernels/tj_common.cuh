@@ -1,0 +1,124 @@
+// Shared device helpers for the generated sm_100a kernels of the tensorjit B200 backend.
+//
+// Arithmetic follows the reference's CUDA expression table
+// (tensorjit/backends/common.py:65-88): every value is f32 inside a kernel,
+// loads convert to f32 and stores round f32 -> storage type to nearest even
+// (tensorjit/backends/cuda_backend.py:46-54).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#define TJ_DEV __device__ __forceinline__
+
+// ---------------------------------------------------------------------------
+// scalar conversions
+// ---------------------------------------------------------------------------
+TJ_DEV float tj_f32(float x) { return x; }
+TJ_DEV float tj_f32(int x) { return (float)x; }
+TJ_DEV float tj_f32(__half x) { return __half2float(x); }
+TJ_DEV float tj_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <typename T> TJ_DEV T tj_from(float x);
+template <> TJ_DEV float tj_from<float>(float x) { return x; }
+template <> TJ_DEV int tj_from<int>(float x) { return (int)x; }
+template <> TJ_DEV __half tj_from<__half>(float x) { return __float2half_rn(x); }
+template <> TJ_DEV __nv_bfloat16 tj_from<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+// ---------------------------------------------------------------------------
+// 16-byte vector loads/stores: VEC = 16 / sizeof(T) elements
+// ---------------------------------------------------------------------------
+template <typename T> struct TjVec { static constexpr int N = 16 / sizeof(T); };
+
+TJ_DEV uint4 tj_ld16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+// streaming load for data read exactly once
+TJ_DEV uint4 tj_ld16_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+TJ_DEV void tj_st16(void* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
+
+TJ_DEV void tj_unpack(uint4 v, float* f, const float*) {
+  f[0] = __uint_as_float(v.x); f[1] = __uint_as_float(v.y);
+  f[2] = __uint_as_float(v.z); f[3] = __uint_as_float(v.w);
+}
+TJ_DEV void tj_unpack(uint4 v, float* f, const __nv_bfloat16*) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+TJ_DEV void tj_unpack(uint4 v, float* f, const __half*) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+    float2 t = __half22float2(h);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+TJ_DEV uint4 tj_pack(const float* f, const float*) {
+  return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+}
+TJ_DEV uint32_t tj_pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+TJ_DEV uint4 tj_pack(const float* f, const __nv_bfloat16*) {
+  return make_uint4(tj_pack_bf16x2(f[0], f[1]), tj_pack_bf16x2(f[2], f[3]), tj_pack_bf16x2(f[4], f[5]),
+                    tj_pack_bf16x2(f[6], f[7]));
+}
+TJ_DEV uint32_t tj_pack_f16x2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+TJ_DEV uint4 tj_pack(const float* f, const __half*) {
+  return make_uint4(tj_pack_f16x2(f[0], f[1]), tj_pack_f16x2(f[2], f[3]), tj_pack_f16x2(f[4], f[5]),
+                    tj_pack_f16x2(f[6], f[7]));
+}
+template <typename T> TJ_DEV void tj_load_vec(const T* p, float* f) { tj_unpack(tj_ld16(p), f, (const T*)nullptr); }
+template <typename T> TJ_DEV void tj_load_vec_stream(const T* p, float* f) {
+  tj_unpack(tj_ld16_stream(p), f, (const T*)nullptr);
+}
+template <typename T> TJ_DEV void tj_store_vec(T* p, const float* f) { tj_st16(p, tj_pack(f, (const T*)nullptr)); }
+
+// ---------------------------------------------------------------------------
+// op semantics (tensorjit/backends/common.py:65-88, CUDA variant)
+// ---------------------------------------------------------------------------
+TJ_DEV float tj_gelu(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+TJ_DEV float tj_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+TJ_DEV float tj_silu(float x) { return x / (1.0f + expf(-x)); }
+TJ_DEV float tj_rsqrt(float x) { return 1.0f / sqrtf(x); }
+TJ_DEV float tj_relu(float x) { return fmaxf(x, 0.0f); }
+TJ_DEV float tj_where(float c, float a, float b) { return c != 0.0f ? a : b; }
+
+// ---------------------------------------------------------------------------
+// reductions
+// ---------------------------------------------------------------------------
+template <int W> TJ_DEV float tj_group_sum(float v) {
+#pragma unroll
+  for (int o = W / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+template <int W> TJ_DEV float tj_group_max(float v) {
+#pragma unroll
+  for (int o = W / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// device status word: the first failing kernel records (code, where)
+// ---------------------------------------------------------------------------
+enum : int { TJ_STATUS_WAIT_TIMEOUT = 1, TJ_STATUS_BOUNDS = 2 };
+TJ_DEV void tj_report(int* status, int code, int where) {
+  if (status && atomicCAS(status, 0, code) == 0) status[1] = where;
+}
+TJ_DEV uint64_t tj_globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}

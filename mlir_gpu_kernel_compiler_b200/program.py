@@ -1,0 +1,246 @@
+"""``B200Program``: the object ``compile_program`` returns — the drop-in for the
+reference's ``CudaProgram`` (``tensorjit/backends/cuda_backend.py:459-553``).
+
+Surface kept from the reference: callable ``(*inputs) -> list[Tensor]`` (a list
+even for one output), ``num_kernels``, ``source``, ``program``, ``plan`` (the
+arena ``MemoryPlan``), ``backend``, ``device``, ``stats`` (``calls``,
+``graph_replays``).  Inputs are borrowed (made contiguous); outputs are fresh
+caller-owned tensors reshaped to the graph's output shapes; a graph output that
+is a constant is materialised with ``torch.full`` (``cuda_backend.py:541-553``).
+
+What differs, by design:
+
+* kernels are sm_100a cubins built by nvcc from the hand-written templates in
+  ``csrc/kernels`` and executed by the C++ runtime through the C ABI;
+* graph mode binds the caller's buffers directly into the captured graph
+  (kernel nodes are re-pointed only when a buffer changes) instead of copying
+  every input into static buffers and cloning every output
+  (``cuda_backend.py:522-535``);
+* arity is checked (``TypeError``), and so are shape, dtype and device
+  (``ValueError``).
+"""
+from __future__ import annotations
+
+import os
+import sys
+from typing import Optional
+
+import torch
+
+from . import runtime as rt
+from .codegen import generate
+from .memory import MemoryPlan, plan_memory
+from .plan import PNode, PProgram, as_plan
+from .toolchain import compile_cubins
+
+TORCH_DTYPE = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16, "i32": torch.int32}
+FROM_TORCH = {v: k for k, v in TORCH_DTYPE.items()}
+
+
+class OutputPool:
+    """Caller-visible output buffers.  A buffer handed out earlier is reused only
+    when nothing outside the pool references it any more (neither the tensor
+    object nor a view of its storage), the policy of ``executor.py:64-79``."""
+
+    MAX_HELD = 8
+
+    def __init__(self):
+        self._held: dict[tuple, list[torch.Tensor]] = {}
+
+    @staticmethod
+    def _free(t: torch.Tensor) -> bool:
+        # refs: the pool's list + getrefcount's argument (+ the loop variable in the caller)
+        if sys.getrefcount(t) > 3:
+            return False
+        if t._use_count() != 1:
+            return False
+        return torch._C._storage_Use_Count(t.untyped_storage()._cdata) <= 2
+
+    def take(self, shape, dtype, device) -> torch.Tensor:
+        key = (tuple(shape), dtype, str(device))
+        held = self._held.setdefault(key, [])
+        for i in range(len(held)):
+            t = held[i]
+            if self._free(t):
+                del t
+                held.append(held.pop(i))
+                return held[-1]
+        t = torch.empty(shape, dtype=dtype, device=device)
+        held.append(t)
+        if len(held) > self.MAX_HELD:
+            held.pop(0)
+        return t
+
+
+class B200Program:
+    backend = "b200"
+
+    def __init__(self, program, device: str | torch.device = "cuda", use_graph: Optional[bool] = None,
+                 tune: bool = True, tiles: dict | None = None):
+        self.program = program
+        self.pplan: PProgram = as_plan(program)
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError(f"the b200 backend runs on CUDA devices, not {self.device}")
+        self.plan: MemoryPlan = plan_memory(self.pplan)
+        if tune and tiles is None:
+            from .autotune import tiles_for_plan
+
+            tiles = tiles_for_plan(self.pplan)
+        self.kernel_sources = generate(self.pplan, tiles=tiles)
+        self.source = "\n\n".join(ks.source for ks in self.kernel_sources)
+        self.cubins = compile_cubins([(ks.symbol, ks.source) for ks in self.kernel_sources])
+        self.use_graph = (os.environ.get("TENSORJIT_B200_GRAPH", "1") == "1") if use_graph is None else use_graph
+        g = self.pplan
+        self._in_index = {n.id: i for i, n in enumerate(g.inputs)}
+        escaping = {g.resolve(o).id for o in g.outputs}
+        self._out_nodes: list[PNode] = []
+        for k in g.kernels:
+            for o in k.outputs:
+                if o.id in escaping and o not in self._out_nodes:
+                    self._out_nodes.append(o)
+        self._out_index = {o.id: j for j, o in enumerate(self._out_nodes)}
+        self._launches, self._args, self._tmaps = self._tables()
+        self._native: Optional[rt.NativeProgram] = None
+        self.pool = OutputPool()
+        self._calls = 0
+
+    # -- launch tables for the C ABI ------------------------------------------
+    def _ref(self, n: PNode) -> tuple[int, int]:
+        src = self.pplan.resolve(n)
+        if src.id in self._in_index:
+            return rt.ARG_INPUT, self._in_index[src.id]
+        if src.id in self._out_index:
+            return rt.ARG_OUTPUT, self._out_index[src.id]
+        off = self.plan.offset(src)
+        if off is None:
+            raise RuntimeError(f"{n.name} has no storage (not an input, output or planned intermediate)")
+        return rt.ARG_ARENA, off
+
+    def _tables(self):
+        launches, args, tmaps = [], [], []
+        for m, ks in enumerate(self.kernel_sources):
+            first_arg = len(args)
+            for kind, node in ks.args:
+                args.append((rt.ARG_STATUS, 0) if kind == "status" else self._ref(node))
+            first_tmap = len(tmaps)
+            for t in ks.tmaps:
+                from .codegen.common import TMAP_DTYPE
+
+                tmaps.append({"arg": t.arg, "dtype": TMAP_DTYPE[t.dtype], "rank": len(t.dims), "swizzle": t.swizzle,
+                              "dims": t.dims, "strides": t.strides, "box": t.box, "param_offset": t.param_offset,
+                              "l2_promotion": t.l2_promotion})
+            launches.append({"symbol": ks.symbol, "module": m, "grid": ks.grid, "block": ks.block,
+                             "cluster": ks.cluster, "smem": ks.smem, "param_bytes": ks.param_bytes,
+                             "first_arg": first_arg, "num_args": len(ks.args), "first_tmap": first_tmap,
+                             "num_tmaps": len(ks.tmaps)})
+        return launches, args, tmaps
+
+    @property
+    def launches(self) -> list[dict]:
+        return self._launches
+
+    @property
+    def num_kernels(self) -> int:
+        return len(self.kernel_sources)
+
+    @property
+    def native(self) -> rt.NativeProgram:
+        if self._native is None:
+            if not torch.cuda.is_available():
+                raise RuntimeError("the b200 backend needs a CUDA device (none is visible)")
+            torch.cuda.init()
+            idx = self.device.index if self.device.index is not None else torch.cuda.current_device()
+            self._native = rt.NativeProgram(self.cubins, self._launches, self._args, self._tmaps,
+                                            self.plan.arena_bytes, len(self.pplan.inputs), len(self._out_nodes),
+                                            idx)
+            self._native.set_graph(self.use_graph)
+        return self._native
+
+    @property
+    def stats(self) -> dict:
+        if self._native is None:
+            return {"calls": 0, "graph_replays": 0}
+        inf = self._native.info()
+        return {"calls": inf["calls"], "graph_replays": inf["graph_replays"], "launches": inf["launches"],
+                "graph_node_updates": inf["graph_node_updates"], "host_us_total": inf["host_us_total"]}
+
+    # -- execution ------------------------------------------------------------
+    def _prepare_inputs(self, inputs) -> list[torch.Tensor]:
+        g = self.pplan
+        if len(inputs) != len(g.inputs):
+            raise TypeError(f"expected {len(g.inputs)} inputs, got {len(inputs)}")
+        ins = []
+        dev = self.device
+        for node, t in zip(g.inputs, inputs):
+            if not isinstance(t, torch.Tensor):
+                raise TypeError(f"{node.name}: expected a torch.Tensor, got {type(t).__name__}")
+            if tuple(t.shape) != tuple(node.shape):
+                raise ValueError(f"{node.name}: expected shape {tuple(node.shape)}, got {tuple(t.shape)}")
+            if t.dtype != TORCH_DTYPE[node.dtype]:
+                raise ValueError(f"{node.name}: expected dtype {TORCH_DTYPE[node.dtype]}, got {t.dtype}")
+            if t.device.type != "cuda" or (dev.index is not None and t.device.index != dev.index):
+                raise ValueError(f"{node.name}: tensor is on {t.device}, program is on {dev}")
+            t = t.contiguous()
+            if t.numel() and t.data_ptr() % 16:
+                t = t.clone()            # 16-byte vector and TMA paths need aligned bases
+            ins.append(t)
+        return ins
+
+    def run_into(self, ins: list[torch.Tensor], outs: list[torch.Tensor], stream: Optional[int] = None) -> None:
+        """Launch the whole program with caller-provided output buffers (no allocation)."""
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+        self.native.run([t.data_ptr() for t in ins], [t.data_ptr() for t in outs], stream)
+
+    def time_kernels(self, ins: list[torch.Tensor], outs: list[torch.Tensor], iters: int = 10,
+                     stream: Optional[int] = None) -> list[float]:
+        """Mean device milliseconds of every kernel over ``iters`` direct (non-graph) runs."""
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+        return self.native.time_kernels([t.data_ptr() for t in ins], [t.data_ptr() for t in outs], stream, iters,
+                                        self.num_kernels)
+
+    def __call__(self, *inputs: torch.Tensor) -> list[torch.Tensor]:
+        ins = self._prepare_inputs(inputs)
+        outs = [self.pool.take(o.shape, TORCH_DTYPE[o.dtype], self.device) for o in self._out_nodes]
+        self.run_into(ins, outs)
+        self._calls += 1
+        return self._assemble(ins, outs)
+
+    def _assemble(self, ins, outs) -> list[torch.Tensor]:
+        g = self.pplan
+        env = {o.id: t for o, t in zip(self._out_nodes, outs)}
+        env.update({n.id: t for n, t in zip(g.inputs, ins)})
+        result = []
+        for o in g.outputs:
+            src = g.resolve(o)
+            if src.id in env:
+                t = env[src.id]
+            elif src.op == "const":
+                t = torch.full(src.shape, float(src.attrs["value"]), dtype=TORCH_DTYPE[src.dtype], device=self.device)
+            else:
+                raise RuntimeError(f"output {o.name} was not produced")
+            result.append(t.reshape(o.shape) if tuple(t.shape) != tuple(o.shape) else t)
+        return result
+
+    def output_specs(self) -> list[tuple[tuple, torch.dtype]]:
+        return [(tuple(o.shape), TORCH_DTYPE[o.dtype]) for o in self._out_nodes]
+
+    def check(self) -> None:
+        """Synchronise and raise if any kernel of this program reported a failure."""
+        code, where = self.native.check_status()
+        if code:
+            raise rt.RuntimeError_(rt.TJ_ERR_DEVICE_STATUS,
+                                   f"kernel status {code} (kernel {where // 16}, site {where % 16})")
+
+    def close(self) -> None:
+        if self._native is not None:
+            self._native.close()
+            self._native = None
+
+
+def compile_program(program, device: str = "cuda", tune: bool = True) -> B200Program:
+    """Backend plugin entry point, same signature as
+    ``tensorjit/backends/cuda_backend.py:556-557``."""
+    return B200Program(program, device=device, tune=tune)
