@@ -48,21 +48,22 @@ class OutputPool:
         self._held: dict[tuple, list[torch.Tensor]] = {}
 
     @staticmethod
-    def _free(t: torch.Tensor) -> bool:
-        # refs: the pool's list + getrefcount's argument (+ the loop variable in the caller)
-        if sys.getrefcount(t) > 3:
+    def _free(held: list, i: int) -> bool:
+        # Python references: the pool's list + getrefcount's own argument.  The
+        # tensor impl must be owned by that one Python object only, and its
+        # storage by that impl (+ the temporary storage handle made here): a live
+        # view of the buffer holds the storage and keeps it busy.
+        if sys.getrefcount(held[i]) != 2:
             return False
-        if t._use_count() != 1:
+        if held[i]._use_count() != 1:
             return False
-        return torch._C._storage_Use_Count(t.untyped_storage()._cdata) <= 2
+        return torch._C._storage_Use_Count(held[i].untyped_storage()._cdata) <= 2
 
     def take(self, shape, dtype, device) -> torch.Tensor:
         key = (tuple(shape), dtype, str(device))
         held = self._held.setdefault(key, [])
         for i in range(len(held)):
-            t = held[i]
-            if self._free(t):
-                del t
+            if self._free(held, i):
                 held.append(held.pop(i))
                 return held[-1]
         t = torch.empty(shape, dtype=dtype, device=device)

@@ -91,14 +91,21 @@ def _matmul(a: np.ndarray, b: np.ndarray, trans_b: bool) -> np.ndarray:
     return np.matmul(a, b, dtype=F32)
 
 
-def evaluate(plan, inputs, outputs_only: bool = True, strict_shapes: bool = True):
+def evaluate(plan, inputs, outputs_only: bool = True, strict_shapes: bool = True, round_stored: bool = False):
     """Evaluate ``plan`` (a ``PProgram``) on ``inputs`` (arrays in graph-input order).
 
     Returns the graph outputs as f32 numpy arrays (or, with ``outputs_only=False``,
     the dict node id -> value of everything computed).  ``strict_shapes=False``
     lets a row-independent plan run on a leading-dimension slice of its row
     inputs (used for the large configs, whose rows are independent).
+
+    ``round_stored=True`` additionally rounds every value a kernel writes to
+    memory (each kernel output) to its plan dtype (bf16/f16, round to nearest
+    even), while values inside a kernel stay f32 — the storage behaviour of a
+    GPU backend that keeps the plan's dtypes in HBM.  With it off (the default)
+    the oracle is the reference ``c`` backend: f32 everywhere.
     """
+    stored = {o.id: o.dtype for k in plan.kernels for o in k.outputs} if round_stored else {}
     if len(inputs) != len(plan.inputs):
         raise TypeError(f"expected {len(plan.inputs)} inputs, got {len(inputs)}")
     env: dict[int, np.ndarray] = {}
@@ -144,10 +151,19 @@ def evaluate(plan, inputs, outputs_only: bool = True, strict_shapes: bool = True
         r = np.asarray(r, dtype=F32)
         if strict_shapes and tuple(r.shape) != tuple(n.shape):
             r = np.broadcast_to(r, n.shape).astype(F32)
+        if stored.get(n.id) in ("bf16", "f16"):
+            r = _round_to(r, stored[n.id])
         env[n.id] = r
 
-    outs = [val(plan.resolve(o)).reshape(o.shape) if strict_shapes else val(o) for o in plan.outputs]
+    outs = [val(plan.resolve(o)).reshape(o.shape) if strict_shapes else val(plan.resolve(o)) for o in plan.outputs]
     return outs if outputs_only else env
+
+
+def _round_to(x: np.ndarray, dtype: str) -> np.ndarray:
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(x))
+    return t.to(torch.bfloat16 if dtype == "bf16" else torch.float16).float().numpy()
 
 
 def _to_f32(x) -> np.ndarray:

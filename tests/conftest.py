@@ -7,6 +7,11 @@ import pytest
 ROOT = Path(__file__).resolve().parents[1]
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
+# the reference package, when it was installed next to the repo (pip --target baseline/_ref);
+# only the tensorjit-integration tests import it, and they skip without it
+_REF = ROOT / "baseline" / "_ref"
+if _REF.exists() and str(_REF) not in sys.path:
+    sys.path.append(str(_REF))
 
 
 def pytest_configure(config):

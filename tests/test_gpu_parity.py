@@ -31,14 +31,27 @@ def _run(case, use_graph=None):
 @pytest.mark.parametrize("case", FX.cases("case"))
 def test_case_matches_reference(case):
     plan, ins, prog, outs = _run(case)
-    tol = FX.TOL[plan.meta["dtype"]]
+    dt = plan.meta["dtype"]
+    tol = FX.TOL[dt]
     exp = FX.case_expected(case)
     assert len(outs) == len(exp)
-    ref = evaluate(plan, [t.cpu() for t in ins])
-    for y, e, r in zip(outs, exp, ref):
-        FX.check_against_golden(y, e, tol)
-        err = normwise_error(y, r)
-        assert err <= tol, f"vs oracle: {err:.3e} > {tol}"
+    cpu_ins = [t.cpu() for t in ins]
+    ref = evaluate(plan, cpu_ins)
+    if dt == "f32":
+        for y, e, r in zip(outs, exp, ref):
+            FX.check_against_golden(y, e, tol)
+            assert normwise_error(y, r) <= tol
+        return
+    # half precision: the plan keeps every stored intermediate in bf16/f16.  The GPU
+    # result must match the oracle that rounds stored values the same way, and the
+    # f32 reference within the stated tolerance -- or, where bf16 storage alone
+    # already moves the result further (tiny N(0,1)-weight cases), within 1.5x that.
+    emul = evaluate(plan, cpu_ins, round_stored=True)
+    for y, e, r, m in zip(outs, exp, ref, emul):
+        assert normwise_error(y, m) <= tol, "vs bf16-storage oracle"
+        allowed = max(tol, 1.5 * normwise_error(m, r))
+        FX.check_against_golden(y, e, allowed)
+        assert normwise_error(y, r) <= allowed
 
 
 @pytest.mark.parametrize("use_graph", [False, True])

@@ -25,8 +25,8 @@ def test_oracle_matches_reference_c_backend(case):
         FX.check_against_golden(torch.from_numpy(np.ascontiguousarray(y)), e, 1e-5)
 
 
-@pytest.mark.parametrize("cfg", ["cfg1", "cfg2"])
-def test_oracle_matches_reference_on_small_configs(cfg):
+@pytest.mark.parametrize("cfg", ["cfg1", "cfg2", "cfg3", "cfg4"])
+def test_oracle_matches_reference_on_configs(cfg):
     w = W.WORKLOADS[cfg]
     plan = FX.load_plan(w.plan)
     outs = evaluate(plan, W.make_inputs(w))

@@ -1,0 +1,56 @@
+"""The b200 backend behind tensorjit's own API (``tj.jit`` / ``compile_graph``).
+
+These tests need the reference package importable (installed under
+``baseline/_ref``); they skip without it.  ``register()`` performs the four
+edits the reference's dispatch needs (``tensorjit/compiler.py:21,24-31,34,61-68``).
+"""
+import pytest
+import torch
+
+tj = pytest.importorskip("tensorjit")
+
+import mlir_gpu_kernel_compiler_b200 as tjb  # noqa: E402
+from oracle import fixtures as FX  # noqa: E402
+from oracle.plan_oracle import evaluate, normwise_error  # noqa: E402
+
+
+def _mlp(x, g, w1, b1, w2, b2):
+    return x + tj.linear(tj.gelu(tj.linear(tj.layer_norm(x, g), w1, b1)), w2, b2)
+
+
+def test_register_adds_backend_and_keeps_the_plan():
+    import tensorjit.compiler as C
+    from tensorjit.ir import DType, TensorType
+
+    tjb.register()
+    assert "b200" in C.BACKENDS and C.ROW_FUSION_MAX_N["b200"] == 8192
+    assert C.pick_backend("cuda") == "b200" and C.pick_backend("cpu") == "c"
+    shapes = [(64, 128), (128,), (256, 128), (256,), (128, 256), (128,)]
+    g = tj.trace(_mlp, [TensorType(s, DType.bf16) for s in shapes])
+    live = tjb.from_tensorjit(C.lower(g, "b200"))
+    fixture = FX.load_plan("cuda_mlp__bf16")
+    assert [k.kind for k in live.kernels] == [k.kind for k in fixture.kernels]
+    assert [[n.op for n in k.nodes] for k in live.kernels] == [[n.op for n in k.nodes] for k in fixture.kernels]
+    assert live.to_dict()["kernels"] == fixture.to_dict()["kernels"]
+
+
+@pytest.mark.gpu
+def test_jit_on_cuda_tensors_runs_b200():
+    tjb.register()
+    torch.manual_seed(0)
+    dev = "cuda"
+    x, g = torch.randn(64, 128, device=dev), torch.ones(128, device=dev)
+    w1, b1 = torch.randn(256, 128, device=dev), torch.randn(256, device=dev)
+    w2, b2 = torch.randn(128, 256, device=dev), torch.randn(128, device=dev)
+    f = tj.jit(_mlp)                              # no backend: cuda tensors pick "b200"
+    out = f(x, g, w1, b1, w2, b2)
+    cp = f.compiled(x, g, w1, b1, w2, b2)
+    assert isinstance(cp, tjb.B200Program) and cp.num_kernels == 3
+    import torch.nn.functional as F
+
+    ref = x + F.linear(F.gelu(F.linear(F.layer_norm(x, (128,), g), w1, b1)), w2, b2)
+    assert normwise_error(out, ref) <= 1e-4
+    out2 = f(x + 1, g, w1, b1, w2, b2)
+    ref2 = (x + 1) + F.linear(F.gelu(F.linear(F.layer_norm(x + 1, (128,), g), w1, b1)), w2, b2)
+    assert normwise_error(out2, ref2) <= 1e-4
+    assert f.stats.compiles == 1 and f.stats.hits >= 2
