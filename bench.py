@@ -236,7 +236,8 @@ def run_b200(a) -> None:
     # end to end through the public call: host rows in, result out, every step
     e2e = None
     if not a.no_e2e:
-        stream_idx = list(w.row_args) if sharded else list(range(len(ins)))
+        # activations stream in every step; weights/gains/biases stay resident
+        stream_idx = list(w.row_args) or list(range(len(ins)))
         host = {i: ins[i].cpu().pin_memory() for i in stream_idx}
         res_shape, res_dtype = prog.output_specs()[0]
         y_host = torch.empty(res_shape, dtype=res_dtype).pin_memory()

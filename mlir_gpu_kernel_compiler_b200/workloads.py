@@ -21,7 +21,6 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass, field
-from typing import Callable
 
 import torch
 
@@ -65,7 +64,7 @@ WORKLOADS: dict[str, Workload] = {
         "cfg2", "cfg2", torch.bfloat16, 1,
         [Arg("x", (16384, 4096), "randn"), Arg("r", (16384, 4096), "randn"), Arg("g", (4096,), "ones"),
          Arg("s", (8192, 8192), "randn")],
-        hbm_bytes=2.0 * (3 * 16384 * 4096 + 2 * 8192 * 8192),
+        hbm_bytes=2.0 * (3 * 16384 * 4096 + 2 * 8192 * 8192), row_args=(0, 1, 3),
         description="rms_norm(x + r, g) and softmax(s), bf16"),
     "cfg3": Workload(
         "cfg3", "cfg3", torch.bfloat16, 2,
@@ -80,6 +79,7 @@ WORKLOADS: dict[str, Workload] = {
          Arg("bo", (D4,), "randn", 0.02), Arg("g2", (D4,), "ones"), Arg("w1", (4 * D4, D4), "randn", 0.02),
          Arg("b1", (4 * D4,), "randn", 0.02), Arg("w2", (D4, 4 * D4), "randn", 0.02), Arg("b2", (D4,), "randn", 0.02)],
         flops=4 * 2.0 * 16384 * D4 * D4 + 2 * 2.0 * 128 * 2048 * 2048 * 64 + 2 * 2.0 * 16384 * D4 * 4 * D4,
+        row_args=(0,),
         description="pre-norm transformer block, B8xT2048, d1024, 16 heads x 64, bf16"),
     "cfg5": Workload(
         "cfg5", "cfg5_m131072", torch.bfloat16, 4,
@@ -132,5 +132,3 @@ def shard_rows(total: int, world: int, rank: int) -> tuple[int, int]:
 def numel(shape) -> int:
     return math.prod(shape) if shape else 1
 
-
-Builder = Callable[..., object]
