@@ -97,6 +97,11 @@ class Clocks:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
+def _trace(*a):
+    if os.environ.get("TJ_BENCH_TRACE") == "1":
+        print("[bench]", *a, file=sys.stderr, flush=True)
+
+
 def _dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -163,6 +168,7 @@ def run_b200(a) -> None:
     from mlir_gpu_kernel_compiler_b200.plan import PProgram
 
     world, rank, local = _dist()
+    _trace("start", world, rank)
     if world > 1:
         from datetime import timedelta
 
@@ -175,9 +181,12 @@ def run_b200(a) -> None:
     plan_name = W.sharded_plan_name(w, world) if sharded else w.plan
     plan = PProgram.load(ROOT / "tests" / "golden" / "plans" / f"{plan_name}.json")
     rows = W.shard_rows(w.rows, world, rank) if sharded else None
+    _trace("inputs")
     ins = W.make_inputs(w, device=dev, rows=rows)
+    _trace("compile")
     prog = B200Program(plan, device=dev, use_graph=True)
     outs = [torch.empty(s, dtype=d, device=dev) for s, d in prog.output_specs()]
+    _trace("run")
     stream = torch.cuda.current_stream(dev)
 
     def barrier():

@@ -67,9 +67,10 @@ def cost_model(cfg: TileConfig, M: int, N: int, K: int, batch: int) -> float:
     t = waves * tile_work / eff
     # fill: padded tile area / useful area
     t *= (m_tiles * 128 * n_tiles * cfg.BN) / max(M * N, 1)
-    # shallow pipelines stall on HBM latency
+    # shallow pipelines stall on HBM latency; every extra stage hides a little more
     if cfg.STAGES < 3:
         t *= 1.25
+    t *= 1.0 + 0.01 * (8 - min(cfg.STAGES, 8))
     # L2 raster: prefer groups covering ~16 m-tiles for wide problems
     t *= 1.0 + 0.02 * abs(math.log2(cfg.GROUP_M / 16))
     return t

@@ -130,7 +130,11 @@ class Epilogue:
                 idx = self.in_index[n.id]
                 off = self.offset(n, bidx, "i", "j")
                 if st[-1] == 1:
-                    L.append(f"      float x{n.id}[8]; tj_load_vec(in{idx} + ({off}), x{n.id});")
+                    if n.dtype == "f32":   # 8 f32 = two 16-byte loads
+                        L.append(f"      float x{n.id}[8]; tj_load_vec(in{idx} + ({off}), x{n.id}); "
+                                 f"tj_load_vec(in{idx} + ({off}) + 4, x{n.id} + 4);")
+                    else:
+                        L.append(f"      float x{n.id}[8]; tj_load_vec(in{idx} + ({off}), x{n.id});")
                     val[n.id] = f"x{n.id}[u]"
                 else:
                     L.append(f"      const float x{n.id} = tj_f32(in{idx}[{off}]);")
@@ -232,7 +236,10 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     bl, bidx = decompose_stmts("b", batch_shape, "bb") if batch_shape else ([], [])
     L = [HEADER, '#include "gemm_sm100.cuh"', params_struct(nptr, 2)]
     L.append("struct Cfg {")
+    epi_warps = 8 if BN % 64 == 0 else 4
+    threads = 64 + 32 * epi_warps
     L.append(f"  static constexpr int BN = {BN}, STAGES = {STAGES}, M = {M}, N = {N}, K = {K}, GROUP_M = {GROUP_M};")
+    L.append(f"  static constexpr int EPI_WARPS = {epi_warps};")
     L.append(f"  static constexpr long BATCH = {batch}L;")
     L.append(f"  static constexpr bool BF16 = {'true' if a.dtype == 'bf16' else 'false'}, B_MN_MAJOR = {'true' if b_mn else 'false'};")
     L.append("  static __device__ __forceinline__ void batch_map(long b, long& ab, long& bb_) {")
@@ -243,7 +250,7 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     L.append(epi.chunk32_function())
     L.append("};")
     smem = 1024 + STAGES * (128 * 64 * 2 + BN * 64 * 2) + (2 * STAGES + 6) * 8 + 16
-    L.append(f'extern "C" __global__ void __launch_bounds__(192, 1) {symbol}(const __grid_constant__ Params prm) {{')
+    L.append(f'extern "C" __global__ void __launch_bounds__({threads}, 1) {symbol}(const __grid_constant__ Params prm) {{')
     L.append(f"  tjg::gemm_sm100<Cfg>(prm, (int*)prm.p[{status_idx}], {kernel_id});")
     L.append("}")
     m_tiles = (M + 127) // 128
@@ -260,7 +267,7 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
         tmB = TMapSpec(arg=in_index[b.id], dtype=b.dtype, dims=[N, K, b_mats], strides=[N * esz, K * N * esz],
                        box=[64, 64, 1], swizzle=3)
     args = [("node", n) for n in ins] + [("node", o) for o in outs] + [("status", None)]
-    ks = KernelSource(symbol, "gemm_tc", "\n".join(L), (grid, 1, 1), (192, 1, 1), args, smem=smem,
+    ks = KernelSource(symbol, "gemm_tc", "\n".join(L), (grid, 1, 1), (threads, 1, 1), args, smem=smem,
                       tmaps=[tmA, tmB],
                       info={"M": M, "N": N, "K": K, "batch": batch, "BN": BN, "stages": STAGES,
                             "flops": 2.0 * batch * M * N * K, "tiles": num_tiles,

@@ -12,8 +12,10 @@
 //               tcgen05.mma.cta_group::1.kind::f16 (128 x BN x 16) four times per stage
 //               into a TMEM accumulator; tcgen05.commit frees the smem stage, and
 //               a final commit per tile signals the epilogue.
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (lane = output row),
-//               generated epilogue functor (bias / GELU / residual ...), 16-byte stores.
+//   warps 2..   epilogue (EPI_WARPS = 4 or 8): tcgen05.ld 32 columns at a time
+//               (lane = output row; with 8 warps, two warps share a TMEM lane quadrant
+//               and split the tile's columns), generated epilogue functor (bias /
+//               GELU / residual ...), 16-byte stores.
 // The accumulator is double-buffered in TMEM (2 x BN columns), so the epilogue of
 // tile t overlaps the main loop of tile t+1.
 //
@@ -168,7 +170,7 @@ TJ_DEV void tile_coords(long t, int m_tiles, int n_tiles, int group_m, long& b, 
 }
 
 // Cfg provides:
-//   static constexpr int BN, STAGES, M, N, K, GROUP_M; static constexpr long BATCH;
+//   static constexpr int BN, STAGES, M, N, K, GROUP_M, EPI_WARPS; static constexpr long BATCH;
 //   static constexpr bool BF16, B_MN_MAJOR;
 //   static __device__ void batch_map(long b, long& a_batch, long& b_batch);
 //   template <class P> static __device__ void epilogue(const P& prm, long b, long i, long j0, const float (&acc)[32]);
@@ -187,6 +189,9 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
   constexpr uint32_t IDESC = idesc_f16(Cfg::BF16, BM, BN, false, Cfg::B_MN_MAJOR);
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
   static_assert(!Cfg::B_MN_MAJOR || BN % 64 == 0, "N-major B needs BN multiple of 64");
+  constexpr int EPI_WARPS = Cfg::EPI_WARPS;
+  static_assert(EPI_WARPS == 4 || (EPI_WARPS == 8 && BN % 64 == 0), "epilogue warps");
+  constexpr int EPI_COLS = BN / (EPI_WARPS / 4);  // columns of the tile one epilogue warp covers
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzle atoms
@@ -213,7 +218,7 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&tfull[b]), 1);
-      mbar_init(smem_u32(&tempty[b]), 128);
+      mbar_init(smem_u32(&tempty[b]), 32 * Cfg::EPI_WARPS);
     }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
@@ -332,8 +337,9 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
       }
     }
   } else {
-    // ---------------- epilogue warps 2..5 ----------------
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    // ---------------- epilogue warps ----------------
+    const int q = warp & 3;                      // TMEM lane quadrant this warp may access
+    const int col0 = ((warp - 2) / 4) * EPI_COLS;  // first tile column this warp covers
     int it = 0;
     for (long t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
       long b;
@@ -344,12 +350,13 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
       if (!__all_sync(0xffffffffu, ok)) break;  // the warp leaves together: tcgen05.ld is warp-collective
       tc_fence_after();
       const long i = static_cast<long>(mt) * BM + q * 32 + lane;
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN + col0);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < EPI_COLS / 32; ++c) {
         float acc[32];
         tmem_ld32(tbase + c * 32, acc);
-        Cfg::epilogue(prm, b, i, static_cast<long>(nt) * BN + c * 32, acc);
+        Cfg::epilogue(prm, b, i, static_cast<long>(nt) * BN + col0 + c * 32, acc);
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&tempty[buf]));

@@ -22,6 +22,7 @@
 #include <chrono>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -413,7 +414,8 @@ int tj_b200_program_create(const void* const* cubins, const size_t* cubin_sizes,
     if (k.launch.smem_bytes > 48 * 1024)
       TJ_CU(d.cuFuncSetAttribute(k.fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, k.launch.smem_bytes),
             "cuFuncSetAttribute(max dynamic smem)");
-    if (d.cuFuncGetParamInfo) {
+    const char* pc = std::getenv("TENSORJIT_B200_PARAM_CHECK");
+    if (d.cuFuncGetParamInfo && !(pc && pc[0] == '0')) {
       size_t off = 0, sz = 0;
       if (d.cuFuncGetParamInfo(k.fn, 0, &off, &sz) == CUDA_SUCCESS && sz != k.launch.param_bytes)
         return fail(TJ_ERR_INVALID, "kernel %s: parameter block is %zu bytes in the cubin, %u in the launch table",

@@ -73,6 +73,11 @@ class OutputPool:
         return t
 
 
+def _trace(*a):
+    if os.environ.get("TJ_TRACE") == "1":
+        print("[b200]", *a, file=sys.stderr, flush=True)
+
+
 class B200Program:
     backend = "b200"
 
@@ -84,13 +89,17 @@ class B200Program:
         if self.device.type != "cuda":
             raise ValueError(f"the b200 backend runs on CUDA devices, not {self.device}")
         self.plan: MemoryPlan = plan_memory(self.pplan)
+        _trace("planned")
         if tune and tiles is None:
             from .autotune import tiles_for_plan
 
             tiles = tiles_for_plan(self.pplan)
+        _trace("tiles", tiles)
         self.kernel_sources = generate(self.pplan, tiles=tiles)
+        _trace("generated")
         self.source = "\n\n".join(ks.source for ks in self.kernel_sources)
         self.cubins = compile_cubins([(ks.symbol, ks.source) for ks in self.kernel_sources])
+        _trace("compiled")
         self.use_graph = (os.environ.get("TENSORJIT_B200_GRAPH", "1") == "1") if use_graph is None else use_graph
         g = self.pplan
         self._in_index = {n.id: i for i, n in enumerate(g.inputs)}
@@ -152,6 +161,10 @@ class B200Program:
                 raise RuntimeError("the b200 backend needs a CUDA device (none is visible)")
             torch.cuda.init()
             idx = self.device.index if self.device.index is not None else torch.cuda.current_device()
+            # Let the CUDA runtime launch the process's first kernel (a one-element fill):
+            # Nsight Compute's injection crashed when the first launch it saw was a
+            # driver-API cuLaunchKernelEx from this library.
+            torch.zeros(1, device=torch.device("cuda", idx))
             self._native = rt.NativeProgram(self.cubins, self._launches, self._args, self._tmaps,
                                             self.plan.arena_bytes, len(self.pplan.inputs), len(self._out_nodes),
                                             idx)

@@ -55,8 +55,25 @@ def nvcc() -> str:
 
 @lru_cache(maxsize=None)
 def nvcc_version() -> str:
-    r = subprocess.run([nvcc(), "--version"], capture_output=True, text=True)
-    return r.stdout.strip().splitlines()[-1] if r.returncode == 0 else "unknown"
+    """nvcc's version line for the cache key.  It is remembered in the cache
+    directory per nvcc binary (size, mtime), so a cache hit spawns no process:
+    a process under a profiler should not start tool subprocesses."""
+    exe = Path(nvcc())
+    st = exe.stat()
+    stamp = cache_dir() / f"nvcc_version.{st.st_size}.{int(st.st_mtime)}.txt"
+    try:
+        v = stamp.read_text().strip()
+        if v:
+            return v
+    except OSError:
+        pass
+    r = subprocess.run([str(exe), "--version"], capture_output=True, text=True)
+    v = r.stdout.strip().splitlines()[-1] if r.returncode == 0 else "unknown"
+    try:
+        stamp.write_text(v + "\n")
+    except OSError:
+        pass
+    return v
 
 
 def cache_dir() -> Path:
@@ -100,6 +117,10 @@ def compile_cubin(source: str, name: str = "kernel", extra_flags: tuple = ()) ->
     key = source_key(source, extra_flags)
     d = cache_dir()
     out = d / f"{key}.cubin"
+    if os.environ.get("TJ_TRACE") == "1":
+        import sys
+
+        print(f"[b200] cubin {name} {key} cached={out.exists()}", file=sys.stderr, flush=True)
     if out.exists():
         try:
             data = out.read_bytes()
