@@ -45,6 +45,21 @@ EXPR = {
 }
 
 
+# Half-precision programs round every stored value to bf16/f16 (relative step
+# 2^-8 / 2^-11), so their kernels use the hardware approximations where those are
+# orders of magnitude tighter than that rounding: __expf (ex2.approx based, rel.
+# error ~1e-6 for the arguments seen here) and __fdividef (rcp.approx * a).  f32
+# programs keep the IEEE-accurate library functions.
+EXPR_FAST = dict(EXPR, exp="__expf({0})", sigmoid="tj_sigmoid_fast({0})", silu="tj_silu_fast({0})",
+                 div="__fdividef({0}, {1})")
+
+
+def fast_math_for(dtypes) -> bool:
+    """Approximate exp/div only when every value the kernel stores is half precision."""
+    ds = set(dtypes)
+    return bool(ds) and ds <= {"bf16", "f16"}
+
+
 def literal(v: float) -> str:
     """f32 literal for a scalar constant (``common.py:113-119``)."""
     v = float(v)
@@ -61,7 +76,7 @@ def is_scalar_const(n: PNode) -> bool:
     return n.op == "const" and n.shape == ()
 
 
-def expr(node: PNode, operand: dict[int, str]) -> str:
+def expr(node: PNode, operand: dict[int, str], fast: bool = False) -> str:
     """Expression of one elementwise node given operand names (scalar consts inline)."""
     args = []
     for i in node.inputs:
@@ -73,7 +88,7 @@ def expr(node: PNode, operand: dict[int, str]) -> str:
             args.append(operand[i.id])
     if node.op in ("transpose", "broadcast_to"):
         return args[0]
-    return EXPR[node.op].format(*args)
+    return (EXPR_FAST if fast else EXPR)[node.op].format(*args)
 
 
 @dataclass

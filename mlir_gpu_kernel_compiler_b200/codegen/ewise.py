@@ -14,8 +14,8 @@ the scalar path with compile-time index decomposition.
 from __future__ import annotations
 
 from ..plan import PKernel, access_strides, contiguous_strides, first_consumer
-from .common import (CTYPE, HEADER, NUM_SMS, KernelSource, coalesce, decompose_stmts, expr, offset_expr,
-                     params_struct, pick_vec, prod)
+from .common import (CTYPE, HEADER, NUM_SMS, KernelSource, coalesce, decompose_stmts, expr, fast_math_for,
+                     offset_expr, params_struct, pick_vec, prod)
 
 THREADS = 256
 UNROLL = 2
@@ -47,6 +47,7 @@ def gen_elementwise(k: PKernel, symbol: str) -> KernelSource:
     for j, o in enumerate(outs):
         L.append(f"  {CTYPE[o.dtype]}* __restrict__ out{j} = ({CTYPE[o.dtype]}*)prm.p[{len(ins) + j}];")
     names = {n.id: f"x{j}" for j, n in enumerate(ins)}
+    fast = fast_math_for([o.dtype for o in outs])
     nvec = numel // VEC
     need_idx = any(st != out_cs for st, out_cs in zip(cin, [cstr[-1]] * len(cin)))
 
@@ -73,7 +74,7 @@ def gen_elementwise(k: PKernel, symbol: str) -> KernelSource:
             comp.append(f"  const float x{j} = {src};")
         local = dict(names)
         for n in k.nodes:
-            comp.append(f"  const float v{n.id} = {expr(n, local)};")
+            comp.append(f"  const float v{n.id} = {expr(n, local, fast)};")
             local[n.id] = f"v{n.id}"
         for j, o in enumerate(outs):
             comp.append(f"  o{tag}[{j}][u] = {local[o.id]};")

@@ -21,7 +21,7 @@ import os
 
 from ..plan import PKernel, PNode, access_strides, contiguous_strides, first_consumer
 from .common import (CTYPE, HEADER, ITEM, NUM_SMS, TMAP_DTYPE, KernelSource, TMapSpec, decompose_stmts, expr,
-                     offset_expr, params_struct, prod)
+                     fast_math_for, offset_expr, params_struct, prod)
 
 
 def _mm_dims(k: PKernel):
@@ -78,6 +78,7 @@ class Epilogue:
             c = first_consumer(n, self.epi_nodes, self.epi_nodes[0] if self.epi_nodes else mm)
             self.strides[n.id] = access_strides(n, c, out_shape)
         self.dtype_out = {o.id: o.dtype for o in k.outputs}
+        self.fast = fast_math_for(self.dtype_out.values())
 
     def vec_ok(self) -> bool:
         """8-column vector path: every epilogue operand unit-stride or broadcast along j,
@@ -107,7 +108,7 @@ class Epilogue:
         m[self.mm.id] = acc
         lines = []
         for n in self.epi_nodes:
-            lines.append(f"const float e{n.id} = {expr(n, m)};")
+            lines.append(f"const float e{n.id} = {expr(n, m, self.fast)};")
             m[n.id] = f"e{n.id}"
         return lines, m
 

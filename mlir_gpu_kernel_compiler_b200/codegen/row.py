@@ -19,7 +19,7 @@ one CTA's registers, so no cluster is needed.
 from __future__ import annotations
 
 from ..plan import PKernel, PNode, broadcast_strides
-from .common import CTYPE, HEADER, KernelSource, expr, literal, offset_expr, params_struct, pick_vec, prod
+from .common import CTYPE, HEADER, KernelSource, expr, fast_math_for, literal, offset_expr, params_struct, pick_vec, prod
 
 CTA_THREADS = 256
 
@@ -71,6 +71,7 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str)
           and all(st[-1] in (0, 1) and all(s % VEC == 0 for s in st[:-1]) for st in vec_strides.values()))
     if not ok:
         VEC = 1
+    fast = fast_math_for([o.dtype for o in outs])
     TPR, VPT, RPC = _geometry(N, VEC)
     NVEC = (N + VEC - 1) // VEC if N else 0
     if N == 0:
@@ -198,7 +199,7 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str)
         out.append(f"  for (int u = 0; u < {VEC}; ++u) {{")
         m = operand_map(nodes + ([reduce_node] if reduce_node else []), True)
         for n in nodes:
-            out.append(f"    const float v{n.id} = {expr(n, m)};")
+            out.append(f"    const float v{n.id} = {expr(n, m, fast)};")
             m[n.id] = f"v{n.id}"
             if n.id in temps:
                 out.append(f"    T{n.id}[jv][u] = v{n.id};")
@@ -237,7 +238,7 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str)
                     m[i.id] = f"T{i.id}[0][0]" if i.id in temps else f"v{i.id}"
                 elif i.id in in_idx:
                     m[i.id] = scalar_load(i, iter_shape)
-            out.append(f"s{n.id} = {expr(n, m)};")
+            out.append(f"s{n.id} = {expr(n, m, fast)};")
             computed_scalar.add(n.id)
             local[n.id] = f"s{n.id}"
             if n.id in escaping:

@@ -95,6 +95,8 @@ TJ_DEV float tj_silu(float x) { return x / (1.0f + expf(-x)); }
 TJ_DEV float tj_rsqrt(float x) { return 1.0f / sqrtf(x); }
 TJ_DEV float tj_relu(float x) { return fmaxf(x, 0.0f); }
 TJ_DEV float tj_where(float c, float a, float b) { return c != 0.0f ? a : b; }
+TJ_DEV float tj_sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+TJ_DEV float tj_silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // ---------------------------------------------------------------------------
 // reductions
