@@ -168,6 +168,57 @@ class Epilogue:
         L.append("  }")
         return "\n".join(L)
 
+    def tma_store_ok(self) -> bool:
+        """One half-precision output written by 32 x 32 TMA stores: needs a 16-byte row
+        pitch (N % 8 == 0) and the vectorised operand path."""
+        outs = self.k.outputs
+        return (len(outs) == 1 and outs[0].dtype in ("bf16", "f16") and self.N % 8 == 0 and self.vec_ok()
+                and os.environ.get("TENSORJIT_B200_NO_TMA_STORE") != "1")
+
+    def vals32_function(self) -> str:
+        """``epilogue_vals(prm, b, i, j0, acc[32], out[32])``: the output values of one row's 32
+        columns (rows >= M and columns >= N are left at 0; the TMA store clips them)."""
+        o = self.k.outputs[0]
+        L = ["  template <class P>",
+             "  static __device__ __forceinline__ void epilogue_vals(const P& prm, long b, long i, long j0, "
+             "const float (&acc)[32], float (&out)[32]) {",
+             "    #pragma unroll",
+             "    for (int c = 0; c < 32; ++c) out[c] = 0.0f;",
+             f"    if (i >= {self.M}L) return;"]
+        for n in self.epi_inputs:
+            idx = self.in_index[n.id]
+            L.append(f"    const {CTYPE[n.dtype]}* __restrict__ in{idx} = (const {CTYPE[n.dtype]}*)prm.p[{idx}];")
+        bl, bidx = self.batch_index_lines("b")
+        L += ["    " + s for s in bl]
+        L.append("    #pragma unroll")
+        L.append("    for (int c = 0; c < 32; c += 8) {")
+        L.append("      const long j = j0 + c;")
+        L.append(f"      if (j >= {self.N}L) break;")
+        val = {}
+        for n in self.epi_inputs:
+            st = self.strides[n.id]
+            idx = self.in_index[n.id]
+            off = self.offset(n, bidx, "i", "j")
+            if st[-1] == 1:
+                if n.dtype == "f32":
+                    L.append(f"      float x{n.id}[8]; tj_load_vec(in{idx} + ({off}), x{n.id}); "
+                             f"tj_load_vec(in{idx} + ({off}) + 4, x{n.id} + 4);")
+                else:
+                    L.append(f"      float x{n.id}[8]; tj_load_vec(in{idx} + ({off}), x{n.id});")
+                val[n.id] = f"x{n.id}[u]"
+            else:
+                L.append(f"      const float x{n.id} = tj_f32(in{idx}[{off}]);")
+                val[n.id] = f"x{n.id}"
+        L.append("      #pragma unroll")
+        L.append("      for (int u = 0; u < 8; ++u) {")
+        comp, m = self.compute_lines("acc[c + u]", val)
+        L += ["        " + s for s in comp]
+        L.append(f"        out[c + u] = {m[o.id]};")
+        L.append("      }")
+        L.append("    }")
+        L.append("  }")
+        return "\n".join(L)
+
     def _ptr_lines(self) -> list[str]:
         L = []
         for n in self.epi_inputs:
@@ -235,12 +286,16 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     a_mats = prod(a.shape[:-2])
     b_mats = prod(b.shape[:-2])
     bl, bidx = decompose_stmts("b", batch_shape, "bb") if batch_shape else ([], [])
-    L = [HEADER, '#include "gemm_sm100.cuh"', params_struct(nptr, 2)]
+    L = [HEADER, '#include "gemm_sm100.cuh"', params_struct(nptr, 3 if epi.tma_store_ok() else 2)]
     L.append("struct Cfg {")
     epi_warps = 8 if BN % 64 == 0 else 4
     threads = 64 + 32 * epi_warps
+    tma_store = epi.tma_store_ok()
+    out_stage = epi_warps * 2 * 32 * 32 * 2 if tma_store else 0
     L.append(f"  static constexpr int BN = {BN}, STAGES = {STAGES}, M = {M}, N = {N}, K = {K}, GROUP_M = {GROUP_M};")
     L.append(f"  static constexpr int EPI_WARPS = {epi_warps};")
+    L.append(f"  static constexpr bool TMA_STORE = {'true' if tma_store else 'false'};")
+    L.append(f"  using OutT = {CTYPE[outs[0].dtype] if tma_store else 'float'};")
     L.append(f"  static constexpr long BATCH = {batch}L;")
     L.append(f"  static constexpr bool BF16 = {'true' if a.dtype == 'bf16' else 'false'}, B_MN_MAJOR = {'true' if b_mn else 'false'};")
     L.append("  static __device__ __forceinline__ void batch_map(long b, long& ab, long& bb_) {")
@@ -248,9 +303,9 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     L.append(f"    ab = {offset_expr(bidx, a_bs) if batch_shape else '0L'};")
     L.append(f"    bb_ = {offset_expr(bidx, b_bs) if batch_shape else '0L'};")
     L.append("  }")
-    L.append(epi.chunk32_function())
+    L.append(epi.vals32_function() if tma_store else epi.chunk32_function())
     L.append("};")
-    smem = 1024 + STAGES * (128 * 64 * 2 + BN * 64 * 2) + (2 * STAGES + 6) * 8 + 16
+    smem = 1024 + STAGES * (128 * 64 * 2 + BN * 64 * 2) + out_stage + (2 * STAGES + 6) * 8 + 16
     L.append(f'extern "C" __global__ void __launch_bounds__({threads}, 1) {symbol}(const __grid_constant__ Params prm) {{')
     L.append(f"  tjg::gemm_sm100<Cfg>(prm, (int*)prm.p[{status_idx}], {kernel_id});")
     L.append("}")
@@ -267,10 +322,17 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     else:
         tmB = TMapSpec(arg=in_index[b.id], dtype=b.dtype, dims=[N, K, b_mats], strides=[N * esz, K * N * esz],
                        box=[64, 64, 1], swizzle=3)
+    tmaps = [tmA, tmB]
+    if tma_store:
+        o = outs[0]
+        oe = ITEM[o.dtype]
+        tmaps.append(TMapSpec(arg=out_index[o.id], dtype=o.dtype, dims=[N, M, batch], strides=[N * oe, M * N * oe],
+                              box=[32, 32, 1], swizzle=2))
     args = [("node", n) for n in ins] + [("node", o) for o in outs] + [("status", None)]
     ks = KernelSource(symbol, "gemm_tc", "\n".join(L), (grid, 1, 1), (threads, 1, 1), args, smem=smem,
-                      tmaps=[tmA, tmB],
+                      tmaps=tmaps,
                       info={"M": M, "N": N, "K": K, "batch": batch, "BN": BN, "stages": STAGES,
+                            "tma_store": tma_store, "epi_warps": epi_warps,
                             "flops": 2.0 * batch * M * N * K, "tiles": num_tiles,
                             "bytes": sum(n.nbytes for n in ins) + sum(o.nbytes for o in outs)})
     ks.finalize_params()

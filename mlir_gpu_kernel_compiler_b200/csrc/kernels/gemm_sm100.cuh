@@ -92,6 +92,19 @@ TJ_DEV void tma_load_3d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0
       : "memory");
 }
 
+// TMA store of a [box] tile from shared memory (bulk-group completion; out-of-range
+// coordinates of the box are clipped by the hardware, so ragged edges are never written).
+TJ_DEV void tma_store_3d(const CUtensorMap* m, uint32_t src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+TJ_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+TJ_DEV void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+TJ_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+TJ_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // UMMA shared-memory matrix descriptor, 128-byte swizzle (sm100 descriptor version 1).
 TJ_DEV uint64_t desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
   uint64_t d = 0;
@@ -171,9 +184,13 @@ TJ_DEV void tile_coords(long t, int m_tiles, int n_tiles, int group_m, long& b, 
 
 // Cfg provides:
 //   static constexpr int BN, STAGES, M, N, K, GROUP_M, EPI_WARPS; static constexpr long BATCH;
-//   static constexpr bool BF16, B_MN_MAJOR;
+//   static constexpr bool BF16, B_MN_MAJOR, TMA_STORE;  using OutT = <output element type>;
 //   static __device__ void batch_map(long b, long& a_batch, long& b_batch);
 //   template <class P> static __device__ void epilogue(const P& prm, long b, long i, long j0, const float (&acc)[32]);
+//     (direct 16-byte stores), or with TMA_STORE:
+//   template <class P> static __device__ void epilogue_vals(const P& prm, long b, long i, long j0,
+//                                                           const float (&acc)[32], float (&out)[32]);
+//     (values only; the kernel stages them in shared memory and stores 32 x 32 tiles with TMA)
 template <class Cfg, class P>
 __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel_id) {
   constexpr int BM = 128, BK = 64;
@@ -198,7 +215,10 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  // TMA-store staging: per epilogue warp two 32 x 32 output tiles (64-byte rows, 64B swizzle)
+  uint8_t* sOut = sB + STAGES * B_BYTES;
+  constexpr uint32_t OUT_STAGE = Cfg::TMA_STORE ? 32 * 32 * 2 : 0;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + EPI_WARPS * 2 * OUT_STAGE);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
@@ -225,6 +245,7 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch(tmA);
     tma_prefetch(tmB);
+    if constexpr (Cfg::TMA_STORE) tma_prefetch(&prm.tm[2]);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
@@ -340,6 +361,8 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
     // ---------------- epilogue warps ----------------
     const int q = warp & 3;                      // TMEM lane quadrant this warp may access
     const int col0 = ((warp - 2) / 4) * EPI_COLS;  // first tile column this warp covers
+    uint8_t* stage_out = sOut + (warp - 2) * 2 * OUT_STAGE;
+    int sbuf = 0;
     int it = 0;
     for (long t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
       long b;
@@ -356,10 +379,37 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
       for (int c = 0; c < EPI_COLS / 32; ++c) {
         float acc[32];
         tmem_ld32(tbase + c * 32, acc);
-        Cfg::epilogue(prm, b, i, static_cast<long>(nt) * BN + col0 + c * 32, acc);
+        const long j0 = static_cast<long>(nt) * BN + col0 + c * 32;
+        if constexpr (!Cfg::TMA_STORE) {
+          Cfg::epilogue(prm, b, i, j0, acc);
+        } else {
+          float vals[32];
+          Cfg::epilogue_vals(prm, b, i, j0, acc, vals);
+          if (lane == 0) bulk_wait_read1();  // the store issued two chunks ago has left this buffer
+          __syncwarp();
+          uint8_t* dst = stage_out + sbuf * OUT_STAGE + lane * 64;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const uint4 v = tj_pack(vals + 8 * cc, static_cast<const typename Cfg::OutT*>(nullptr));
+            // 64B swizzle: 16-byte chunk index ^= (row >> 1) & 3  (bank-conflict free, matches the tensor map)
+            *reinterpret_cast<uint4*>(dst + ((cc ^ ((lane >> 1) & 3)) << 4)) = v;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&prm.tm[2], smem_u32(stage_out + sbuf * OUT_STAGE), static_cast<int>(j0),
+                         mt * BM + q * 32, static_cast<int>(b));
+            bulk_commit();
+          }
+          sbuf ^= 1;
+        }
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&tempty[buf]));
+    }
+    if constexpr (Cfg::TMA_STORE) {
+      if (lane == 0) bulk_wait_all();  // every store complete before shared memory is released
+      __syncwarp();
     }
   }
   __syncwarp();
@@ -369,9 +419,5 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
   if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
-template <int BN, int STAGES>
-constexpr int gemm_smem_bytes() {
-  return 1024 + STAGES * (128 * 64 * 2 + BN * 64 * 2) + (2 * STAGES + 6) * 8 + 16;
-}
 
 }  // namespace tjg

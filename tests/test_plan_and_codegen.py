@@ -50,7 +50,7 @@ def test_launch_geometry_and_kernel_families():
     ks16 = generate(p16)
     assert [k.family for k in ks16] == ["row", "gemm_tc", "gemm_tc"]
     for k in ks16[1:]:
-        assert k.block[0] in (192, 320) and len(k.tmaps) == 2 and k.grid[0] <= 148
+        assert k.block[0] in (192, 320) and len(k.tmaps) in (2, 3) and k.grid[0] <= 148
 
 
 def test_tensor_core_path_only_for_half_precision_with_aligned_pitch():
