@@ -9,9 +9,13 @@ Here the same three steps run over the sm_100a space:
   shared-memory stages that fit in ~200 KB, and the L2 raster group GROUP_M;
 * cost model: tensor time at the tile's MMA shape efficiency + wave
   quantisation over 148 SMs + the epilogue's HBM traffic;
-* timing: ``autotune_gemm`` compiles the top-k candidates and times them with
+* timing: ``autotune_plan`` compiles the top-k candidates and times them with
   CUDA events on the device (GPU only); winners are stored in
   ``<cache>/autotune_b200.json`` keyed by (M, N, K, batch, dtype, B layout).
+  Winners measured on B200 for the benchmark programs ship in ``tuned_tiles.json``
+  (consulted after the local store, before the cost model).
+
+    python -m mlir_gpu_kernel_compiler_b200.autotune plan.json [...] [--out tuned_tiles.json]
 """
 from __future__ import annotations
 
@@ -114,6 +118,79 @@ def record(M, N, K, batch, dtype, b_mn_major, cfg: TileConfig, ms: float) -> Non
         os.replace(tmp, p)
 
 
+def _shipped() -> dict:
+    """Timed winners shipped with the package (measured on B200 by ``autotune_plan``)."""
+    p = Path(__file__).resolve().parent / "tuned_tiles.json"
+    try:
+        return json.loads(p.read_text())
+    except (OSError, ValueError):
+        return {}
+
+
+def lookup_any(M, N, K, batch, dtype, b_mn_major) -> TileConfig | None:
+    cfg = lookup(M, N, K, batch, dtype, b_mn_major)
+    if cfg is None:
+        d = _shipped().get(key(M, N, K, batch, dtype, b_mn_major))
+        cfg = TileConfig(**d["config"]) if d else None
+    return cfg
+
+
+def _single_kernel_plan(plan, k):
+    """A program holding just kernel ``k`` (its inputs become program inputs)."""
+    from .plan import PProgram
+
+    nodes = list(k.inputs) + [n for n in k.nodes if n not in k.inputs]
+    consts = [i for n in k.nodes for i in n.inputs if i.op == "const" and i not in nodes]
+    return PProgram(name=f"{plan.name}_k", nodes=consts + nodes, inputs=list(k.inputs), outputs=list(k.outputs),
+                    kernels=[k], aliases={})
+
+
+def autotune_plan(plan, device="cuda", top_k: int = 6, iters: int = 10, verbose: bool = False) -> dict:
+    """Time the top-k cost-model candidates of every tcgen05 GEMM of ``plan`` on the
+    device and record the fastest (CUDA events around the kernel, inputs random)."""
+    import torch
+
+    from .codegen.gemm import _mm_dims, tc_eligible
+    from .program import TORCH_DTYPE, B200Program
+
+    results = {}
+    for idx, k in enumerate(plan.kernels):
+        if k.kind != "matmul" or not tc_eligible(k):
+            continue
+        mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
+        batch = math.prod(out_shape[:-2]) if len(out_shape) > 2 else 1
+        sub = _single_kernel_plan(plan, k)
+        ins = [torch.randn(n.shape, device=device).mul_(0.05).to(TORCH_DTYPE[n.dtype]) for n in sub.inputs]
+        ranked = sorted(candidates(N, not tb), key=lambda c: cost_model(c, M, N, K, batch))
+        per_bn: dict[int, list] = {}
+        for c in ranked:                      # the best two of every tile width, best widths first
+            per_bn.setdefault(c.BN, [])
+            if len(per_bn[c.BN]) < 2:
+                per_bn[c.BN].append(c)
+        cands = [c for lst in per_bn.values() for c in lst][:top_k]
+        best, best_ms = None, float("inf")
+        for cfg in cands:
+            try:
+                prog = B200Program(sub, device=device, use_graph=False, tiles={0: cfg.as_dict()})
+                outs = [torch.empty(s, dtype=d, device=device) for s, d in prog.output_specs()]
+                prog.time_kernels(ins, outs, iters=2)
+                ms = prog.time_kernels(ins, outs, iters=iters)[0]
+                prog.check()
+                prog.close()
+            except Exception as e:  # a candidate that does not build or run is skipped
+                if verbose:
+                    print(f"  {cfg}: failed {str(e)[:120]}")
+                continue
+            if verbose:
+                print(f"  kernel {idx} {M}x{N}x{K} b{batch}: {cfg} {ms * 1e3:.1f} us")
+            if ms < best_ms:
+                best, best_ms = cfg, ms
+        if best is not None:
+            record(M, N, K, batch, a.dtype, not tb, best, best_ms)
+            results[key(M, N, K, batch, a.dtype, not tb)] = {"config": best.as_dict(), "ms": best_ms}
+    return results
+
+
 def tiles_for_plan(plan) -> dict:
     """Tile choice per matmul kernel index: a stored (timed) winner if there is one,
     else the cost-model pick.  ``TENSORJIT_B200_TILE=BN:STAGES[:GROUP_M]`` overrides."""
@@ -130,6 +207,34 @@ def tiles_for_plan(plan) -> dict:
             parts = [int(x) for x in env.split(":")]
             cfg = TileConfig(parts[0], parts[1], parts[2] if len(parts) > 2 else 16)
         else:
-            cfg = lookup(M, N, K, batch, a.dtype, not tb) or pick(M, N, K, batch, not tb)
+            cfg = lookup_any(M, N, K, batch, a.dtype, not tb) or pick(M, N, K, batch, not tb)
         out[idx] = cfg.as_dict()
     return out
+
+
+def main(argv=None):
+    import argparse
+
+    from .plan import PProgram
+
+    ap = argparse.ArgumentParser(description="time tcgen05 GEMM tile candidates for plans on the GPU")
+    ap.add_argument("plans", nargs="+")
+    ap.add_argument("--top-k", type=int, default=6)
+    ap.add_argument("--out", default=None, help="also merge the winners into this JSON file")
+    a = ap.parse_args(argv)
+    allres = {}
+    for p in a.plans:
+        print(p)
+        allres.update(autotune_plan(PProgram.load(p), top_k=a.top_k, verbose=True))
+    if a.out:
+        try:
+            cur = json.loads(Path(a.out).read_text())
+        except (OSError, ValueError):
+            cur = {}
+        cur.update(allres)
+        Path(a.out).write_text(json.dumps(cur, indent=1, sort_keys=True))
+    print(json.dumps(allres, indent=1))
+
+
+if __name__ == "__main__":
+    main()

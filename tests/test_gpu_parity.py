@@ -140,3 +140,24 @@ def test_unaligned_and_noncontiguous_inputs():
     wt = ins[1].t().contiguous().t()         # non-contiguous view of the same values
     y = B200Program(plan)(xv, wt, *ins[2:])[0]
     assert normwise_error(y, ref) <= 2e-2
+
+
+def test_host_pipeline_matches_direct_calls():
+    """Batches streamed from pinned host memory through HostPipeline equal direct calls."""
+    from mlir_gpu_kernel_compiler_b200 import B200Program
+    from mlir_gpu_kernel_compiler_b200.pipeline import HostPipeline
+
+    case = "cuda_mlp__bf16"
+    plan = FX.load_plan(case)
+    ins = [t.cuda() for t in FX.case_inputs(case)]
+    prog = B200Program(plan)
+    resident = {i: t for i, t in enumerate(ins) if i != 0}
+    pipe = HostPipeline(prog, [0], resident, depth=2)
+    xs = [(ins[0] + 0.25 * k).cpu().pin_memory() for k in range(5)]
+    outs = [[torch.empty(s, dtype=d).pin_memory() for s, d in prog.output_specs()] for _ in range(5)]
+    for k in range(5):
+        pipe.submit({0: xs[k]}, outs[k])
+    pipe.synchronize()
+    for k in range(5):
+        ref = prog(xs[k].cuda(), *ins[1:])[0].cpu()
+        assert torch.equal(outs[k][0], ref)
