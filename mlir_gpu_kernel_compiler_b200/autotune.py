@@ -145,6 +145,35 @@ def _single_kernel_plan(plan, k):
                     kernels=[k], aliases={})
 
 
+def _ranked_candidates(M, N, K, batch, b_mn_major, top_k):
+    ranked = sorted(candidates(N, b_mn_major), key=lambda c: cost_model(c, M, N, K, batch))
+    per_bn: dict[int, list] = {}
+    for c in ranked:                      # the best two of every tile width, best widths first
+        per_bn.setdefault(c.BN, [])
+        if len(per_bn[c.BN]) < 2:
+            per_bn[c.BN].append(c)
+    return [c for lst in per_bn.values() for c in lst][:top_k]
+
+
+def candidate_sources(plan, top_k: int = 6) -> list[tuple[str, str]]:
+    """(name, CUDA source) of every candidate ``autotune_plan`` would time, so they can be
+    compiled ahead of time (nvcc runs on the CPU)."""
+    from .codegen import generate
+    from .codegen.gemm import _mm_dims, tc_eligible
+
+    out = []
+    for k in plan.kernels:
+        if k.kind != "matmul" or not tc_eligible(k):
+            continue
+        mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
+        batch = math.prod(out_shape[:-2]) if len(out_shape) > 2 else 1
+        sub = _single_kernel_plan(plan, k)
+        for cfg in _ranked_candidates(M, N, K, batch, not tb, top_k):
+            ks = generate(sub, tiles={0: cfg.as_dict()})[0]
+            out.append((ks.symbol, ks.source))
+    return out
+
+
 def autotune_plan(plan, device="cuda", top_k: int = 6, iters: int = 10, verbose: bool = False) -> dict:
     """Time the top-k cost-model candidates of every tcgen05 GEMM of ``plan`` on the
     device and record the fastest (CUDA events around the kernel, inputs random)."""
@@ -161,13 +190,7 @@ def autotune_plan(plan, device="cuda", top_k: int = 6, iters: int = 10, verbose:
         batch = math.prod(out_shape[:-2]) if len(out_shape) > 2 else 1
         sub = _single_kernel_plan(plan, k)
         ins = [torch.randn(n.shape, device=device).mul_(0.05).to(TORCH_DTYPE[n.dtype]) for n in sub.inputs]
-        ranked = sorted(candidates(N, not tb), key=lambda c: cost_model(c, M, N, K, batch))
-        per_bn: dict[int, list] = {}
-        for c in ranked:                      # the best two of every tile width, best widths first
-            per_bn.setdefault(c.BN, [])
-            if len(per_bn[c.BN]) < 2:
-                per_bn[c.BN].append(c)
-        cands = [c for lst in per_bn.values() for c in lst][:top_k]
+        cands = _ranked_candidates(M, N, K, batch, not tb, top_k)
         best, best_ms = None, float("inf")
         for cfg in cands:
             try:

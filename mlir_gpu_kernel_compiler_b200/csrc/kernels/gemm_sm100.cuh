@@ -256,16 +256,24 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // stages the producer filled (and the phase it filled them in): on an abort, the
+  // copies still in flight are waited for before shared memory is released
+  uint32_t issued_phase[STAGES];
+  bool pending[STAGES];
+#pragma unroll
+  for (int s = 0; s < STAGES; ++s) pending[s] = false;
+
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t issued_phase[STAGES];
-      bool pending[STAGES];
-#pragma unroll
-      for (int s = 0; s < STAGES; ++s) pending[s] = false;
       bool ok = true;
+#ifdef TJ_TEST_STALL_FIRST_LOAD
+      // Failure-path test build only: the first stage is never filled, so the MMA warp's
+      // bounded wait on it must run out and report through the status words.
+      bool stall_pending = true;
+#endif
       for (long t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         long b;
         int mt, nt;
@@ -279,6 +287,16 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
             ok = false;
             break;
           }
+#ifdef TJ_TEST_STALL_FIRST_LOAD
+          if (stall_pending) {
+            stall_pending = false;
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
+#endif
           const uint32_t fb = smem_u32(&full[stage]);
           mbar_expect_tx(fb, STAGE_BYTES);
           tma_load_2d(smem_u32(sA + stage * A_BYTES), tmA, fb, kb * BK, a_row);
@@ -297,14 +315,6 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
             phase ^= 1u;
           }
         }
-      }
-      if (!ok) {
-        // abort: let every copy this thread issued land before shared memory is released
-        for (int s = 0; s < STAGES; ++s)
-          if (pending[s]) {
-            volatile int no_abort = 0;
-            mbar_wait(smem_u32(&full[s]), issued_phase[s], &no_abort, status, kernel_id * 16 + 5, 200000000ull);
-          }
       }
     }
   } else if (warp == 1) {
@@ -416,6 +426,14 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (warp == 0 && lane == 0 && *abort_flag) {
+    // abort: every copy the producer issued lands before this CTA's shared memory is released
+    for (int s = 0; s < STAGES; ++s)
+      if (pending[s]) {
+        volatile int no_abort = 0;
+        mbar_wait(smem_u32(&full[s]), issued_phase[s], &no_abort, status, kernel_id * 16 + 5, 200000000ull);
+      }
+  }
   if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
 }
 

@@ -82,7 +82,7 @@ class B200Program:
     backend = "b200"
 
     def __init__(self, program, device: str | torch.device = "cuda", use_graph: Optional[bool] = None,
-                 tune: bool = True, tiles: dict | None = None):
+                 tune: bool = True, tiles: dict | None = None, nvcc_flags: tuple = ()):
         self.program = program
         self.pplan: PProgram = as_plan(program)
         self.device = torch.device(device)
@@ -98,7 +98,7 @@ class B200Program:
         self.kernel_sources = generate(self.pplan, tiles=tiles)
         _trace("generated")
         self.source = "\n\n".join(ks.source for ks in self.kernel_sources)
-        self.cubins = compile_cubins([(ks.symbol, ks.source) for ks in self.kernel_sources])
+        self.cubins = compile_cubins([(ks.symbol, ks.source) for ks in self.kernel_sources], tuple(nvcc_flags))
         _trace("compiled")
         self.use_graph = (os.environ.get("TENSORJIT_B200_GRAPH", "1") == "1") if use_graph is None else use_graph
         g = self.pplan

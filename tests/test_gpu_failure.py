@@ -1,0 +1,45 @@
+"""Failure detection on the GPU without a fault: a bounded wait that runs out.
+
+A test build of the tcgen05 GEMM (``-DTJ_TEST_STALL_FIRST_LOAD``) never fills its
+first pipeline stage, so the MMA warp's wait on that stage cannot complete.  With
+the wait limit lowered to 20 ms (``-DTJ_WAIT_NS``), every CTA must give up, record
+(TIMEOUT, kernel*16 + site) in the program's status words, let its in-flight copies
+land, free TMEM and return.  The host reads the status, and the context must stay
+usable: the normal build of the same program then runs and matches the oracle.
+"""
+import pytest
+import torch
+
+from oracle import fixtures as FX
+from oracle.plan_oracle import evaluate, normwise_error
+
+pytestmark = pytest.mark.gpu
+
+
+def test_bounded_wait_timeout_reports_status_and_context_survives():
+    from mlir_gpu_kernel_compiler_b200 import B200Program
+    from mlir_gpu_kernel_compiler_b200.runtime import RuntimeError_
+
+    case = "gemm_tc_aligned__bf16"
+    plan = FX.load_plan(case)
+    ins = [t.cuda() for t in FX.case_inputs(case)]
+    bad = B200Program(plan, use_graph=False, nvcc_flags=("-DTJ_TEST_STALL_FIRST_LOAD", "-DTJ_WAIT_NS=20000000ull"))
+    outs = [torch.empty(s, dtype=d, device="cuda") for s, d in bad.output_specs()]
+    bad.run_into(ins, outs)
+    torch.cuda.synchronize()
+    code, where = bad.native.check_status()
+    assert code == 1                       # TJ_STATUS_WAIT_TIMEOUT
+    assert where // 16 == 0 and where % 16 in (1, 2, 3, 4)
+    # the words were cleared by the read
+    assert bad.native.check_status() == (0, 0)
+    # B200Program.check() raises on a recorded failure
+    bad.run_into(ins, outs)
+    with pytest.raises(RuntimeError_):
+        bad.check()
+    bad.close()
+    # the context is still healthy
+    good = B200Program(plan)
+    y = good(*ins)[0]
+    good.check()
+    ref = evaluate(plan, [t.cpu() for t in ins], round_stored=True)[0]
+    assert normwise_error(y, ref) <= 2e-2
