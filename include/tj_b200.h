@@ -84,7 +84,9 @@ typedef struct tj_launch {
   int32_t module;         /* index into the cubin list */
   uint32_t grid[3];       /* a zero extent skips the launch (empty tensors) */
   uint32_t block[3];
-  uint32_t cluster[3];    /* 0 or 1 = no cluster */
+  uint32_t cluster[3];    /* 0 or 1 = no cluster; a cluster launch must be a persistent kernel
+                             (work strided by gridDim): its grid is clamped at create time to the
+                             number of clusters that can be resident at once */
   uint32_t smem_bytes;    /* dynamic shared memory */
   uint32_t param_bytes;
   int32_t first_arg, num_args;

@@ -36,41 +36,55 @@ class TileConfig:
     BN: int
     STAGES: int
     GROUP_M: int = 16
+    PAIR: bool = False      # 2-SM cluster (cta_group::2), 256-row tiles
 
     def as_dict(self) -> dict:
         return asdict(self)
 
 
+STAGING = 32 * 1024          # TMA-store staging of the epilogue (8 warps x 2 x 2 KB)
+SMEM_BUDGET = 232448 - 1024 - STAGING - 256
+
+
 def candidates(N: int, b_mn_major: bool) -> list[TileConfig]:
     out = []
-    for bn in (256, 128, 64, 32):
-        if b_mn_major and bn % 64:
+    # CTA-pair (cta_group::2) tiles are correct but measured ~1.8x slower than single-CTA
+    # 128 x 256 tiles on B200 (cfg3: 1.52 ms vs 0.83 ms); they are searched only on request.
+    pairs = (False, True) if os.environ.get("TENSORJIT_B200_PAIR") == "1" else (False,)
+    for pair in pairs:
+        if pair and b_mn_major:
             continue
-        if bn > 64 and N <= bn // 2:
-            continue
-        stage = 128 * 64 * 2 + bn * 64 * 2
-        smax = max(2, min(8, (200 * 1024) // stage))
-        for st in sorted({smax, max(2, smax - 1), 3, 4} - {0}):
-            if st > smax:
+        for bn in ((256, 128) if pair else (256, 128, 64, 32)):
+            if b_mn_major and bn % 64:
                 continue
-            for gm in (8, 16, 32):
-                out.append(TileConfig(bn, st, gm))
+            if bn > 64 and N <= bn // 2:
+                continue
+            stage = 128 * 64 * 2 + (bn // 2 if pair else bn) * 64 * 2
+            smax = max(2, min(8, SMEM_BUDGET // stage))
+            for st in sorted({smax, max(2, smax - 1), 3, 4} - {0}):
+                if st > smax:
+                    continue
+                for gm in (8, 16, 32):
+                    out.append(TileConfig(bn, st, gm, pair))
     return out
 
 
 def cost_model(cfg: TileConfig, M: int, N: int, K: int, batch: int) -> float:
     """Lower is better (arbitrary units proportional to time)."""
-    m_tiles = math.ceil(M / 128)
+    rows = 256 if cfg.PAIR else 128
+    m_tiles = math.ceil(M / rows)
     n_tiles = math.ceil(N / cfg.BN)
     tiles = batch * m_tiles * n_tiles
-    waves = math.ceil(tiles / NUM_SMS)
+    waves = math.ceil(tiles / (NUM_SMS // 2 if cfg.PAIR else NUM_SMS))
     # MMA issue efficiency per tile: wider N amortises the A operand and the per-k overheads
     eff = {256: 1.0, 128: 0.93, 64: 0.8, 32: 0.6}[cfg.BN]
-    # work per wave in units of a full 128 x 256 x K tile
+    # work per wave in units of a full 128 x 256 x K tile per SM
     tile_work = (128 * cfg.BN * K) / (128 * 256 * max(K, 1))
     t = waves * tile_work / eff
+    if cfg.PAIR:
+        t *= 0.93     # half the B operand traffic per SM
     # fill: padded tile area / useful area
-    t *= (m_tiles * 128 * n_tiles * cfg.BN) / max(M * N, 1)
+    t *= (m_tiles * rows * n_tiles * cfg.BN) / max(M * N, 1)
     # shallow pipelines stall on HBM latency; every extra stage hides a little more
     if cfg.STAGES < 3:
         t *= 1.25
@@ -147,11 +161,11 @@ def _single_kernel_plan(plan, k):
 
 def _ranked_candidates(M, N, K, batch, b_mn_major, top_k):
     ranked = sorted(candidates(N, b_mn_major), key=lambda c: cost_model(c, M, N, K, batch))
-    per_bn: dict[int, list] = {}
-    for c in ranked:                      # the best two of every tile width, best widths first
-        per_bn.setdefault(c.BN, [])
-        if len(per_bn[c.BN]) < 2:
-            per_bn[c.BN].append(c)
+    per_bn: dict[tuple, list] = {}
+    for c in ranked:                      # the best two of every tile shape, best shapes first
+        per_bn.setdefault((c.BN, c.PAIR), [])
+        if len(per_bn[(c.BN, c.PAIR)]) < 2:
+            per_bn[(c.BN, c.PAIR)].append(c)
     return [c for lst in per_bn.values() for c in lst][:top_k]
 
 
@@ -216,7 +230,7 @@ def autotune_plan(plan, device="cuda", top_k: int = 6, iters: int = 10, verbose:
 
 def tiles_for_plan(plan) -> dict:
     """Tile choice per matmul kernel index: a stored (timed) winner if there is one,
-    else the cost-model pick.  ``TENSORJIT_B200_TILE=BN:STAGES[:GROUP_M]`` overrides."""
+    else the cost-model pick.  ``TENSORJIT_B200_TILE=BN:STAGES[:GROUP_M[:PAIR]]`` overrides."""
     from .codegen.gemm import _mm_dims, tc_eligible
 
     env = os.environ.get("TENSORJIT_B200_TILE")
@@ -228,7 +242,10 @@ def tiles_for_plan(plan) -> dict:
         batch = math.prod(out_shape[:-2]) if len(out_shape) > 2 else 1
         if env:
             parts = [int(x) for x in env.split(":")]
-            cfg = TileConfig(parts[0], parts[1], parts[2] if len(parts) > 2 else 16)
+            cfg = TileConfig(parts[0], parts[1], parts[2] if len(parts) > 2 else 16,
+                             bool(parts[3]) if len(parts) > 3 else False)
+            if cfg.PAIR and not tb:
+                cfg = TileConfig(cfg.BN, cfg.STAGES, cfg.GROUP_M, False)
         else:
             cfg = lookup_any(M, N, K, batch, a.dtype, not tb) or pick(M, N, K, batch, not tb)
         out[idx] = cfg.as_dict()

@@ -281,14 +281,16 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     epi = Epilogue(k, in_index, out_index)
     b_mn = not tb
     BN, STAGES, GROUP_M = choose_tile(M, N, batch, b_mn, tile)
+    pair = bool(tile and tile.get("PAIR")) and tb and BN in (128, 256)
     a_bs = _batch_strides(a, batch_shape)
     b_bs = _batch_strides(b, batch_shape)
     a_mats = prod(a.shape[:-2])
     b_mats = prod(b.shape[:-2])
     bl, bidx = decompose_stmts("b", batch_shape, "bb") if batch_shape else ([], [])
-    L = [HEADER, '#include "gemm_sm100.cuh"', params_struct(nptr, 3 if epi.tma_store_ok() else 2)]
+    L = [HEADER, '#include "gemm_sm100_pair.cuh"' if (tile and tile.get("PAIR") and tb) else '#include "gemm_sm100.cuh"',
+         params_struct(nptr, 3 if epi.tma_store_ok() else 2)]
     L.append("struct Cfg {")
-    epi_warps = 8 if BN % 64 == 0 else 4
+    epi_warps = 8 if (BN % 64 == 0 or pair) else 4
     threads = 64 + 32 * epi_warps
     tma_store = epi.tma_store_ok()
     out_stage = epi_warps * 2 * 32 * 32 * 2 if tma_store else 0
@@ -305,20 +307,24 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     L.append("  }")
     L.append(epi.vals32_function() if tma_store else epi.chunk32_function())
     L.append("};")
-    smem = 1024 + STAGES * (128 * 64 * 2 + BN * 64 * 2) + out_stage + (2 * STAGES + 6) * 8 + 16
+    b_rows = BN // 2 if pair else BN
+    smem = 1024 + STAGES * (128 * 64 * 2 + b_rows * 64 * 2) + out_stage + (2 * STAGES + 6) * 8 + 16
+    if smem > 232448:
+        raise ValueError(f"tile BN={BN} STAGES={STAGES} pair={pair} needs {smem} B of shared memory")
     L.append(f'extern "C" __global__ void __launch_bounds__({threads}, 1) {symbol}(const __grid_constant__ Params prm) {{')
-    L.append(f"  tjg::gemm_sm100<Cfg>(prm, (int*)prm.p[{status_idx}], {kernel_id});")
+    fn = "gemm_sm100_pair" if pair else "gemm_sm100"
+    L.append(f"  tjg::{fn}<Cfg>(prm, (int*)prm.p[{status_idx}], {kernel_id});")
     L.append("}")
-    m_tiles = (M + 127) // 128
+    m_tiles = (M + (255 if pair else 127)) // (256 if pair else 128)
     n_tiles = (N + BN - 1) // BN
     num_tiles = batch * m_tiles * n_tiles
-    grid = min(num_tiles, NUM_SMS)
+    grid = 2 * min(num_tiles, NUM_SMS // 2) if pair else min(num_tiles, NUM_SMS)
     esz = ITEM[a.dtype]
     tmA = TMapSpec(arg=in_index[a.id], dtype=a.dtype, dims=[K, a_mats * M], strides=[K * esz], box=[64, 128],
                    swizzle=3)
     if tb:
-        tmB = TMapSpec(arg=in_index[b.id], dtype=b.dtype, dims=[K, b_mats * N], strides=[K * esz], box=[64, BN],
-                       swizzle=3)
+        tmB = TMapSpec(arg=in_index[b.id], dtype=b.dtype, dims=[K, b_mats * N], strides=[K * esz],
+                       box=[64, BN // 2 if pair else BN], swizzle=3)
     else:
         tmB = TMapSpec(arg=in_index[b.id], dtype=b.dtype, dims=[N, K, b_mats], strides=[N * esz, K * N * esz],
                        box=[64, 64, 1], swizzle=3)
@@ -330,9 +336,9 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
                               box=[32, 32, 1], swizzle=2))
     args = [("node", n) for n in ins] + [("node", o) for o in outs] + [("status", None)]
     ks = KernelSource(symbol, "gemm_tc", "\n".join(L), (grid, 1, 1), (threads, 1, 1), args, smem=smem,
-                      tmaps=tmaps,
+                      tmaps=tmaps, cluster=(2, 1, 1) if pair else (1, 1, 1),
                       info={"M": M, "N": N, "K": K, "batch": batch, "BN": BN, "stages": STAGES,
-                            "tma_store": tma_store, "epi_warps": epi_warps,
+                            "tma_store": tma_store, "epi_warps": epi_warps, "pair": pair,
                             "flops": 2.0 * batch * M * N * K, "tiles": num_tiles,
                             "bytes": sum(n.nbytes for n in ins) + sum(o.nbytes for o in outs)})
     ks.finalize_params()

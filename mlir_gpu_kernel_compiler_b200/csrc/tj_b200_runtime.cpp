@@ -83,6 +83,7 @@ struct Driver {
   TJ_FN(cuEventRecord);
   TJ_FN(cuEventSynchronize);
   TJ_FN(cuEventElapsedTime);
+  TJ_FN(cuOccupancyMaxActiveClusters);
 #undef TJ_FN
 
   void load() {
@@ -106,6 +107,7 @@ struct Driver {
     TJ_SYM(cuGraphInstantiateWithFlags) TJ_SYM(cuGraphLaunch) TJ_SYM(cuGraphExecKernelNodeSetParams_v2)
     TJ_SYM(cuGraphExecDestroy) TJ_SYM(cuGraphDestroy) TJ_SYM(cuGetErrorString) TJ_SYM(cuEventCreate)
     TJ_SYM(cuEventDestroy_v2) TJ_SYM(cuEventRecord) TJ_SYM(cuEventSynchronize) TJ_SYM(cuEventElapsedTime)
+    TJ_SYM_OPT(cuOccupancyMaxActiveClusters)
 #undef TJ_SYM
 #undef TJ_SYM_OPT
     if (!all) return;
@@ -414,6 +416,33 @@ int tj_b200_program_create(const void* const* cubins, const size_t* cubin_sizes,
     if (k.launch.smem_bytes > 48 * 1024)
       TJ_CU(d.cuFuncSetAttribute(k.fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, k.launch.smem_bytes),
             "cuFuncSetAttribute(max dynamic smem)");
+    const uint32_t* cl = k.launch.cluster;
+    const uint32_t csize = (cl[0] ? cl[0] : 1) * (cl[1] ? cl[1] : 1) * (cl[2] ? cl[2] : 1);
+    if (csize > 1 && d.cuOccupancyMaxActiveClusters && !k.skip) {
+      // Cluster launches are persistent kernels (tiles strided by gridDim): clamp the grid to
+      // the clusters that can be resident at once, so no cluster waits for a second wave.
+      CUlaunchConfig cfg{};
+      cfg.gridDimX = k.launch.grid[0];
+      cfg.gridDimY = k.launch.grid[1];
+      cfg.gridDimZ = k.launch.grid[2];
+      cfg.blockDimX = k.launch.block[0];
+      cfg.blockDimY = k.launch.block[1];
+      cfg.blockDimZ = k.launch.block[2];
+      cfg.sharedMemBytes = k.launch.smem_bytes;
+      CUlaunchAttribute attr{};
+      attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+      attr.value.clusterDim.x = cl[0] ? cl[0] : 1;
+      attr.value.clusterDim.y = cl[1] ? cl[1] : 1;
+      attr.value.clusterDim.z = cl[2] ? cl[2] : 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int nclusters = 0;
+      if (d.cuOccupancyMaxActiveClusters(&nclusters, k.fn, &cfg) == CUDA_SUCCESS && nclusters > 0 &&
+          k.launch.grid[1] == 1 && k.launch.grid[2] == 1) {
+        const uint32_t cap = static_cast<uint32_t>(nclusters) * attr.value.clusterDim.x;
+        if (k.launch.grid[0] > cap) k.launch.grid[0] = cap;
+      }
+    }
     const char* pc = std::getenv("TENSORJIT_B200_PARAM_CHECK");
     if (d.cuFuncGetParamInfo && !(pc && pc[0] == '0')) {
       size_t off = 0, sz = 0;
