@@ -211,7 +211,7 @@ def autotune_plan(plan, device="cuda", top_k: int = 6, iters: int = 10, verbose:
                 prog = B200Program(sub, device=device, use_graph=False, tiles={0: cfg.as_dict()})
                 outs = [torch.empty(s, dtype=d, device=device) for s, d in prog.output_specs()]
                 prog.time_kernels(ins, outs, iters=2)
-                ms = prog.time_kernels(ins, outs, iters=iters)[0]
+                ms = sum(prog.time_kernels(ins, outs, iters=iters))
                 prog.check()
                 prog.close()
             except Exception as e:  # a candidate that does not build or run is skipped
@@ -240,6 +240,11 @@ def tiles_for_plan(plan) -> dict:
             continue
         mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
         batch = math.prod(out_shape[:-2]) if len(out_shape) > 2 else 1
+        if a.dtype == "f32":      # 3xTF32 kernels: a timed entry, else the generator's own choice
+            cfg = lookup_any(M, N, K, batch, a.dtype, not tb)
+            if cfg is not None:
+                out[idx] = cfg.as_dict()
+            continue
         if env:
             parts = [int(x) for x in env.split(":")]
             cfg = TileConfig(parts[0], parts[1], parts[2] if len(parts) > 2 else 16,

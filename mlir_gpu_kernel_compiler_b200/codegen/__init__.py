@@ -3,15 +3,17 @@
 ``generate`` walks the fused plan in order and dispatches on ``Kernel.kind``
 exactly like the reference backend (``tensorjit/backends/cuda_backend.py:437-456``):
 elementwise/copy -> vectorised grid-stride kernel, row -> staged row kernel,
-reduce -> row kernel with one stage, matmul -> tcgen05 GEMM (bf16/f16) or the
-SIMT GEMM (everything else).
+reduce -> row kernel with one stage, matmul -> tcgen05 GEMM (bf16/f16), the
+3xTF32 tcgen05 path (f32 with a K-major B: operand split pre-passes + GEMM), or the
+SIMT GEMM (everything else).  A plan kernel can therefore become several launches;
+``KernelSource.info["index"]`` names the plan kernel each launch belongs to.
 """
 from __future__ import annotations
 
 from ..plan import PProgram
 from .common import KernelSource
 from .ewise import gen_elementwise
-from .gemm import gen_gemm_simt, gen_gemm_tc, tc_eligible
+from .gemm import gen_gemm_simt, gen_gemm_tc, gen_matmul_tc_x3, tc_eligible, x3_eligible
 from .row import gen_row
 
 
@@ -27,6 +29,13 @@ def generate(plan: PProgram, tiles: dict | None = None, prefix: str = "tj") -> l
             x = k.anchor.inputs[0]
             ks = gen_row(k, [k], tuple(x.shape[:-1]), int(x.shape[-1]) if x.shape else 1, sym)
         elif k.kind == "matmul":
+            if tc_eligible(k) and x3_eligible(k):
+                parts = gen_matmul_tc_x3(k, sym, idx, (tiles or {}).get(idx))
+                for ks in parts:
+                    ks.info["kind"] = k.kind
+                    ks.info["index"] = idx
+                out += parts
+                continue
             if tc_eligible(k):
                 ks = gen_gemm_tc(k, sym, idx, (tiles or {}).get(idx))
             else:

@@ -49,13 +49,75 @@ def tc_eligible(k: PKernel) -> bool:
     mm, a, b, tb, M, N, K, _ = _mm_dims(k)
     if os.environ.get("TENSORJIT_B200_NO_TCGEN05") == "1":
         return False
+    if M == 0 or N == 0:
+        return False
+    if a.dtype == "f32" and b.dtype == "f32":
+        return x3_eligible(k)
     if a.dtype not in ("bf16", "f16") or b.dtype != a.dtype:
         return False
-    if K < 8 or K % 8 != 0 or M == 0 or N == 0:
+    if K < 8 or K % 8 != 0:
         return False
     if not tb and N % 8 != 0:
         return False
     return True
+
+
+def x3_eligible(k: PKernel) -> bool:
+    """f32 operands on the tensor cores as 3xTF32: needs a K-major B (nn.Linear weights)
+    and a 16-byte row pitch (K % 4 == 0)."""
+    mm, a, b, tb, M, N, K, _ = _mm_dims(k)
+    if os.environ.get("TENSORJIT_B200_NO_TF32X3") == "1":
+        return False
+    return a.dtype == b.dtype == "f32" and tb and K >= 4 and K % 4 == 0 and M > 0 and N > 0
+
+
+def gen_split_tf32(symbol: str, numel: int, src: tuple, hi_off: int, lo_off: int) -> KernelSource:
+    """x -> (hi, lo) with hi = x with its 13 low mantissa bits cleared (exactly a TF32 value)
+    and lo = x - hi (exact in f32): the operand split of 3xTF32 (hi*hi + hi*lo + lo*hi keeps
+    ~21 mantissa bits of every product)."""
+    n4 = numel // 4
+    L = [HEADER, params_struct(3, 0),
+         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{',
+         "  const float4* __restrict__ x = (const float4*)prm.p[0];",
+         "  float4* __restrict__ hi = (float4*)prm.p[1];",
+         "  float4* __restrict__ lo = (float4*)prm.p[2];",
+         f"  for (long i = (long)blockIdx.x * 256 + threadIdx.x; i < {n4}L; i += (long)gridDim.x * 256) {{",
+         "    const float4 v = __ldg(x + i);",
+         "    float4 h;",
+         "    h.x = __uint_as_float(__float_as_uint(v.x) & 0xffffe000u);",
+         "    h.y = __uint_as_float(__float_as_uint(v.y) & 0xffffe000u);",
+         "    h.z = __uint_as_float(__float_as_uint(v.z) & 0xffffe000u);",
+         "    h.w = __uint_as_float(__float_as_uint(v.w) & 0xffffe000u);",
+         "    hi[i] = h;",
+         "    lo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);",
+         "  }",
+         "}"]
+    grid = max(1, min((n4 + 255) // 256, NUM_SMS * 8))
+    ks = KernelSource(symbol, "split", "\n".join(L), (grid, 1, 1), (256, 1, 1),
+                      [src, ("scratch", hi_off), ("scratch", lo_off)],
+                      info={"bytes": numel * 12, "numel": numel})
+    ks.finalize_params()
+    return ks
+
+
+def _align(x: int, a: int = 256) -> int:
+    return (x + a - 1) // a * a
+
+
+def gen_matmul_tc_x3(k: PKernel, symbol: str, kernel_id: int, tile: dict | None) -> list[KernelSource]:
+    """f32 matmul as [split(A), split(B), 3xTF32 tcgen05 GEMM]; the hi/lo copies live in
+    the program's workspace (arena space after the planned intermediates)."""
+    mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
+    a_hi, a_lo = 0, _align(a.nbytes)
+    b_hi = a_lo + _align(a.nbytes)
+    b_lo = b_hi + _align(b.nbytes)
+    ws = b_lo + _align(b.nbytes)
+    sa = gen_split_tf32(f"{symbol}_split_a", a.numel, ("node", a), a_hi, a_lo)
+    sb = gen_split_tf32(f"{symbol}_split_b", b.numel, ("node", b), b_hi, b_lo)
+    g = gen_gemm_tc(k, symbol, kernel_id, tile, x3_scratch=(a_hi, b_hi, a_lo, b_lo))
+    for ks in (sa, sb, g):
+        ks.info["scratch_bytes"] = ws
+    return [sa, sb, g]
 
 
 # ---------------------------------------------------------------------------
@@ -269,33 +331,41 @@ def choose_tile(M: int, N: int, batch: int, b_mn_major: bool, override: dict | N
     return BN, STAGES, 16
 
 
-def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = None) -> KernelSource:
+def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = None,
+                x3_scratch: tuple | None = None) -> KernelSource:
     mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
     batch_shape = out_shape[:-2]
     batch = prod(batch_shape)
     ins, outs = list(k.inputs), list(k.outputs)
     in_index = {n.id: j for j, n in enumerate(ins)}
     out_index = {o.id: len(ins) + j for j, o in enumerate(outs)}
-    nptr = len(ins) + len(outs) + 1          # + status word
-    status_idx = nptr - 1
+    x3 = x3_scratch is not None
+    nptr = len(ins) + len(outs) + 1 + (4 if x3 else 0)   # + status word (+ hi/lo operand copies)
+    status_idx = len(ins) + len(outs)
     epi = Epilogue(k, in_index, out_index)
     b_mn = not tb
+    if x3 and not tile:
+        tile = {"BN": 64 if (M + 127) // 128 * ((N + 127) // 128) * batch < NUM_SMS else 128,
+                "STAGES": 4, "GROUP_M": 16}
     BN, STAGES, GROUP_M = choose_tile(M, N, batch, b_mn, tile)
-    pair = bool(tile and tile.get("PAIR")) and tb and BN in (128, 256)
+    if x3:
+        STAGES = min(STAGES, max(2, (200 * 1024) // (2 * (128 * 128 + BN * 128))))
+    pair = bool(tile and tile.get("PAIR")) and tb and BN in (128, 256) and not x3
     a_bs = _batch_strides(a, batch_shape)
     b_bs = _batch_strides(b, batch_shape)
     a_mats = prod(a.shape[:-2])
     b_mats = prod(b.shape[:-2])
     bl, bidx = decompose_stmts("b", batch_shape, "bb") if batch_shape else ([], [])
-    L = [HEADER, '#include "gemm_sm100_pair.cuh"' if (tile and tile.get("PAIR") and tb) else '#include "gemm_sm100.cuh"',
-         params_struct(nptr, 3 if epi.tma_store_ok() else 2)]
+    tma_store = epi.tma_store_ok() and not x3
+    L = [HEADER, '#include "gemm_sm100_pair.cuh"' if pair else '#include "gemm_sm100.cuh"',
+         params_struct(nptr, 4 if x3 else (3 if tma_store else 2))]
     L.append("struct Cfg {")
     epi_warps = 8 if (BN % 64 == 0 or pair) else 4
     threads = 64 + 32 * epi_warps
-    tma_store = epi.tma_store_ok()
     out_stage = epi_warps * 2 * 32 * 32 * 2 if tma_store else 0
     L.append(f"  static constexpr int BN = {BN}, STAGES = {STAGES}, M = {M}, N = {N}, K = {K}, GROUP_M = {GROUP_M};")
     L.append(f"  static constexpr int EPI_WARPS = {epi_warps};")
+    L.append(f"  static constexpr bool TF32X3 = {'true' if x3 else 'false'};")
     L.append(f"  static constexpr bool TMA_STORE = {'true' if tma_store else 'false'};")
     L.append(f"  using OutT = {CTYPE[outs[0].dtype] if tma_store else 'float'};")
     L.append(f"  static constexpr long BATCH = {batch}L;")
@@ -308,7 +378,7 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     L.append(epi.vals32_function() if tma_store else epi.chunk32_function())
     L.append("};")
     b_rows = BN // 2 if pair else BN
-    smem = 1024 + STAGES * (128 * 64 * 2 + b_rows * 64 * 2) + out_stage + (2 * STAGES + 6) * 8 + 16
+    smem = 1024 + STAGES * (2 if x3 else 1) * (128 * 128 + b_rows * 128) + out_stage + (2 * STAGES + 6) * 8 + 16
     if smem > 232448:
         raise ValueError(f"tile BN={BN} STAGES={STAGES} pair={pair} needs {smem} B of shared memory")
     L.append(f'extern "C" __global__ void __launch_bounds__({threads}, 1) {symbol}(const __grid_constant__ Params prm) {{')
@@ -320,25 +390,35 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     num_tiles = batch * m_tiles * n_tiles
     grid = 2 * min(num_tiles, NUM_SMS // 2) if pair else min(num_tiles, NUM_SMS)
     esz = ITEM[a.dtype]
-    tmA = TMapSpec(arg=in_index[a.id], dtype=a.dtype, dims=[K, a_mats * M], strides=[K * esz], box=[64, 128],
-                   swizzle=3)
+    bk = 128 // esz                      # K elements per 128-byte swizzle row
+    a_arg = in_index[a.id] if not x3 else status_idx + 1
+    b_arg = in_index[b.id] if not x3 else status_idx + 2
+    tmA = TMapSpec(arg=a_arg, dtype=a.dtype, dims=[K, a_mats * M], strides=[K * esz], box=[bk, 128], swizzle=3)
     if tb:
-        tmB = TMapSpec(arg=in_index[b.id], dtype=b.dtype, dims=[K, b_mats * N], strides=[K * esz],
-                       box=[64, BN // 2 if pair else BN], swizzle=3)
+        tmB = TMapSpec(arg=b_arg, dtype=b.dtype, dims=[K, b_mats * N], strides=[K * esz],
+                       box=[bk, BN // 2 if pair else BN], swizzle=3)
     else:
         tmB = TMapSpec(arg=in_index[b.id], dtype=b.dtype, dims=[N, K, b_mats], strides=[N * esz, K * N * esz],
                        box=[64, 64, 1], swizzle=3)
     tmaps = [tmA, tmB]
+    if x3:
+        tmaps.append(TMapSpec(arg=status_idx + 3, dtype="f32", dims=[K, a_mats * M], strides=[K * 4], box=[32, 128],
+                              swizzle=3))
+        tmaps.append(TMapSpec(arg=status_idx + 4, dtype="f32", dims=[K, b_mats * N], strides=[K * 4], box=[32, BN],
+                              swizzle=3))
     if tma_store:
         o = outs[0]
         oe = ITEM[o.dtype]
         tmaps.append(TMapSpec(arg=out_index[o.id], dtype=o.dtype, dims=[N, M, batch], strides=[N * oe, M * N * oe],
                               box=[32, 32, 1], swizzle=2))
     args = [("node", n) for n in ins] + [("node", o) for o in outs] + [("status", None)]
+    if x3:
+        a_hi, b_hi, a_lo, b_lo = x3_scratch
+        args += [("scratch", a_hi), ("scratch", b_hi), ("scratch", a_lo), ("scratch", b_lo)]
     ks = KernelSource(symbol, "gemm_tc", "\n".join(L), (grid, 1, 1), (threads, 1, 1), args, smem=smem,
                       tmaps=tmaps, cluster=(2, 1, 1) if pair else (1, 1, 1),
                       info={"M": M, "N": N, "K": K, "batch": batch, "BN": BN, "stages": STAGES,
-                            "tma_store": tma_store, "epi_warps": epi_warps, "pair": pair,
+                            "tma_store": tma_store, "epi_warps": epi_warps, "pair": pair, "tf32x3": x3,
                             "flops": 2.0 * batch * M * N * K, "tiles": num_tiles,
                             "bytes": sum(n.nbytes for n in ins) + sum(o.nbytes for o in outs)})
     ks.finalize_params()

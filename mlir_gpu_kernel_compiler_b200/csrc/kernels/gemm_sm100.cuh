@@ -128,6 +128,17 @@ TJ_DEV void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t i
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+TJ_DEV void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Instruction descriptor for kind::tf32 with f32 accumulation (A and B K-major).
+constexpr uint32_t idesc_tf32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
 TJ_DEV void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -193,17 +204,24 @@ TJ_DEV void tile_coords(long t, int m_tiles, int n_tiles, int group_m, long& b, 
 //     (values only; the kernel stages them in shared memory and stores 32 x 32 tiles with TMA)
 template <class Cfg, class P>
 __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel_id) {
-  constexpr int BM = 128, BK = 64;
+  // 3xTF32 mode (f32 operands): the stage holds hi and lo copies of A and B (written by the
+  // split pre-pass), and every k-step issues hi*hi + hi*lo + lo*hi into the f32 accumulator.
+  constexpr bool X3 = Cfg::TF32X3;
+  constexpr int ESZ = X3 ? 4 : 2;
+  constexpr int BM = 128, BK = 128 / ESZ;  // one 128-byte swizzle row of K per stage
+  constexpr int UK = 32 / ESZ;             // K of one MMA instruction (16 x 16-bit or 8 x tf32)
+  constexpr int OPC = X3 ? 2 : 1;          // operand copies per stage
   constexpr int BN = Cfg::BN, STAGES = Cfg::STAGES;
-  constexpr uint32_t A_BYTES = BM * BK * 2;
-  constexpr uint32_t B_BYTES = BN * BK * 2;
-  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t A_BYTES = BM * 128;
+  constexpr uint32_t B_BYTES = BN * 128;
+  constexpr uint32_t STAGE_BYTES = OPC * (A_BYTES + B_BYTES);
+  static_assert(!X3 || (!Cfg::B_MN_MAJOR && !Cfg::TMA_STORE), "3xTF32 mode: K-major B, direct stores");
   constexpr int m_tiles = (Cfg::M + BM - 1) / BM;
   constexpr int n_tiles = (Cfg::N + BN - 1) / BN;
   constexpr int k_blocks = (Cfg::K + BK - 1) / BK;
   constexpr long num_tiles = Cfg::BATCH * m_tiles * n_tiles;
   constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
-  constexpr uint32_t IDESC = idesc_f16(Cfg::BF16, BM, BN, false, Cfg::B_MN_MAJOR);
+  constexpr uint32_t IDESC = X3 ? idesc_tf32(BM, BN) : idesc_f16(Cfg::BF16, BM, BN, false, Cfg::B_MN_MAJOR);
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
   static_assert(!Cfg::B_MN_MAJOR || BN % 64 == 0, "N-major B needs BN multiple of 64");
   constexpr int EPI_WARPS = Cfg::EPI_WARPS;
@@ -213,10 +231,10 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzle atoms
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint8_t* sA = smem;                              // stage s: [A (hi)][A lo]
+  uint8_t* sB = smem + STAGES * OPC * A_BYTES;     // stage s: [B (hi)][B lo]
   // TMA-store staging: per epilogue warp two 32 x 32 output tiles (64-byte rows, 64B swizzle)
-  uint8_t* sOut = sB + STAGES * B_BYTES;
+  uint8_t* sOut = sB + STAGES * OPC * B_BYTES;
   constexpr uint32_t OUT_STAGE = Cfg::TMA_STORE ? 32 * 32 * 2 : 0;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + EPI_WARPS * 2 * OUT_STAGE);
   uint64_t* full = bars;
@@ -245,7 +263,8 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch(tmA);
     tma_prefetch(tmB);
-    if constexpr (Cfg::TMA_STORE) tma_prefetch(&prm.tm[2]);
+    if constexpr (Cfg::TMA_STORE || X3) tma_prefetch(&prm.tm[2]);
+    if constexpr (X3) tma_prefetch(&prm.tm[3]);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
@@ -299,14 +318,19 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
 #endif
           const uint32_t fb = smem_u32(&full[stage]);
           mbar_expect_tx(fb, STAGE_BYTES);
-          tma_load_2d(smem_u32(sA + stage * A_BYTES), tmA, fb, kb * BK, a_row);
+          uint8_t* a_st = sA + stage * OPC * A_BYTES;
+          uint8_t* b_st = sB + stage * OPC * B_BYTES;
+          tma_load_2d(smem_u32(a_st), tmA, fb, kb * BK, a_row);
           if constexpr (!Cfg::B_MN_MAJOR) {
-            tma_load_2d(smem_u32(sB + stage * B_BYTES), tmB, fb, kb * BK, static_cast<int>(bb * Cfg::N + n0));
+            tma_load_2d(smem_u32(b_st), tmB, fb, kb * BK, static_cast<int>(bb * Cfg::N + n0));
           } else {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c)
-              tma_load_3d(smem_u32(sB + stage * B_BYTES + c * (BK * 128)), tmB, fb, n0 + 64 * c, kb * BK,
-                          static_cast<int>(bb));
+              tma_load_3d(smem_u32(b_st + c * (BK * 128)), tmB, fb, n0 + 64 * c, kb * BK, static_cast<int>(bb));
+          }
+          if constexpr (X3) {
+            tma_load_2d(smem_u32(a_st + A_BYTES), &prm.tm[2], fb, kb * BK, a_row);
+            tma_load_2d(smem_u32(b_st + B_BYTES), &prm.tm[3], fb, kb * BK, static_cast<int>(bb * Cfg::N + n0));
           }
           pending[stage] = true;
           issued_phase[stage] = phase;
@@ -339,17 +363,25 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+          const uint32_t a0 = smem_u32(sA + stage * OPC * A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * OPC * B_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
+          for (int kk = 0; kk < BK / UK; ++kk) {
             const uint64_t ad = desc_sw128(a0 + kk * 32, 16, 1024);
             uint64_t bd;
             if constexpr (!Cfg::B_MN_MAJOR)
               bd = desc_sw128(b0 + kk * 32, 16, 1024);
             else
-              bd = desc_sw128(b0 + kk * 16 * 128, BK * 128, 1024);
-            umma_f16(d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+              bd = desc_sw128(b0 + kk * UK * 128, BK * 128, 1024);
+            if constexpr (!X3) {
+              umma_f16(d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+            } else {
+              const uint64_t ad_lo = desc_sw128(a0 + A_BYTES + kk * 32, 16, 1024);
+              const uint64_t bd_lo = desc_sw128(b0 + B_BYTES + kk * 32, 16, 1024);
+              umma_tf32(d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+              umma_tf32(d, ad, bd_lo, IDESC, 1u);
+              umma_tf32(d, ad_lo, bd, IDESC, 1u);
+            }
           }
           umma_commit(smem_u32(&empty[stage]));
           issued_any = true;

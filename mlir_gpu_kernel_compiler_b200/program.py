@@ -110,6 +110,10 @@ class B200Program:
                 if o.id in escaping and o not in self._out_nodes:
                     self._out_nodes.append(o)
         self._out_index = {o.id: j for j, o in enumerate(self._out_nodes)}
+        # kernel workspace (e.g. the 3xTF32 operand copies) follows the planned intermediates
+        self.ws_base = (self.plan.arena_bytes + 255) // 256 * 256
+        self.workspace_bytes = max([ks.info.get("scratch_bytes", 0) for ks in self.kernel_sources] + [0])
+        self.arena_bytes = self.ws_base + self.workspace_bytes if self.workspace_bytes else self.plan.arena_bytes
         self._launches, self._args, self._tmaps = self._tables()
         self._native: Optional[rt.NativeProgram] = None
         self.pool = OutputPool()
@@ -132,7 +136,12 @@ class B200Program:
         for m, ks in enumerate(self.kernel_sources):
             first_arg = len(args)
             for kind, node in ks.args:
-                args.append((rt.ARG_STATUS, 0) if kind == "status" else self._ref(node))
+                if kind == "status":
+                    args.append((rt.ARG_STATUS, 0))
+                elif kind == "scratch":
+                    args.append((rt.ARG_ARENA, self.ws_base + node))
+                else:
+                    args.append(self._ref(node))
             first_tmap = len(tmaps)
             for t in ks.tmaps:
                 from .codegen.common import TMAP_DTYPE
@@ -152,6 +161,11 @@ class B200Program:
 
     @property
     def num_kernels(self) -> int:
+        """Kernels of the plan (a plan kernel may take more than one launch)."""
+        return len(self.pplan.kernels)
+
+    @property
+    def num_launches(self) -> int:
         return len(self.kernel_sources)
 
     @property
@@ -166,8 +180,7 @@ class B200Program:
             # driver-API cuLaunchKernelEx from this library.
             torch.zeros(1, device=torch.device("cuda", idx))
             self._native = rt.NativeProgram(self.cubins, self._launches, self._args, self._tmaps,
-                                            self.plan.arena_bytes, len(self.pplan.inputs), len(self._out_nodes),
-                                            idx)
+                                            self.arena_bytes, len(self.pplan.inputs), len(self._out_nodes), idx)
             self._native.set_graph(self.use_graph)
         return self._native
 
@@ -209,11 +222,11 @@ class B200Program:
 
     def time_kernels(self, ins: list[torch.Tensor], outs: list[torch.Tensor], iters: int = 10,
                      stream: Optional[int] = None) -> list[float]:
-        """Mean device milliseconds of every kernel over ``iters`` direct (non-graph) runs."""
+        """Mean device milliseconds of every launch over ``iters`` direct (non-graph) runs."""
         if stream is None:
             stream = torch.cuda.current_stream(self.device).cuda_stream
         return self.native.time_kernels([t.data_ptr() for t in ins], [t.data_ptr() for t in outs], stream, iters,
-                                        self.num_kernels)
+                                        self.num_launches)
 
     def __call__(self, *inputs: torch.Tensor) -> list[torch.Tensor]:
         ins = self._prepare_inputs(inputs)

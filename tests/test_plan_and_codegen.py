@@ -43,7 +43,10 @@ def test_launch_geometry_and_kernel_families():
     p = FX.load_plan("cuda_mlp__f32")
     assert [k.kind for k in p.kernels] == ["row", "matmul", "matmul"]
     ks = generate(p)
-    assert [k.family for k in ks] == ["row", "gemm_simt", "gemm_simt"]
+    # f32 matmuls with a K-major B run as 3xTF32: two operand-split launches + the tcgen05 GEMM
+    assert [k.family for k in ks] == ["row", "split", "split", "gemm_tc", "split", "split", "gemm_tc"]
+    assert [k.info["index"] for k in ks] == [0, 1, 1, 1, 2, 2, 2]
+    assert all(k.info.get("tf32x3") for k in ks if k.family == "gemm_tc")
     # one row group per row, 256-thread CTAs
     assert ks[0].block[0] == 256 and ks[0].grid[0] * ks[0].info["rpc"] >= 64
     p16 = FX.load_plan("cuda_mlp__bf16")
@@ -58,7 +61,8 @@ def test_tensor_core_path_only_for_half_precision_with_aligned_pitch():
     fam = lambda n: [k.family for k in generate(FX.load_plan(n)) if k.family.startswith("gemm")]
     assert fam("cuda_wmma__f16") == ["gemm_tc"]
     assert fam("cuda_wmma__bf16") == ["gemm_tc"]
-    assert fam("cuda_wmma__f32") == ["gemm_simt"]
+    assert fam("cuda_wmma__f32") == ["gemm_tc"]                 # f32, K-major B: 3xTF32
+    assert fam("gemm_tc_nn_batched__f32") == ["gemm_simt"]      # f32 with an N-major B
     assert fam("matmul_epi_7x13x5__bf16") == ["gemm_simt"]       # K % 8 != 0
     assert fam("matmul_epi_33x128x65__bf16") == ["gemm_simt"]    # N-major B with N % 8 != 0
     assert fam("gemm_tc_nn_batched__bf16") == ["gemm_tc"]
@@ -154,3 +158,14 @@ def test_bf16_storage_emulation_in_oracle():
     a = evaluate(plan, ins)[0]
     b = evaluate(plan, ins, round_stored=True)[0]
     assert 0 < normwise_error(b, a) < 1e-2
+
+
+def test_x3_workspace_follows_the_planned_arena():
+    from mlir_gpu_kernel_compiler_b200.program import B200Program
+
+    prog = B200Program(FX.load_plan("cfg1"))
+    assert prog.ws_base >= prog.plan.arena_bytes and prog.ws_base % 256 == 0
+    a_bytes = 512 * 3072 * 4        # the larger A operand (h1) of the second GEMM
+    assert prog.workspace_bytes >= 2 * a_bytes
+    scratch = [v for (kind, v), L in zip(prog._args, [None] * len(prog._args)) if kind == 1 and v >= prog.ws_base]
+    assert scratch and max(scratch) < prog.arena_bytes
