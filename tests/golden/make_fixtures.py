@@ -118,6 +118,7 @@ def cases(tj):
     add("rows_odd", lambda x, g, b: tj.layer_norm(x, g, b), [(37, 333), (333,), (333,)])
     add("empty_rows", lambda x, b: tj.gelu(x + b), [(0, 16), (16,)], dtypes=(F32,))
     add("transpose_2d", lambda x: tj.permute(x, 1, 0) * 2.0, [(67, 129)])
+    add("linear_nobias_ragged", lambda x, w: tj.linear(x, w), [(200, 136), (300, 136)], dtypes=(F32,))
     return C
 
 
