@@ -144,6 +144,20 @@ TJ_API int tj_b200_program_info(void* program, tj_program_info* info);
 
 TJ_API int tj_b200_destroy(void* program);
 
+/* C[M,N] = A[M,K] * B[N,K]^T in f32 (row-major, contiguous, 16-byte aligned; K % 4 == 0),
+ * computed as 3xTF32 on the tensor cores -- WITHOUT allocating any device memory.
+ * No counterpart in the reference.  For callers that cannot call cudaMalloc: code inside a
+ * host application that owns all device memory and hands out only input/output buffers,
+ * and paths where an allocation could block or fail at the wrong moment.  Its workspace (the
+ * TF32 hi/lo copies of A and B) is a static __device__ array of 4 x 2^21 floats (32 MiB,
+ * held by every GPU that loads this library until exit): M*K and N*K must each be
+ * <= 2097152, larger calls return TJ_ERR_INVALID.  All calls share that array, so calls
+ * whose GPU work overlaps (different streams) race; serialise them.  The first call on a
+ * device resolves the array's address (cudaGetSymbolAddress, that device current) and
+ * should come before any stream capture.  `stream` is a cudaStream_t (NULL = legacy). */
+TJ_API int tj_b200_linear_f32_noalloc(const float* A, const float* B, float* C, int32_t M, int32_t N, int32_t K,
+                                      void* stream);
+
 /* Message of the last failure on this thread ("" if none). */
 TJ_API const char* tj_b200_last_error(void);
 

@@ -317,6 +317,9 @@ int build_graph(Program& p) {
 
 }  // namespace
 
+// Lets the other translation units of this library report through tj_b200_last_error().
+void tj_b200_internal_set_error(const char* msg) { g_last_error = msg ? msg : ""; }
+
 extern "C" {
 
 int tj_b200_abi_version(void) { return TJ_B200_ABI_VERSION; }

@@ -158,19 +158,22 @@ def compile_cubins(sources: list[tuple[str, str]], extra_flags: tuple = ()) -> l
 
 
 def build_runtime(force: bool = False) -> Path:
-    """Compile ``libtj_b200.so`` in-tree (g++, no CUDA library linked)."""
+    """Compile ``libtj_b200.so`` in-tree: the driver-API runtime (host C++; libcuda is opened
+    at run time) plus the allocation-free linear entry point (``tj_b200_noalloc.cu``, sm_100a,
+    static CUDA runtime).  The library loads on machines without a GPU."""
     with _lock:
         src = CSRC / "tj_b200_runtime.cpp"
+        na = CSRC / "tj_b200_noalloc.cu"
         hdr = INCLUDE / "tj_b200.h"
         stamp = LIB_PATH.with_suffix(".hash")
-        h = hashlib.sha256(src.read_bytes() + hdr.read_bytes()).hexdigest()
+        h = hashlib.sha256(src.read_bytes() + na.read_bytes() + hdr.read_bytes() + _headers_hash().encode()).hexdigest()
         if not force and LIB_PATH.exists() and stamp.exists() and stamp.read_text() == h:
             return LIB_PATH
         LIB_PATH.parent.mkdir(parents=True, exist_ok=True)
-        cxx = shutil.which("g++") or "/usr/bin/g++"
         tmp = LIB_PATH.with_suffix(f".{os.getpid()}.tmp")
-        cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", "-Wall",
-               f"-I{cuda_home() / 'include'}", f"-I{INCLUDE}", str(src), "-o", str(tmp), "-ldl", "-lpthread"]
+        cmd = [nvcc(), "-O2", "-std=c++17", "-shared", *ARCH_FLAGS, "-Xcompiler", "-fPIC,-fvisibility=hidden,-Wall",
+               "--expt-relaxed-constexpr", f"-I{INCLUDE}", f"-I{KDIR}", str(src), str(na), "-o", str(tmp),
+               "-ldl", "-lpthread"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise BuildError(f"runtime build failed:\n{r.stderr[-4000:]}")
