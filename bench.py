@@ -44,6 +44,11 @@ REF_SAMPLE = {"cfg1": ("cfg1", None), "cfg2": ("cfg2", None), "cfg3": ("cfg3_m51
               "cfg5": ("cfg5_m1024", 1024)}
 
 
+def _tensor_family(family: str) -> bool:
+    """Kernels whose roofline is the tensor core (GEMMs and the fused attention)."""
+    return family.startswith("gemm") or family == "attention"
+
+
 def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -244,7 +249,7 @@ def run_b200(a) -> None:
     pk = peaks()
     dom = max(range(len(kms)), key=lambda i: kms[i])
     ks = prog.kernel_sources[dom]
-    if ks.family.startswith("gemm"):
+    if _tensor_family(ks.family):
         ach = ks.info["flops"] / (kms[dom] * 1e-3) / 1e12
         peak = pk["bf16_tflops_sustained"] if a.config in ("cfg4", "cfg5") else pk["bf16_tflops"]
         roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
@@ -258,9 +263,9 @@ def run_b200(a) -> None:
                 "peak_kind": "copy bandwidth, " + ("of measured" if pk["source"] == "measured" else "of fallback")}
     roof["traffic"] = TRAFFIC.get((a.config, ks.symbol))
     per_kernel = [{"kernel": k.symbol, "family": k.family, "ms": round(m, 4),
-                   "rate": round((k.info["flops"] / (m * 1e-3) / 1e12) if k.family.startswith("gemm")
+                   "rate": round((k.info["flops"] / (m * 1e-3) / 1e12) if _tensor_family(k.family)
                                  else (k.info["bytes"] / (m * 1e-3) / 1e9), 1) if m > 0 else None,
-                   "rate_unit": "TFLOP/s" if k.family.startswith("gemm") else "GB/s"}
+                   "rate_unit": "TFLOP/s" if _tensor_family(k.family) else "GB/s"}
                   for k, m in zip(prog.kernel_sources, kms)]
 
     # end to end through the public API with host data every step: HostPipeline streams the

@@ -5,12 +5,14 @@ exactly like the reference backend (``tensorjit/backends/cuda_backend.py:437-456
 elementwise/copy -> vectorised grid-stride kernel, row -> staged row kernel,
 reduce -> row kernel with one stage, matmul -> tcgen05 GEMM (bf16/f16), the
 3xTF32 tcgen05 path (f32 with a K-major B: operand split pre-passes + GEMM), or the
-SIMT GEMM (everything else).  A plan kernel can therefore become several launches;
+SIMT GEMM (everything else); ``attention`` (the matmul -> softmax -> matmul chain
+``fuse.py`` folds into one kernel) -> the fused tcgen05 attention kernel.  A plan kernel can therefore become several launches;
 ``KernelSource.info["index"]`` names the plan kernel each launch belongs to.
 """
 from __future__ import annotations
 
 from ..plan import PProgram
+from .attention import gen_attention
 from .common import KernelSource
 from .ewise import gen_elementwise
 from .gemm import gen_gemm_simt, gen_gemm_tc, gen_matmul_tc_x3, tc_eligible, x3_eligible
@@ -28,6 +30,8 @@ def generate(plan: PProgram, tiles: dict | None = None, prefix: str = "tj") -> l
         elif k.kind == "reduce":
             x = k.anchor.inputs[0]
             ks = gen_row(k, [k], tuple(x.shape[:-1]), int(x.shape[-1]) if x.shape else 1, sym)
+        elif k.kind == "attention":
+            ks = gen_attention(k, sym, idx)
         elif k.kind == "matmul":
             if tc_eligible(k) and x3_eligible(k):
                 parts = gen_matmul_tc_x3(k, sym, idx, (tiles or {}).get(idx))

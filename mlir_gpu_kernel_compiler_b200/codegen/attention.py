@@ -1,0 +1,112 @@
+"""Code generation for ``attention`` kernels (the fused chain built by ``fuse.py``).
+
+The generated translation unit binds the shapes, the softmax scale and the
+operand addressing (including folded transposes) as compile-time constants of a
+``Cfg`` struct and instantiates ``tja::attention_sm100`` from
+``csrc/kernels/attention_sm100.cuh``.
+
+Addressing: every operand is read through a TMA tensor map whose dimensions are
+the operand's non-trivial logical dims ordered by memory stride (the head
+dimension first, stride 1).  The box is 64 elements of the head dimension by 128
+rows of the sequence dimension and 1 of every batch dimension, so whatever the
+memory layout ([B, H, S, D] contiguous, or the [B, S, H, D] a head split leaves
+before its transpose) the tile lands in shared memory as [128 rows][64] with the
+128-byte swizzle the tensor core reads.
+"""
+from __future__ import annotations
+
+from ..plan import PKernel
+from .common import CTYPE, ITEM, HEADER, KernelSource, TMapSpec, decompose_stmts, params_struct, prod
+
+LOG2E = 1.4426950408889634
+BM = 128
+BN = 128
+STAGES = 3
+THREADS = 384
+
+
+def _map_for(shape: tuple, strides: tuple, n_batch: int):
+    """Tensor-map dims of a logical [*batch, S, D] operand: ``ordered`` lists
+    (element stride, role, extent) innermost first, role 'd', 's' or a batch dim
+    index (size-1 batch dims are dropped); ``dims`` the extents in that order."""
+    roles = []
+    for i, (e, st) in enumerate(zip(shape, strides)):
+        if i < n_batch and e == 1:
+            continue
+        role = "d" if i == len(shape) - 1 else ("s" if i == len(shape) - 2 else i)
+        roles.append((st, role, e))
+    d = [x for x in roles if x[1] == "d"]
+    rest = sorted([x for x in roles if x[1] != "d"], key=lambda x: x[0])
+    ordered = d + rest
+    dims = [e for _, _, e in ordered]
+    return ordered, dims
+
+
+def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
+    a = k.attrs
+    batch = tuple(a["batch"])
+    nb = len(batch)
+    sq, sk, d, dv, dt = a["sq"], a["sk"], a["d"], a["dv"], a["dtype"]
+    esz = ITEM[dt]
+    ins = list(k.inputs)
+    out_node, out_st = a["out"]
+    in_index = {n.id: j for j, n in enumerate(ins)}
+    out_idx = len(ins)
+    status_idx = out_idx + 1
+    bh_total = prod(batch)
+    qpairs = (sq + 2 * BM - 1) // (2 * BM)
+
+    bl, bidx = decompose_stmts("bh", batch, "b") if batch else ([], [])
+    L = [HEADER, '#include "attention_sm100.cuh"', params_struct(status_idx + 1, 3)]
+    L.append("struct Cfg {")
+    L.append(f"  using T = {CTYPE[dt]};")
+    L.append(f"  static constexpr int SQ = {sq}, SK = {sk}, D = {d}, DV = {dv}, STAGES = {STAGES};")
+    L.append(f"  static constexpr long BATCH = {bh_total}L;")
+    L.append(f"  static constexpr bool BF16 = {'true' if dt == 'bf16' else 'false'};")
+    c = float(a["scale"]) * LOG2E
+    L.append(f"  static constexpr float C = {c!r}f;")
+    tmaps = []
+    for name, seq in (("q", sq), ("k", sk), ("v", sk)):
+        src, st = a[name]
+        shape = batch + (seq, d if name != "v" else dv)
+        ordered, dims = _map_for(shape, tuple(st), nb)
+        rank = len(ordered)
+        if not 2 <= rank <= 5:
+            raise ValueError(f"attention operand {name}: tensor map rank {rank}")
+        L.append(f"  static constexpr int {name.upper()}R = {rank};")
+        L.append(f"  static __device__ __forceinline__ void {name}_coords(long bh, int s0, int (&c)[5]) {{")
+        L += ["    " + s for s in bl]
+        for mi, (_, role, _) in enumerate(ordered):
+            if role == "d":
+                e = "0"
+            elif role == "s":
+                e = "s0"
+            else:
+                e = f"static_cast<int>({bidx[role]})"
+            L.append(f"    c[{mi}] = {e};")
+        L.append("  }")
+        box = [64] + [BM if role == "s" else 1 for _, role, _ in ordered[1:]]
+        tmaps.append(TMapSpec(arg=in_index[src.id], dtype=dt, dims=dims,
+                              strides=[s * esz for s, _, _ in ordered[1:]], box=box, swizzle=3))
+    L.append("  static __device__ __forceinline__ long out_offset(long bh, long s) {")
+    L += ["    " + s for s in bl]
+    terms = [f"{bidx[i]} * {out_st[i]}L" for i in range(nb) if batch[i] != 1 and out_st[i] != 0]
+    terms.append(f"s * {out_st[nb]}L")
+    L.append(f"    return {' + '.join(terms)};")
+    L.append("  }")
+    L.append("};")
+    L.append(f'extern "C" __global__ void __launch_bounds__({THREADS}, 1) {symbol}(const __grid_constant__ Params prm) {{')
+    L.append(f"  tja::attention_sm100<Cfg>(prm, ({CTYPE[dt]}*)prm.p[{out_idx}], (int*)prm.p[{status_idx}], {kernel_id});")
+    L.append("}")
+    q_bytes, kv_bytes, p_bytes = BM * d * esz, BN * d * esz, BM * BN * esz
+    smem = 1024 + 2 * q_bytes + 2 * p_bytes + STAGES * 2 * kv_bytes + (1 + 3 * STAGES + 8 + 1) * 8 + 16
+    args = [("node", n) for n in ins] + [("node", out_node), ("status", None)]
+    flops = 2.0 * bh_total * sq * sk * (d + dv)
+    nbytes = sum(n.nbytes for n in ins) + out_node.nbytes
+    ks = KernelSource(symbol, "attention", "\n".join(L), (bh_total * qpairs, 1, 1), (THREADS, 1, 1), args,
+                      smem=smem, tmaps=tmaps,
+                      info={"batch": bh_total, "sq": sq, "sk": sk, "d": d, "dv": dv, "flops": flops,
+                            "bytes": nbytes, "exps": float(bh_total * sq * sk), "scale": a["scale"],
+                            "ctas": bh_total * qpairs})
+    ks.finalize_params()
+    return ks

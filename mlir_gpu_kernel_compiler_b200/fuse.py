@@ -1,0 +1,219 @@
+"""Plan rewrites the B200 backend applies before code generation.
+
+tensorjit's fusion pass (``tensorjit/passes/fusion.py:104-330``) stops at matmul
+boundaries, so scaled-dot-product attention reaches a backend as three kernels:
+
+    k_i    matmul   S = Q @ K^T            (trans_b) [* c | / c]       -> [.., Sq, Sk]
+    k_i+1  row      P = exp(S - max(S)) / sum(exp(S - max(S)))  over the last axis
+    k_i+2  matmul   O = P @ V                                            -> [.., Sq, Dv]
+
+and, when Q/K/V come from a head split, with ``copy`` kernels (transposes) before
+them and after O.  ``fuse_attention`` replaces such a chain by one kernel of kind
+``attention`` whose score and probability matrices never reach HBM, and folds a
+transpose that only feeds Q, K or V (or only consumes O) into that kernel's
+addressing, so the copy kernel disappears as well.
+
+The rewrite is semantic-preserving for the plan's outputs only: S and P must not
+escape (not graph outputs, no user outside the chain), otherwise the chain is left
+as it is (e.g. a graph that returns the attention probabilities).  The memory plan
+of the rewritten program no longer holds S, P or the folded transposes.
+
+A fused kernel's ``attrs`` carry what code generation needs:
+    q, k, v: (source node, element strides over the logical [*batch, S, D] index)
+    out:     (node written, element strides over [*batch, Sq, Dv])
+    batch, sq, sk, d, dv, dtype, scale
+"""
+from __future__ import annotations
+
+import os
+from typing import Optional
+
+from .plan import PKernel, PNode, PProgram, contiguous_strides
+
+ATTENTION_HEAD_DIMS = (64,)
+
+
+def _const_value(n: PNode) -> Optional[float]:
+    if n.op == "const" and "value" in n.attrs:
+        return float(n.attrs["value"])
+    return None
+
+
+def _is_last_axis(node: PNode, rank: int) -> bool:
+    ax = node.attrs.get("axis")
+    return ax in (-1, rank - 1) and bool(node.attrs.get("keepdim"))
+
+
+def _only_users(n: PNode, allowed: set[int]) -> bool:
+    return bool(n.users) and all(u.id in allowed for u in n.users)
+
+
+def _copy_transpose_producer(plan: PProgram, x: PNode, consumer: PNode, escaping: set[int]):
+    """The copy kernel that materialises ``x`` as a plain transpose read only by
+    ``consumer`` (so the copy can be folded into the consumer's addressing)."""
+    if x.op != "transpose" or x.id in escaping or not _only_users(x, {consumer.id}):
+        return None
+    for ki, k in enumerate(plan.kernels):
+        if k.kind == "copy" and len(k.nodes) == 1 and k.nodes[0] is x and k.outputs == [x]:
+            return ki
+    return None
+
+
+def _operand(plan: PProgram, x: PNode, consumer: PNode, escaping: set[int]):
+    """(memory node, logical strides, folded copy kernel index or None) for a matmul operand."""
+    ki = _copy_transpose_producer(plan, x, consumer, escaping)
+    if ki is not None:
+        src = x.inputs[0]
+        cs = contiguous_strides(src.shape)
+        return src, tuple(cs[p] for p in x.attrs["perm"]), ki
+    return x, contiguous_strides(x.shape), None
+
+
+def match_attention(plan: PProgram, i: int, escaping: set[int]) -> Optional[dict]:
+    ks = plan.kernels
+    if i + 2 >= len(ks):
+        return None
+    k1, k2, k3 = ks[i], ks[i + 1], ks[i + 2]
+    if (k1.kind, k2.kind, k3.kind) != ("matmul", "row", "matmul"):
+        return None
+    mm1 = k1.anchor
+    if mm1 is None or mm1.op != "matmul" or not mm1.attrs.get("trans_b"):
+        return None
+    scale = 1.0
+    if len(k1.nodes) == 1:
+        s_node = mm1
+    elif len(k1.nodes) == 2:
+        e = k1.nodes[1]
+        others = [x for x in e.inputs if x is not mm1]
+        if len(e.inputs) != 2 or len(others) != 1 or _const_value(others[0]) is None:
+            return None
+        c = _const_value(others[0])
+        if e.op == "mul":
+            scale = c
+        elif e.op == "div" and e.inputs[0] is mm1 and c != 0.0:
+            scale = 1.0 / c
+        else:
+            return None
+        if not _only_users(mm1, {e.id}):
+            return None
+        s_node = e
+    else:
+        return None
+    if not (scale > 0.0 and scale < float("inf")):
+        return None
+    if k1.outputs != [s_node] or s_node.id in escaping or mm1.id in escaping:
+        return None
+    rank = len(s_node.shape)
+    if rank < 2:
+        return None
+    # the row kernel must be exactly a last-axis softmax of S
+    by_op: dict[str, list[PNode]] = {}
+    for n in k2.nodes:
+        by_op.setdefault(n.op, []).append(n)
+    if sorted(by_op) != ["div", "exp", "max", "sub", "sum"] or any(len(v) != 1 for v in by_op.values()):
+        return None
+    mx, sb, ex, sm, dv = by_op["max"][0], by_op["sub"][0], by_op["exp"][0], by_op["sum"][0], by_op["div"][0]
+    if not (mx.inputs == [s_node] and _is_last_axis(mx, rank) and sb.inputs == [s_node, mx]
+            and ex.inputs == [sb] and sm.inputs == [ex] and _is_last_axis(sm, rank) and dv.inputs == [ex, sm]):
+        return None
+    if k2.outputs != [dv] or dv.id in escaping or not _only_users(s_node, {mx.id, sb.id}):
+        return None
+    mm2 = k3.anchor
+    if mm2 is None or mm2.op != "matmul" or mm2.attrs.get("trans_b") or k3.nodes != [mm2] or k3.outputs != [mm2]:
+        return None
+    if mm2.inputs[0] is not dv or not _only_users(dv, {mm2.id}):
+        return None
+    q, kk, v = mm1.inputs[0], mm1.inputs[1], mm2.inputs[1]
+    dt = q.dtype
+    if dt not in ("bf16", "f16") or any(x.dtype != dt for x in (kk, v, mm1, s_node, mx, sb, ex, sm, dv, mm2)):
+        return None
+    if len(q.shape) != rank or len(kk.shape) != rank or len(v.shape) != rank:
+        return None
+    batch = tuple(q.shape[:-2])
+    sq, d = q.shape[-2:]
+    sk = kk.shape[-2]
+    dv_ = v.shape[-1]
+    if tuple(kk.shape[:-2]) != batch or tuple(v.shape[:-2]) != batch or kk.shape[-1] != d or v.shape[-2] != sk:
+        return None
+    if d not in ATTENTION_HEAD_DIMS or dv_ != d or sq < 1 or sk < 1:
+        return None
+    if sum(1 for b in batch if b != 1) > 3:
+        return None
+    folded = []
+    ops = {}
+    for name, x, consumer in (("q", q, mm1), ("k", kk, mm1), ("v", v, mm2)):
+        src, st, ki = _operand(plan, x, consumer, escaping)
+        if st[-1] != 1 or any(s % 8 for s, e in zip(st[:-1], x.shape[:-1]) if e != 1):
+            return None   # TMA: unit-stride rows, 16-byte aligned row/batch strides
+        ops[name] = (src, st)
+        if ki is not None:
+            folded.append(ki)
+    # O, possibly written through a transpose that is its only consumer
+    out_node, out_st = mm2, contiguous_strides(mm2.shape)
+    if mm2.id not in escaping and len(mm2.users) == 1 and mm2.users[0].op == "transpose":
+        t = mm2.users[0]
+        for ki, k in enumerate(ks):
+            if k.kind == "copy" and len(k.nodes) == 1 and k.nodes[0] is t and k.outputs == [t] and ki == i + 3:
+                perm = t.attrs["perm"]
+                cs_t = contiguous_strides(t.shape)
+                st = [0] * len(perm)
+                for dpos, p in enumerate(perm):
+                    st[p] = cs_t[dpos]
+                if st[-1] == 1 and all(s % 8 == 0 for s in st[:-1]):
+                    out_node, out_st = t, tuple(st)
+                    folded.append(ki)
+                break
+    return {
+        "kernels": (i, i + 1, i + 2), "folded": sorted(set(folded)),
+        "nodes": [mm1] + ([s_node] if s_node is not mm1 else []) + [mx, sb, ex, sm, dv, mm2],
+        "q": ops["q"], "k": ops["k"], "v": ops["v"], "out": (out_node, out_st),
+        "batch": batch, "sq": sq, "sk": sk, "d": d, "dv": dv_, "dtype": dt, "scale": scale,
+    }
+
+
+def fuse_attention(plan: PProgram) -> PProgram:
+    """Return ``plan`` with every eligible attention chain replaced by one kernel
+    (a new ``PProgram`` sharing the nodes; ``plan`` itself is not modified)."""
+    escaping = {plan.resolve(o).id for o in plan.outputs}
+    matches = []
+    i = 0
+    while i < len(plan.kernels):
+        m = match_attention(plan, i, escaping)
+        if m is not None:
+            matches.append(m)
+            i += 3
+        else:
+            i += 1
+    if not matches:
+        return plan
+    drop: set[int] = set()
+    replace: dict[int, PKernel] = {}
+    for m in matches:
+        i0, i1, i2 = m["kernels"]
+        drop.update((i1, i2))
+        drop.update(m["folded"])
+        srcs: list[PNode] = []
+        for name in ("q", "k", "v"):
+            if all(s is not m[name][0] for s in srcs):
+                srcs.append(m[name][0])
+        out_node = m["out"][0]
+        nodes = list(m["nodes"]) + ([out_node] if out_node is not m["nodes"][-1] else [])
+        fk = PKernel(kind="attention", nodes=nodes, anchor=m["nodes"][0], inputs=srcs, outputs=[out_node],
+                     iter_shape=tuple(out_node.shape))
+        fk.attrs = {k: m[k] for k in ("q", "k", "v", "out", "batch", "sq", "sk", "d", "dv", "dtype", "scale")}
+        replace[i0] = fk
+    kernels = []
+    for ki, k in enumerate(plan.kernels):
+        if ki in replace:
+            kernels.append(replace[ki])
+        elif ki not in drop:
+            kernels.append(k)
+    return PProgram(name=plan.name, nodes=plan.nodes, inputs=plan.inputs, outputs=plan.outputs, kernels=kernels,
+                    aliases=plan.aliases, meta=dict(plan.meta, fused_attention=len(matches)))
+
+
+def fuse(plan: PProgram) -> PProgram:
+    """All backend rewrites (``TENSORJIT_B200_FUSE=0`` disables them)."""
+    if os.environ.get("TENSORJIT_B200_FUSE", "1") == "0":
+        return plan
+    return fuse_attention(plan)

@@ -82,6 +82,7 @@ class PKernel:
     stages: list["PKernel"] = field(default_factory=list)
     rows: tuple = ()
     n: int = 0
+    attrs: dict = field(default_factory=dict)   # backend-side rewrites (fuse.py) describe their kernels here
 
     def __repr__(self) -> str:
         return f"PKernel<{self.kind} {[x.op for x in self.nodes]} -> {[o.name for o in self.outputs]}>"

@@ -29,6 +29,7 @@ import torch
 
 from . import runtime as rt
 from .codegen import generate
+from .fuse import fuse
 from .memory import MemoryPlan, plan_memory
 from .plan import PNode, PProgram, as_plan
 from .toolchain import compile_cubins
@@ -82,26 +83,28 @@ class B200Program:
     backend = "b200"
 
     def __init__(self, program, device: str | torch.device = "cuda", use_graph: Optional[bool] = None,
-                 tune: bool = True, tiles: dict | None = None, nvcc_flags: tuple = ()):
+                 tune: bool = True, tiles: dict | None = None, nvcc_flags: tuple = (), fuse_kernels: bool = True):
         self.program = program
         self.pplan: PProgram = as_plan(program)
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError(f"the b200 backend runs on CUDA devices, not {self.device}")
-        self.plan: MemoryPlan = plan_memory(self.pplan)
+        # the executed plan: attention chains fused, transposes folded (same inputs/outputs)
+        self.xplan: PProgram = fuse(self.pplan) if fuse_kernels else self.pplan
+        self.plan: MemoryPlan = plan_memory(self.xplan)
         _trace("planned")
         if tune and tiles is None:
             from .autotune import tiles_for_plan
 
-            tiles = tiles_for_plan(self.pplan)
+            tiles = tiles_for_plan(self.xplan)
         _trace("tiles", tiles)
-        self.kernel_sources = generate(self.pplan, tiles=tiles)
+        self.kernel_sources = generate(self.xplan, tiles=tiles)
         _trace("generated")
         self.source = "\n\n".join(ks.source for ks in self.kernel_sources)
         self.cubins = compile_cubins([(ks.symbol, ks.source) for ks in self.kernel_sources], tuple(nvcc_flags))
         _trace("compiled")
         self.use_graph = (os.environ.get("TENSORJIT_B200_GRAPH", "1") == "1") if use_graph is None else use_graph
-        g = self.pplan
+        g = self.xplan
         self._in_index = {n.id: i for i, n in enumerate(g.inputs)}
         escaping = {g.resolve(o).id for o in g.outputs}
         self._out_nodes: list[PNode] = []
@@ -161,8 +164,9 @@ class B200Program:
 
     @property
     def num_kernels(self) -> int:
-        """Kernels of the plan (a plan kernel may take more than one launch)."""
-        return len(self.pplan.kernels)
+        """Kernels of the executed plan (after attention fusion; a plan kernel may take
+        more than one launch)."""
+        return len(self.xplan.kernels)
 
     @property
     def num_launches(self) -> int:

@@ -125,6 +125,24 @@ def cases(tj):
     add("attention_probs_escape",
         lambda q, k, v: (lambda p_: (tj.matmul(p_, v), p_))(tj.softmax(tj.matmul(q, tj.transpose(k, -1, -2)) * 0.125)),
         [(1, 2, 128, 64), (1, 2, 384, 64), (1, 2, 384, 64)], dtypes=(BF16,))
+    # ragged query/key lengths (partial 128-row tiles and a masked last key block), scale as a divide
+    add("attention_ragged", lambda q, k, v: tj.matmul(tj.softmax(tj.matmul(q, tj.transpose(k, -1, -2)) / 8.0), v),
+        [(3, 200, 64), (3, 300, 64), (3, 300, 64)], dtypes=(BF16, F16))
+    # no scale, fewer queries and keys than one tile
+    add("attention_short", lambda q, k, v: tj.matmul(tj.softmax(tj.matmul(q, tj.transpose(k, -1, -2))), v),
+        [(2, 2, 40, 64), (2, 2, 72, 64), (2, 2, 72, 64)], dtypes=(F16,))
+
+    # head split / merge around the attention (the transformer config's layout, small)
+    def mha(x, wq, wk, wv, wo):
+        def heads(t):
+            return tj.permute(tj.reshape(t, (2, 256, 4, 64)), 0, 2, 1, 3)
+
+        # projections scaled by 1/sqrt(fan-in) so that q, k, v ~ N(0, 1) and the scores stay O(1)
+        q, k, v = (heads(tj.linear(x, w) * 0.08838834764831845) for w in (wq, wk, wv))
+        s = tj.softmax(tj.matmul(q, tj.transpose(k, -1, -2)) * 0.125)
+        return tj.linear(tj.reshape(tj.permute(tj.matmul(s, v), 0, 2, 1, 3), (512, 256)), wo) * 0.0625
+
+    add("attention_heads", mha, [(512, 128), (256, 128), (256, 128), (256, 128), (128, 256)], dtypes=(BF16,))
     return C
 
 

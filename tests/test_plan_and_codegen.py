@@ -169,3 +169,86 @@ def test_x3_workspace_follows_the_planned_arena():
     assert prog.workspace_bytes >= 2 * a_bytes
     scratch = [v for (kind, v), L in zip(prog._args, [None] * len(prog._args)) if kind == 1 and v >= prog.ws_base]
     assert scratch and max(scratch) < prog.arena_bytes
+
+
+# -- attention fusion (fuse.py) ----------------------------------------------------------
+def _fused(name):
+    from mlir_gpu_kernel_compiler_b200.fuse import fuse_attention
+
+    p = FX.load_plan(name)
+    return p, fuse_attention(p)
+
+
+@pytest.mark.parametrize("name,before,after", [
+    ("attention_core__bf16", 3, 1), ("attention_ragged__bf16", 3, 1), ("attention_ragged__f16", 3, 1),
+    ("attention_short__f16", 3, 1), ("attention_heads__bf16", 11, 5), ("cfg4", 16, 10)])
+def test_attention_chains_fuse_and_fold_their_transposes(name, before, after):
+    p, f = _fused(name)
+    assert len(p.kernels) == before and len(f.kernels) == after
+    att = [k for k in f.kernels if k.kind == "attention"]
+    assert len(att) == 1
+    a = att[0].attrs
+    assert a["d"] == a["dv"] == 64 and a["scale"] > 0
+    # no intermediate of the chain (scores, probabilities, folded copies) keeps arena storage
+    mp = plan_memory(f)
+    kept = {b.node.op for b in mp.buffers.values() if b.node is not att[0].outputs[0]}
+    assert not kept & {"div", "exp", "max", "sum", "transpose"}
+    assert mp.arena_bytes <= plan_memory(p).arena_bytes
+    # the original plan is left untouched
+    assert len(FX.load_plan(name).kernels) == len(p.kernels)
+
+
+def test_cfg4_attention_reads_and_writes_the_head_split_layout():
+    p, f = _fused("cfg4")
+    a = [k for k in f.kernels if k.kind == "attention"][0].attrs
+    # [8, 2048, 16, 64] matmul output viewed as [8, 16, 2048, 64]: (b, h, s, d) strides
+    for name in ("q", "k", "v"):
+        assert a[name][1] == (2048 * 16 * 64, 64, 16 * 64, 1)
+    assert a["out"][0].op == "transpose" and a["out"][1] == (2048 * 16 * 64, 64, 16 * 64, 1)
+    assert a["batch"] == (8, 16) and a["sq"] == a["sk"] == 2048 and a["scale"] == 0.125
+
+
+def test_attention_not_fused_when_probabilities_escape(monkeypatch):
+    p, f = _fused("attention_probs_escape__bf16")
+    assert [k.kind for k in f.kernels] == ["matmul", "row", "matmul"]
+    from mlir_gpu_kernel_compiler_b200.fuse import fuse
+
+    monkeypatch.setenv("TENSORJIT_B200_FUSE", "0")
+    p2 = FX.load_plan("attention_core__bf16")
+    assert fuse(p2) is p2
+
+
+def test_attention_not_fused_for_other_row_kernels():
+    from mlir_gpu_kernel_compiler_b200.fuse import fuse_attention
+
+    p = FX.load_plan("attention_core__bf16")
+    row = p.kernels[1]
+    ex = [n for n in row.nodes if n.op == "exp"][0]
+    ex.op = "tanh"                     # not a softmax any more
+    assert [k.kind for k in fuse_attention(p).kernels] == ["matmul", "row", "matmul"]
+
+
+def test_attention_tensor_maps_and_launch_geometry():
+    _, f = _fused("cfg4")
+    ks = [k for k in generate(f) if k.family == "attention"][0]
+    assert ks.grid == (128 * 8, 1, 1) and ks.block == (384, 1, 1)
+    assert ks.smem <= 232448 and len(ks.tmaps) == 3
+    for t in ks.tmaps:
+        # head dim innermost, then heads, sequence, batch -- strides increasing, 16-byte multiples
+        assert t.dims == [64, 16, 2048, 8] and t.box == [64, 1, 128, 1]
+        assert t.strides == sorted(t.strides) and all(s % 16 == 0 for s in t.strides)
+    _, f = _fused("attention_ragged__bf16")
+    ks = [k for k in generate(f) if k.family == "attention"][0]
+    assert ks.grid == (3, 1, 1)
+    assert [t.dims for t in ks.tmaps] == [[64, 200, 3], [64, 300, 3], [64, 300, 3]]
+
+
+@pytest.mark.parametrize("name", ["attention_core__bf16", "attention_ragged__f16", "attention_heads__bf16"])
+def test_fused_attention_compiles_for_sm100a(name):
+    from mlir_gpu_kernel_compiler_b200.toolchain import compile_cubins
+
+    _, f = _fused(name)
+    ks = generate(f)
+    assert any(k.family == "attention" for k in ks)
+    imgs = compile_cubins([(k.symbol, k.source) for k in ks])
+    assert all(img[:4] == b"\x7fELF" for img in imgs)
