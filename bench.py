@@ -59,13 +59,15 @@ def peaks() -> dict:
 
 
 class Clocks:
-    """SM clock and throttle reasons sampled every ~20 ms during the timed region (NVML;
-    nvidia-smi if NVML is unavailable)."""
+    """SM clock and throttle reasons sampled every ~3 ms during the timed region (NVML;
+    nvidia-smi every 200 ms if NVML is unavailable).  ``__enter__`` returns only once the
+    sampler is running, so even a timed region of a few milliseconds gets samples."""
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
     def __init__(self, index: int):
         self.index, self.rows, self._stop = index, [], threading.Event()
+        self._ready = threading.Event()
         self._t = None
 
     def _run_nvml(self):
@@ -75,11 +77,12 @@ class Clocks:
         try:
             h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
             mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self._ready.set()
             while not self._stop.is_set():
                 sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
                 r = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h)
                 self.rows.append((float(sm), float(mx), [k for k, v in self.REASONS.items() if r & v]))
-                self._stop.wait(0.02)
+                self._stop.wait(0.003)
         finally:
             pynvml.nvmlShutdown()
 
@@ -99,6 +102,7 @@ class Clocks:
         try:
             self._run_nvml()
         except Exception:
+            self._ready.set()
             try:
                 self._run_smi()
             except Exception:
@@ -107,6 +111,7 @@ class Clocks:
     def __enter__(self):
         self._t = threading.Thread(target=self._run, daemon=True)
         self._t.start()
+        self._ready.wait(timeout=10)
         return self
 
     def __exit__(self, *a):

@@ -15,14 +15,35 @@ before its transpose) the tile lands in shared memory as [128 rows][64] with the
 """
 from __future__ import annotations
 
+import os
+
 from ..plan import PKernel
 from .common import CTYPE, ITEM, HEADER, KernelSource, TMapSpec, decompose_stmts, params_struct, prod
 
 LOG2E = 1.4426950408889634
+# Softmax tuning: EMU of every 16 exponential pairs on the FMA pipe (polynomial) instead of
+# MUFU; DESYNC staggers the two query tiles by one key block; STAGES is the depth of the
+# K/V ring.
+# ``TENSORJIT_B200_ATTN="EMU=4,DESYNC=1"`` overrides.
+ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3}
+
+
+def attention_knobs() -> dict:
+    k = dict(ATTN_DEFAULTS)
+    env = os.environ.get("TENSORJIT_B200_ATTN", "")
+    for part in filter(None, (x.strip() for x in env.split(","))):
+        name, _, val = part.partition("=")
+        if name not in k:
+            raise ValueError(f"TENSORJIT_B200_ATTN: unknown knob {name!r}")
+        k[name] = int(val)
+    if not 0 <= k["EMU"] <= 16:
+        raise ValueError("TENSORJIT_B200_ATTN: EMU must be in 0..16")
+    if not 2 <= k["STAGES"] <= 6:
+        raise ValueError("TENSORJIT_B200_ATTN: STAGES must be in 2..6")
+    return k
 BM = 128
 BN = 128
-STAGES = 3
-THREADS = 384
+THREADS = 640
 
 
 def _map_for(shape: tuple, strides: tuple, n_batch: int):
@@ -56,6 +77,8 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     bh_total = prod(batch)
     qpairs = (sq + 2 * BM - 1) // (2 * BM)
 
+    kn = attention_knobs()
+    STAGES = kn["STAGES"]
     bl, bidx = decompose_stmts("bh", batch, "b") if batch else ([], [])
     L = [HEADER, '#include "attention_sm100.cuh"', params_struct(status_idx + 1, 3)]
     L.append("struct Cfg {")
@@ -63,6 +86,8 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     L.append(f"  static constexpr int SQ = {sq}, SK = {sk}, D = {d}, DV = {dv}, STAGES = {STAGES};")
     L.append(f"  static constexpr long BATCH = {bh_total}L;")
     L.append(f"  static constexpr bool BF16 = {'true' if dt == 'bf16' else 'false'};")
+    L.append(f"  static constexpr int EMU = {kn['EMU']};")
+    L.append(f"  static constexpr bool DESYNC = {'true' if kn['DESYNC'] else 'false'};")
     c = float(a["scale"]) * LOG2E
     L.append(f"  static constexpr float C = {c!r}f;")
     tmaps = []
@@ -98,8 +123,11 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     L.append(f'extern "C" __global__ void __launch_bounds__({THREADS}, 1) {symbol}(const __grid_constant__ Params prm) {{')
     L.append(f"  tja::attention_sm100<Cfg>(prm, ({CTYPE[dt]}*)prm.p[{out_idx}], (int*)prm.p[{status_idx}], {kernel_id});")
     L.append("}")
-    q_bytes, kv_bytes, p_bytes = BM * d * esz, BN * d * esz, BM * BN * esz
-    smem = 1024 + 2 * q_bytes + 2 * p_bytes + STAGES * 2 * kv_bytes + (1 + 3 * STAGES + 8 + 1) * 8 + 16
+    q_bytes, kv_bytes = BM * d * esz, BN * d * esz
+    # + half-row maxima (2 parities x 2 tiles x 2 halves x 128 f32) and sums (2 x 2 x 128 f32)
+    # + mbarriers (q_full, k/v_full and kv_empty per stage, s_full/s_free/p_ready/o_done/drain
+    # per tile, 8 half-row exchange barriers) + TMEM slot and abort flag
+    smem = 1024 + 2 * q_bytes + STAGES * 2 * kv_bytes + 4096 + 2048 + (19 + 3 * STAGES) * 8 + 8
     args = [("node", n) for n in ins] + [("node", out_node), ("status", None)]
     flops = 2.0 * bh_total * sq * sk * (d + dv)
     nbytes = sum(n.nbytes for n in ins) + out_node.nbytes

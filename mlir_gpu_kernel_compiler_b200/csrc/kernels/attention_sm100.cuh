@@ -5,24 +5,29 @@
 // which tensorjit plans as three kernels (matmul, row, matmul; the reference backend runs
 // them as tensorjit/backends/cuda_backend.py:299-429 and :163-297) that write and re-read the
 // [.., Sq, Sk] score and probability matrices through HBM.  Here S and P never leave the SM:
-// S lives in TMEM, P (bf16/f16, unnormalised) in shared memory, and the row statistics in
-// registers (online softmax: running max m and running sum l per query row; O is divided by
-// l once at the end).
+// S and P (bf16/f16, unnormalised) live in TMEM and the row statistics in registers (online
+// softmax: running max m and running sum l per query row; O is divided by l once at the end).
 //
 // One CTA owns two 128-row query tiles of one (batch, head) and streams the K/V blocks of
-// that head through a 3-stage TMA ring shared by both tiles.  Roles (384 threads; the
-// register budget of 12 warps, 168 per thread, holds a softmax thread's 128 scores without spills):
+// that head through a TMA ring shared by both tiles.  Roles (640 threads):
 //   warp 0      TMA producer: both Q tiles once, then K_j / V_j (128 keys x 64) per stage.
-//   warp 1      TMEM owner + MMA issuer (one lane):
-//                 S_t(j) = Q_t K_j^T      tcgen05.mma 128x128x16 x4   -> TMEM cols [128t, 128t+128)
-//                 O_t   += P_t(j) V_j      tcgen05.mma 128x64x16  x8   -> TMEM cols [256+64t, +64)
+//   warps 1, 2  MMA issuers for tile 0 / tile 1 (warp 1 also owns TMEM); each runs its loop
+//               converged and elect.sync picks the lane that issues each tcgen05.mma / commit:
+//                 S_t(j) = Q_t K_j^T    128x128x16 x4, A and B from smem -> TMEM S_t
+//                 O_t   += P_t(j) V_j    128x64x16  x8, A = P_t from TMEM -> TMEM O_t
 //               S_t(j+1) is issued as soon as softmax t has read S_t(j) out of TMEM, so the
-//               tensor core computes the next scores while the exponentials of block j run.
-//   warps 2-3   idle after setup.
-//   warps 4-7   softmax for tile 0, warps 8-11 for tile 1 (thread = query row = TMEM lane):
-//               tcgen05.ld S row, row max, lazy rescale, p = 2^(s*c - m) (c = scale*log2 e),
-//               row sum, P row -> shared memory (K-major, 128B swizzle: the A operand layout
-//               of the P V MMA), then the final O / l, stored straight to global memory.
+//               tensor core computes the next scores while the exponentials of block j run;
+//               one issuer per tile keeps each tile's chain independent of the other's.
+//   warp 3      idle after setup.
+//   warps 4-11  softmax for tile 0, warps 12-19 for tile 1.  A query row (TMEM lane) is shared
+//               by two threads in warps w and w+4 (same lane quadrant), one per half of the
+//               128 key columns: tcgen05.ld of its 64 scores, half-row max, the two halves'
+//               maxima exchanged through shared memory (one 64-arrival mbarrier per warp pair,
+//               one phase per key block, so the wait stays bounded), lazy rescale, p = 2^(s*c - m) (c = scale * log2 e), the
+//               half-row sum, 64 P values -> its 32 P columns in TMEM; at the end the two
+//               half sums are combined and each thread stores its 32 columns of O / l.
+// Two threads per row gives 16 softmax warps (4 per SM sub-partition), enough independent
+// work to keep the MUFU busy through the TMEM-load and row-max phases of the other warps.
 // Lazy rescale: the running max m moves only when a block's max exceeds it by more than
 // 8 (log2 units), so p <= 2^8 and the O accumulator is rescaled in TMEM (ld, scale, st)
 // only on those rare steps; the result is the same softmax since O and l share m.
@@ -34,6 +39,8 @@
 #include "gemm_sm100.cuh"
 
 namespace tja {
+using namespace tjg;
+
 using namespace tjg;
 
 TJ_DEV void tma_load_4d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int c1, int c2, int c3) {
@@ -67,6 +74,28 @@ TJ_DEV float ex2_approx(float x) {
   return y;
 }
 
+// 2^x without MUFU, for the share of exponentials moved to the FMA/ALU pipes:
+// x = j + f with j = round(x) (added to the exponent field) and f in [-0.5, 0.5], where
+// 2^f is a degree-3 polynomial whose coefficients were fitted here for minimal relative
+// error on that interval (Lawson-weighted least squares; max relative error 7.7e-5, below
+// half an ulp of the bf16/f16 probabilities it feeds).  Valid for x <= 127; x < -126
+// (including -inf for masked keys) returns 2^-126 * 2^f, i.e. 0 after rounding to bf16/f16.
+TJ_DEV float ex2_poly(float x) {
+  x = fmaxf(x, -126.0f);
+  const float t = x + 12582912.0f;  // 1.5 * 2^23: x rounded to an integer in the low mantissa bits
+  const float f = x - (t - 12582912.0f);
+  const float p = fmaf(fmaf(fmaf(0.05522261559963226f, f, 0.24261537194252014f), f, 0.6932516098022461f), f,
+                       0.9999275803565979f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// max of three (one PTX max.f32 with three sources, sm_100)
+TJ_DEV float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // 32 lanes x 32 consecutive f32 columns, no wait (the caller waits once for several loads).
 TJ_DEV void tmem_ld32_async(uint32_t taddr, uint32_t* r) {
   asm volatile(
@@ -80,18 +109,15 @@ TJ_DEV void tmem_ld32_async(uint32_t taddr, uint32_t* r) {
       : "memory");
 }
 
-// Four 32-column loads (128 columns of one lane quadrant) and one wait that names every
+// Two 32-column loads (64 columns of one lane quadrant) and one wait that names every
 // destination register, so no use of them can be scheduled before the data has landed.
-TJ_DEV void tmem_ld128(uint32_t taddr, uint32_t (&r)[128]) {
+TJ_DEV void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
   tmem_ld32_async(taddr, r);
   tmem_ld32_async(taddr + 32, r + 32);
-  tmem_ld32_async(taddr + 64, r + 64);
-  tmem_ld32_async(taddr + 96, r + 96);
 #define TJA_R8(i) "+r"(r[i]), "+r"(r[i + 1]), "+r"(r[i + 2]), "+r"(r[i + 3]), "+r"(r[i + 4]), "+r"(r[i + 5]), \
                   "+r"(r[i + 6]), "+r"(r[i + 7])
   asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : TJA_R8(0), TJA_R8(8), TJA_R8(16), TJA_R8(24), TJA_R8(32), TJA_R8(40), TJA_R8(48), TJA_R8(56),
-                 TJA_R8(64), TJA_R8(72), TJA_R8(80), TJA_R8(88), TJA_R8(96), TJA_R8(104), TJA_R8(112), TJA_R8(120)
+               : TJA_R8(0), TJA_R8(8), TJA_R8(16), TJA_R8(24), TJA_R8(32), TJA_R8(40), TJA_R8(48), TJA_R8(56)
                :
                : "memory");
 #undef TJA_R8
@@ -110,12 +136,68 @@ TJ_DEV void tmem_st32_wait(uint32_t taddr, const float (&v)[32]) {
       : "memory");
 }
 
+// the same for 32 packed words (two bf16/f16 per column)
+TJ_DEV void tmem_st32_wait(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+// D (TMEM) += A (TMEM) * B (smem descriptor), kind::f16; A is M x 16 with row i in lane i and
+// two 16-bit elements per 32-bit column (8 columns per instruction).  Issued by one elected
+// lane of a converged warp.
+TJ_DEV void umma_f16_ts_elect(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n elect.sync _|e, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+
 template <class T> TJ_DEV uint32_t pack2(float lo, float hi);
 template <> TJ_DEV uint32_t pack2<__nv_bfloat16>(float lo, float hi) { return tj_pack_bf16x2(lo, hi); }
 template <> TJ_DEV uint32_t pack2<__half>(float lo, float hi) { return tj_pack_f16x2(lo, hi); }
 
+// p = 2^(x*c - m) for the column pairs [I0, I0 + 16) of a 64-column half row, packed two per
+// word to the element type; l0 / l1 accumulate the sum of the even / odd columns.  EMU of
+// every 16 pairs use ex2_poly (FMA pipe), the rest ex2.approx (MUFU).
+template <int I0, class T, int EMU>
+TJ_DEV void exp_pairs(const float (&x)[64], float c, float m, uint32_t (&pk)[16], float& l0, float& l1) {
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int i = I0 + k;
+    const float a0 = fmaf(x[2 * i], c, -m), a1 = fmaf(x[2 * i + 1], c, -m);
+    const bool emu = (i & 15) < EMU;
+    const float p0 = emu ? ex2_poly(a0) : ex2_approx(a0);
+    const float p1 = emu ? ex2_poly(a1) : ex2_approx(a1);
+    l0 += p0;
+    l1 += p1;
+    pk[k] = pack2<T>(p0, p1);
+  }
+}
+
+// 16 consecutive 32-bit columns of one lane quadrant from registers into TMEM, then wait.
+TJ_DEV void tmem_st16_wait(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16};\n"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
 // Cfg provides:
 //   static constexpr int SQ, SK, D, DV, STAGES, QR, KR, VR (tensor-map ranks);
+//   static constexpr int EMU (exponentials of every 16 column pairs computed by ex2_poly, 0..16);
+//   static constexpr bool DESYNC (tile 1 starts one key block behind tile 0);
 //   static constexpr long BATCH;  static constexpr bool BF16;  static constexpr float C (scale * log2 e, > 0);
 //   using T = element type (__nv_bfloat16 / __half);
 //   static __device__ void q_coords(long bh, int s0, int (&c)[5]);   (and k_coords, v_coords)
@@ -130,11 +212,14 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
   constexpr uint32_t Q_BYTES = BM * D * 2;   // 16 KB, [128 rows][64] 128B-swizzled
   constexpr uint32_t K_BYTES = BN * D * 2;   // 16 KB
   constexpr uint32_t V_BYTES = BN * DV * 2;  // 16 KB, [128 keys][64 dv] (N-major B operand)
-  constexpr uint32_t P_BYTES = BM * BN * 2;  // 32 KB, two [128][64] K-major chunks
   constexpr int NB = (Cfg::SK + BN - 1) / BN;
   constexpr int LAST_VALID = Cfg::SK - (NB - 1) * BN;  // valid keys in the last block
   constexpr int QPAIRS = (Cfg::SQ + 2 * BM - 1) / (2 * BM);
+  constexpr int SM_THREADS = 256;  // softmax threads per tile (8 warps)
+  // TMEM columns: S_0 [0,128) S_1 [128,256) O_0 [256,320) O_1 [320,384)
+  //               P_0 [384,448) P_1 [448,512) (128 keys of bf16/f16 packed two per column)
   constexpr uint32_t TMEM_COLS = 512;
+  constexpr uint32_t P_COL = 2 * BN + 2 * DV;
   constexpr uint32_t IDESC_S = idesc_f16(Cfg::BF16, BM, BN, false, false);
   constexpr uint32_t IDESC_O = idesc_f16(Cfg::BF16, BM, DV, false, true);
   constexpr float RESCALE_THRESHOLD = 8.0f;
@@ -142,10 +227,11 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                        // 2 x Q_BYTES
-  uint8_t* sP = sQ + 2 * Q_BYTES;            // 2 x P_BYTES
-  uint8_t* sK = sP + 2 * P_BYTES;            // STAGES x K_BYTES
+  uint8_t* sK = sQ + 2 * Q_BYTES;            // STAGES x K_BYTES
   uint8_t* sV = sK + STAGES * K_BYTES;       // STAGES x V_BYTES
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + STAGES * V_BYTES);
+  float* xmax = reinterpret_cast<float*>(sV + STAGES * V_BYTES);  // [2 parity][2 tiles][2 halves][128 rows]
+  float* xsum = xmax + 2 * 2 * 2 * BM;                             // [2 tiles][2 halves][128 rows]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xsum + 2 * 2 * BM);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + STAGES;
@@ -154,8 +240,9 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
   uint64_t* s_free = s_full + 2;         // [2]
   uint64_t* p_ready = s_free + 2;        // [2]
   uint64_t* o_done = p_ready + 2;        // [2]
-  uint64_t* drain = o_done + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* drain = o_done + 2;          // [2]
+  uint64_t* xbar = drain + 2;            // [2 tiles x 4 lane quadrants]: half-row exchange
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -168,15 +255,16 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(&k_full[s]), 1);
       mbar_init(smem_u32(&v_full[s]), 1);
-      mbar_init(smem_u32(&kv_empty[s]), 1);
+      mbar_init(smem_u32(&kv_empty[s]), ntiles);  // one commit per tile's MMA warp
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(smem_u32(&s_full[t]), 1);
-      mbar_init(smem_u32(&s_free[t]), 128);
-      mbar_init(smem_u32(&p_ready[t]), 128);
+      mbar_init(smem_u32(&s_free[t]), SM_THREADS);
+      mbar_init(smem_u32(&p_ready[t]), SM_THREADS);
       mbar_init(smem_u32(&o_done[t]), 1);
+      mbar_init(smem_u32(&drain[t]), 1);
     }
-    mbar_init(smem_u32(drain), 1);
+    for (int i = 0; i < 8; ++i) mbar_init(smem_u32(&xbar[i]), 64);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch(&prm.tm[0]);
@@ -220,114 +308,128 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
         issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
       }
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, status, kernel_id * 16 + 2) &&
-                mbar_wait(smem_u32(&k_full[0]), 0, abort_flag, status, kernel_id * 16 + 2);
-      bool issued_any = false;
-      auto issue_s = [&](int t, int s) {
-        const uint32_t a0 = smem_u32(sQ + t * Q_BYTES), b0 = smem_u32(sK + s * K_BYTES);
+  } else if (warp == 1 || warp == 2) {
+    // ---------------- MMA issuers: warp 1 for tile 0, warp 2 for tile 1 ----------------
+    const int t = warp - 1;
+    bool ok = t < ntiles;
+    bool issued_any = false;
+    if (ok)
+      ok = mbar_wait_warp(smem_u32(q_full), 0, abort_flag, status, kernel_id * 16 + 2) &&
+           mbar_wait_warp(smem_u32(&k_full[0]), 0, abort_flag, status, kernel_id * 16 + 2);
+    // smem descriptors built once; stepping through K adds (byte offset >> 4) to the
+    // start-address field, so each MMA costs one 64-bit add on warp-uniform values
+    const uint64_t dq = desc_sw128(smem_u32(sQ + t * Q_BYTES), 16, 1024);
+    const uint64_t dk0 = desc_sw128(smem_u32(sK), 16, 1024);
+    const uint64_t dv0 = desc_sw128(smem_u32(sV), BN * 128, 1024);
+    const uint32_t tS = tmem_base + t * BN, tO = tmem_base + 2 * BN + t * DV, tP = tmem_base + P_COL + t * (BN / 2);
+    auto issue_s = [&](int s) {
+      const uint64_t b = dk0 + ((s * K_BYTES) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_f16(tmem_base + t * BN, desc_sw128(a0 + kk * 32, 16, 1024), desc_sw128(b0 + kk * 32, 16, 1024), IDESC_S,
-                   kk > 0 ? 1u : 0u);
-        umma_commit(smem_u32(&s_full[t]));
-        issued_any = true;
-      };
-      auto issue_pv = [&](int t, int s, bool acc) {
-        const uint32_t a0 = smem_u32(sP + t * P_BYTES), b0 = smem_u32(sV + s * V_BYTES);
+      for (int kk = 0; kk < D / 16; ++kk) umma_f16_elect(tS, dq + 2 * kk, b + 2 * kk, IDESC_S, kk > 0);
+      umma_commit_elect(smem_u32(&s_full[t]));
+      issued_any = true;
+    };
+    auto issue_pv = [&](int s, bool acc) {
+      const uint64_t b = dv0 + ((s * V_BYTES) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          umma_f16(tmem_base + 2 * BN + t * DV, desc_sw128(a0 + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024),
-                   desc_sw128(b0 + kk * 16 * 128, BN * 128, 1024), IDESC_O, (acc || kk > 0) ? 1u : 0u);
-        umma_commit(smem_u32(&o_done[t]));
-        issued_any = true;
-      };
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < ntiles; ++t) issue_s(t, 0);
-      }
-      for (int j = 0; j < NB && ok; ++j) {
-        const int s = j % STAGES;
-        if (j + 1 < NB) {
-          const int s1 = (j + 1) % STAGES;
-          if (!mbar_wait(smem_u32(&k_full[s1]), ((j + 1) / STAGES) & 1, abort_flag, status, kernel_id * 16 + 3)) {
-            ok = false;
-            break;
-          }
-          for (int t = 0; t < ntiles && ok; ++t) {
-            if (!mbar_wait(smem_u32(&s_free[t]), j & 1, abort_flag, status, kernel_id * 16 + 4)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_s(t, s1);
-          }
-          if (!ok) break;
-        }
-        if (!mbar_wait(smem_u32(&v_full[s]), (j / STAGES) & 1, abort_flag, status, kernel_id * 16 + 3)) {
+      for (int kk = 0; kk < BN / 16; ++kk)
+        umma_f16_ts_elect(tO, tP + kk * 8, b + ((kk * 16 * 128) >> 4), IDESC_O, (acc || kk > 0) ? 1u : 0u);
+      umma_commit_elect(smem_u32(&o_done[t]));
+      issued_any = true;
+    };
+    if (ok) {
+      tc_fence_after();
+      issue_s(0);
+    }
+    // per key block j: S_t(j+1) as soon as softmax t has read S_t(j) out of TMEM, then
+    // O_t += P_t(j) V_j once softmax t has written P_t(j)
+    for (int j = 0; j < NB && ok; ++j) {
+      const int s = j % STAGES;
+      if (j + 1 < NB) {
+        const int s1 = (j + 1) % STAGES;
+        if (!mbar_wait_warp(smem_u32(&k_full[s1]), ((j + 1) / STAGES) & 1, abort_flag, status, kernel_id * 16 + 3) ||
+            !mbar_wait_warp(smem_u32(&s_free[t]), j & 1, abort_flag, status, kernel_id * 16 + 4)) {
           ok = false;
           break;
         }
-        for (int t = 0; t < ntiles && ok; ++t) {
-          if (!mbar_wait(smem_u32(&p_ready[t]), j & 1, abort_flag, status, kernel_id * 16 + 5)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_pv(t, s, j > 0);
-        }
-        if (!ok) break;
-        umma_commit(smem_u32(&kv_empty[s]));  // K_j and V_j are free once every MMA so far is done
+        tc_fence_after();
+        issue_s(s1);
       }
-      if (!ok && issued_any) {
-        umma_commit(smem_u32(drain));
-        volatile int no_abort = 0;
-        mbar_wait(smem_u32(drain), 0, &no_abort, status, kernel_id * 16 + 6, 200000000ull);
+      if (!mbar_wait_warp(smem_u32(&v_full[s]), (j / STAGES) & 1, abort_flag, status, kernel_id * 16 + 3) ||
+          !mbar_wait_warp(smem_u32(&p_ready[t]), j & 1, abort_flag, status, kernel_id * 16 + 5)) {
+        ok = false;
+        break;
       }
+      tc_fence_after();
+      issue_pv(s, j > 0);
+      umma_commit_elect(smem_u32(&kv_empty[s]));  // this tile is done with K_j and V_j
+    }
+    if (!ok && issued_any) {
+      umma_commit_elect(smem_u32(&drain[t]));
+      volatile int no_abort = 0;
+      mbar_wait_warp(smem_u32(&drain[t]), 0, &no_abort, status, kernel_id * 16 + 6, 200000000ull);
     }
   } else if (warp >= 4) {
     // ---------------- softmax warps ----------------
-    const int t = (warp - 4) >> 2;  // query tile
-    const int q = warp & 3;         // TMEM lane quadrant this warp may access
-    const int r = q * 32 + lane;    // row of the tile = TMEM lane
+    const int t = (warp - 4) >> 3;         // query tile
+    const int h = ((warp - 4) >> 2) & 1;   // half of the 128 key columns
+    const int q = warp & 3;                // TMEM lane quadrant this warp may access
+    const int r = q * 32 + lane;           // row of the tile = TMEM lane
+    const uint32_t pair_bar = smem_u32(&xbar[t * 4 + q]);  // shared by warps w and w+4
     if (t < ntiles) {
       const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-      const uint32_t tS = tmem_base + lane_off + t * BN;
-      const uint32_t tO = tmem_base + lane_off + 2 * BN + t * DV;
-      uint8_t* prow = sP + t * P_BYTES + r * 128;
-      const int sw = r & 7;
+      const uint32_t tS = tmem_base + lane_off + t * BN + h * 64;
+      const uint32_t tO = tmem_base + lane_off + 2 * BN + t * DV + h * 32;
+      const uint32_t tP = tmem_base + lane_off + P_COL + t * (BN / 2) + h * 32;
+      float* my_max = xmax + (t * 2 + h) * BM + r;         // + parity * 4 * BM
+      const float* other_max = xmax + (t * 2 + (h ^ 1)) * BM + r;
       float m = 0.0f, l = 0.0f;
       bool ok = true;
-      for (int j = 0; j < NB; ++j) {
+      if (Cfg::DESYNC && t == 1) {
+        // start tile 1 one key block behind tile 0
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&p_ready[0]), 0, abort_flag, status, kernel_id * 16 + 11));
+      }
+      for (int j = 0; j < NB && ok; ++j) {
         ok = mbar_wait(smem_u32(&s_full[t]), j & 1, abort_flag, status, kernel_id * 16 + 7);
         if (!__all_sync(0xffffffffu, ok)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint32_t sr[128];
-        tmem_ld128(tS, sr);
+        uint32_t sr[64];
+        tmem_ld64(tS, sr);
         tc_fence_before();
         mbar_arrive(smem_u32(&s_free[t]));  // the tensor core may overwrite S_t now
-        float x[128];
+        float x[64];
 #pragma unroll
-        for (int i = 0; i < 128; ++i) x[i] = __uint_as_float(sr[i]);
+        for (int i = 0; i < 64; ++i) x[i] = __uint_as_float(sr[i]);
         if (j == NB - 1 && LAST_VALID < BN) {
 #pragma unroll
-          for (int i = 0; i < 128; ++i)
-            if (i >= LAST_VALID) x[i] = -INFINITY;
+          for (int i = 0; i < 64; ++i)
+            if (h * 64 + i >= LAST_VALID) x[i] = -INFINITY;
         }
+        // half-row max: four independent chains of 3-input maxima
         float mx0 = x[0], mx1 = x[1], mx2 = x[2], mx3 = x[3];
 #pragma unroll
-        for (int i = 4; i < 128; i += 4) {
-          mx0 = fmaxf(mx0, x[i]);
-          mx1 = fmaxf(mx1, x[i + 1]);
-          mx2 = fmaxf(mx2, x[i + 2]);
-          mx3 = fmaxf(mx3, x[i + 3]);
+        for (int i = 4; i < 60; i += 8) {
+          mx0 = fmax3(mx0, x[i], x[i + 4]);
+          mx1 = fmax3(mx1, x[i + 1], x[i + 5]);
+          mx2 = fmax3(mx2, x[i + 2], x[i + 6]);
+          mx3 = fmax3(mx3, x[i + 3], x[i + 7]);
         }
-        const float mblk = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * Cfg::C;
+        mx0 = fmax3(mx0, x[60], x[61]);
+        mx1 = fmax3(mx1, x[62], x[63]);
+        const float hmax = fmax3(mx0, mx1, fmaxf(mx2, mx3));
+        // row max = max of the two halves (shared memory, double-buffered by block parity;
+        // the arrive releases the store, the completed phase acquires the partner's)
+        my_max[(j & 1) * 4 * BM] = hmax;
+        mbar_arrive(pair_bar);
+        ok = mbar_wait(pair_bar, j & 1, abort_flag, status, kernel_id * 16 + 12);
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+        const float mblk = fmaxf(hmax, other_max[(j & 1) * 4 * BM]) * Cfg::C;
         float alpha = 1.0f;
         bool rescale = false;
         if (j == 0) {
@@ -338,19 +440,10 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
           m = mblk;
           rescale = true;
         }
-        // p = 2^(x*c - m), packed to the element type; the row sum uses the packed values
-        uint32_t pk[64];
         float l0 = 0.f, l1 = 0.f;
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const float p0 = ex2_approx(fmaf(x[2 * i], Cfg::C, -m));
-          const float p1 = ex2_approx(fmaf(x[2 * i + 1], Cfg::C, -m));
-          l0 += p0;
-          l1 += p1;
-          pk[i] = pack2<T>(p0, p1);
-        }
-        l += l0 + l1;
-        // P_t and O_t are the previous P V MMA's operands: wait until it has finished
+        uint32_t pk[16];
+        exp_pairs<0, T, Cfg::EMU>(x, Cfg::C, m, pk, l0, l1);
+        // P_t and O_t are operands of the previous P V MMA: wait until it has finished
         if (j > 0) {
           ok = mbar_wait(smem_u32(&o_done[t]), (j - 1) & 1, abort_flag, status, kernel_id * 16 + 8);
           if (!__all_sync(0xffffffffu, ok)) {
@@ -358,48 +451,45 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
             break;
           }
           tc_fence_after();
-          if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-            for (int h = 0; h < DV / 32; ++h) {
-              float o[32];
-              tmem_ld32(tO + h * 32, o);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] *= alpha;
-              tmem_st32_wait(tO + h * 32, o);
-            }
-          }
         }
+        tmem_st16_wait(tP, pk);
+        exp_pairs<16, T, Cfg::EMU>(x, Cfg::C, m, pk, l0, l1);
+        tmem_st16_wait(tP + 16, pk);
+        l += l0 + l1;
+        if (__any_sync(0xffffffffu, rescale)) {
+          // O_t *= alpha on the rows whose running max moved (this thread's 32 columns)
+          float o[32];
+          tmem_ld32(tO, o);
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          // keys 8u..8u+7: chunk u/8 (64 keys), 16-byte unit (u%8) ^ (row%8) of the row
-          uint8_t* dst = prow + (u >> 3) * (BM * 128) + (((u & 7) ^ sw) << 4);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32_wait(tO, o);
         }
-        fence_proxy_async_smem();  // generic-proxy P writes -> visible to the tensor core
         tc_fence_before();
         mbar_arrive(smem_u32(&p_ready[t]));
       }
       if (ok) {
-        ok = mbar_wait(smem_u32(&o_done[t]), (NB - 1) & 1, abort_flag, status, kernel_id * 16 + 9);
+        // row sum = the two halves' sums (same m)
+        xsum[(t * 2 + h) * BM + r] = l;
+        mbar_arrive(pair_bar);
+        ok = mbar_wait(pair_bar, NB & 1, abort_flag, status, kernel_id * 16 + 12) &&
+             mbar_wait(smem_u32(&o_done[t]), (NB - 1) & 1, abort_flag, status, kernel_id * 16 + 9);
         if (__all_sync(0xffffffffu, ok)) {
+          l += xsum[(t * 2 + (h ^ 1)) * BM + r];
           tc_fence_after();
           const int row = q0 + t * BM + r;
           const float inv = 1.0f / l;
-          T* orow = out + Cfg::out_offset(bh, row);
+          float o[32];
+          tmem_ld32(tO, o);
+          if (row < Cfg::SQ) {
+            T* orow = out + Cfg::out_offset(bh, row) + h * 32;
 #pragma unroll
-          for (int h = 0; h < DV / 32; ++h) {
-            float o[32];
-            tmem_ld32(tO + h * 32, o);
-            if (row < Cfg::SQ) {
-#pragma unroll
-              for (int v = 0; v < 4; ++v) {
-                uint4 w;
-                w.x = pack2<T>(o[8 * v + 0] * inv, o[8 * v + 1] * inv);
-                w.y = pack2<T>(o[8 * v + 2] * inv, o[8 * v + 3] * inv);
-                w.z = pack2<T>(o[8 * v + 4] * inv, o[8 * v + 5] * inv);
-                w.w = pack2<T>(o[8 * v + 6] * inv, o[8 * v + 7] * inv);
-                *reinterpret_cast<uint4*>(orow + h * 32 + 8 * v) = w;
-              }
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack2<T>(o[8 * v + 0] * inv, o[8 * v + 1] * inv);
+              w.y = pack2<T>(o[8 * v + 2] * inv, o[8 * v + 3] * inv);
+              w.z = pack2<T>(o[8 * v + 4] * inv, o[8 * v + 5] * inv);
+              w.w = pack2<T>(o[8 * v + 6] * inv, o[8 * v + 7] * inv);
+              *reinterpret_cast<uint4*>(orow + 8 * v) = w;
             }
           }
         }

@@ -8,7 +8,8 @@
 // Roles (192 threads, one CTA per SM, tiles handed out round-robin):
 //   warp 0      TMA producer: A tile [128 x 64] and B tile [BN x 64] per stage into
 //               128B-swizzled shared memory, completion tracked by mbarrier tx bytes.
-//   warp 1      TMEM allocator + MMA issuer: one elected lane issues
+//   warp 1      TMEM allocator + MMA issuer: the warp runs the loop converged and one lane
+//               picked by elect.sync issues
 //               tcgen05.mma.cta_group::1.kind::f16 (128 x BN x 16) four times per stage
 //               into a TMEM accumulator; tcgen05.commit frees the smem stage, and
 //               a final commit per tile signals the epilogue.
@@ -75,6 +76,12 @@ TJ_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, i
   }
 }
 
+// bounded wait by a whole warp; false (for every lane) unless every lane saw the phase
+TJ_DEV bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status, int where,
+                           uint64_t budget_ns = TJ_WAIT_NS) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, status, where, budget_ns));
+}
+
 TJ_DEV void tma_prefetch(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
@@ -138,6 +145,30 @@ TJ_DEV void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t 
 constexpr uint32_t idesc_tf32(int M, int N) {
   return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
          (static_cast<uint32_t>(M >> 4) << 24);
+}
+// Warp-converged forms: every lane of the issuing warp executes them with the same
+// (warp-uniform) operands and one lane chosen by elect.sync issues the instruction, so the
+// descriptors stay in uniform registers (issuing from a lane-0-only branch instead costs
+// per-thread -> uniform register moves on every MMA).
+TJ_DEV void umma_f16_elect(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n elect.sync _|e, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+TJ_DEV void umma_tf32_elect(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n elect.sync _|e, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n"
+      " @e tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+TJ_DEV void umma_commit_elect(uint32_t bar) {
+  asm volatile(
+      "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(bar)
+      : "memory");
 }
 TJ_DEV void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
@@ -342,62 +373,57 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      int stage = 0;
-      uint32_t phase = 0;
-      int it = 0;
-      bool ok = true;
-      bool issued_any = false;
-      for (long t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
-        const int buf = it & 1;
-        if (!mbar_wait(smem_u32(&tempty[buf]), ((it >> 1) & 1) ^ 1u, abort_flag, status, kernel_id * 16 + 2)) {
+    // ---------------- MMA issuer: the warp runs the loop converged, elect.sync issues ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int it = 0;
+    bool ok = true;
+    bool issued_any = false;
+    // smem descriptors of stage 0; a stage / k step adds (byte offset >> 4) to the start address
+    const uint64_t da0 = desc_sw128(smem_u32(sA), 16, 1024);
+    const uint64_t db0 = Cfg::B_MN_MAJOR ? desc_sw128(smem_u32(sB), BK * 128, 1024) : desc_sw128(smem_u32(sB), 16, 1024);
+    for (long t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+      const int buf = it & 1;
+      if (!mbar_wait_warp(smem_u32(&tempty[buf]), ((it >> 1) & 1) ^ 1u, abort_flag, status, kernel_id * 16 + 2)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN);
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!mbar_wait_warp(smem_u32(&full[stage]), phase, abort_flag, status, kernel_id * 16 + 3)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN);
-        for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, status, kernel_id * 16 + 3)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + stage * OPC * A_BYTES);
-          const uint32_t b0 = smem_u32(sB + stage * OPC * B_BYTES);
+        const uint64_t a0 = da0 + ((stage * OPC * A_BYTES) >> 4);
+        const uint64_t b0 = db0 + ((stage * OPC * B_BYTES) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < BK / UK; ++kk) {
-            const uint64_t ad = desc_sw128(a0 + kk * 32, 16, 1024);
-            uint64_t bd;
-            if constexpr (!Cfg::B_MN_MAJOR)
-              bd = desc_sw128(b0 + kk * 32, 16, 1024);
-            else
-              bd = desc_sw128(b0 + kk * UK * 128, BK * 128, 1024);
-            if constexpr (!X3) {
-              umma_f16(d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
-            } else {
-              const uint64_t ad_lo = desc_sw128(a0 + A_BYTES + kk * 32, 16, 1024);
-              const uint64_t bd_lo = desc_sw128(b0 + B_BYTES + kk * 32, 16, 1024);
-              umma_tf32(d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
-              umma_tf32(d, ad, bd_lo, IDESC, 1u);
-              umma_tf32(d, ad_lo, bd, IDESC, 1u);
-            }
-          }
-          umma_commit(smem_u32(&empty[stage]));
-          issued_any = true;
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
+        for (int kk = 0; kk < BK / UK; ++kk) {
+          const uint64_t ad = a0 + 2 * kk;  // 32 bytes of K per step
+          const uint64_t bd = Cfg::B_MN_MAJOR ? b0 + ((kk * UK * 128) >> 4) : b0 + 2 * kk;
+          if constexpr (!X3) {
+            umma_f16_elect(d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+          } else {
+            umma_tf32_elect(d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+            umma_tf32_elect(d, ad, bd + (B_BYTES >> 4), IDESC, 1u);
+            umma_tf32_elect(d, ad + (A_BYTES >> 4), bd, IDESC, 1u);
           }
         }
-        if (ok) umma_commit(smem_u32(&tfull[buf]));
+        umma_commit_elect(smem_u32(&empty[stage]));
+        issued_any = true;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
       }
-      if (!ok && issued_any) {
-        // abort: wait for the MMAs already issued before TMEM / smem go away
-        umma_commit(smem_u32(drain));
-        volatile int no_abort = 0;
-        mbar_wait(smem_u32(drain), 0, &no_abort, status, kernel_id * 16 + 6, 200000000ull);
-      }
+      if (ok) umma_commit_elect(smem_u32(&tfull[buf]));
+    }
+    if (!ok && issued_any) {
+      // abort: wait for the MMAs already issued before TMEM / smem go away
+      umma_commit_elect(smem_u32(drain));
+      volatile int no_abort = 0;
+      mbar_wait_warp(smem_u32(drain), 0, &no_abort, status, kernel_id * 16 + 6, 200000000ull);
     }
   } else {
     // ---------------- epilogue warps ----------------

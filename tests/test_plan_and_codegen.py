@@ -4,6 +4,8 @@ launch geometry, and the tensorjit registration hook."""
 import json
 import math
 
+import numpy as np
+
 import pytest
 
 from mlir_gpu_kernel_compiler_b200.codegen import generate
@@ -231,7 +233,7 @@ def test_attention_not_fused_for_other_row_kernels():
 def test_attention_tensor_maps_and_launch_geometry():
     _, f = _fused("cfg4")
     ks = [k for k in generate(f) if k.family == "attention"][0]
-    assert ks.grid == (128 * 8, 1, 1) and ks.block == (384, 1, 1)
+    assert ks.grid == (128 * 8, 1, 1) and ks.block == (640, 1, 1)
     assert ks.smem <= 232448 and len(ks.tmaps) == 3
     for t in ks.tmaps:
         # head dim innermost, then heads, sequence, batch -- strides increasing, 16-byte multiples
@@ -252,3 +254,27 @@ def test_fused_attention_compiles_for_sm100a(name):
     assert any(k.family == "attention" for k in ks)
     imgs = compile_cubins([(k.symbol, k.source) for k in ks])
     assert all(img[:4] == b"\x7fELF" for img in imgs)
+
+
+def _ex2_poly_f32(x):
+    """numpy float32 restatement of ex2_poly (csrc/kernels/attention_sm100.cuh)."""
+    x = np.maximum(np.asarray(x, np.float32), np.float32(-126.0))
+    magic = np.float32(12582912.0)
+    t = (x + magic).astype(np.float32)
+    f = (x - (t - magic)).astype(np.float32)
+    c3, c2, c1, c0 = (np.float32(v) for v in (0.05522261559963226, 0.24261537194252014, 0.6932516098022461,
+                                              0.9999275803565979))
+    p = ((c3 * f + c2) * f + c1) * f + c0
+    bits = p.view(np.int32) + (t.view(np.int32) << np.int32(23))
+    return bits.view(np.float32)
+
+
+def test_polynomial_exp2_is_below_half_an_ulp_of_bf16_and_f16():
+    x = np.concatenate([np.linspace(-30.0, 8.0, 400001), -np.logspace(-6, 1.5, 2000)]).astype(np.float32)
+    y = _ex2_poly_f32(x).astype(np.float64)
+    ref = np.exp2(x.astype(np.float64))
+    rel = np.abs(y / ref - 1.0)
+    assert rel.max() < 1e-4          # bf16 half-ulp 2^-9, f16 half-ulp 2^-12 = 2.4e-4
+    # masked keys (-inf) and far-below-range arguments vanish after rounding to half precision
+    tiny = _ex2_poly_f32(np.array([-np.inf, -200.0, -127.0], np.float32))
+    assert np.all(tiny < 2.0 ** -125) and np.all(tiny >= 0)
