@@ -209,9 +209,12 @@ def run_b200(a) -> None:
     torch.cuda.set_device(dev)
     w = W.WORKLOADS[a.config]
     sharded = a.config == "cfg5"
-    plan_name = W.sharded_plan_name(w, world) if sharded else w.plan
+    total_rows = a.rows or w.rows
+    if a.rows and (not sharded or w.rows % a.rows or a.rows % world):
+        raise SystemExit("--rows: cfg5 only, a divisor of its 131072 rows and a multiple of the GPU count")
+    plan_name = W.sharded_plan_name(w, world, total_rows) if sharded else w.plan
     plan = PProgram.load(ROOT / "tests" / "golden" / "plans" / f"{plan_name}.json")
-    rows = W.shard_rows(w.rows, world, rank) if sharded else None
+    rows = W.shard_rows(total_rows, world, rank) if sharded else None
     _trace("inputs")
     ins = W.make_inputs(w, device=dev, rows=rows)
     _trace("compile")
@@ -322,7 +325,7 @@ def run_b200(a) -> None:
             "vs_baseline": None, "dtype": "bf16" if w.dtype == torch.bfloat16 else "f32",
             "data": "synthetic: seeded CPU-generator inputs with the BASELINE shapes and distributions",
             "config": {"workload": f"{a.config}: {w.description}", "plan": plan_name, "rows_per_rank": (
-                rows[1] - rows[0]) if rows else None, "global_rows": w.rows if sharded else None,
+                rows[1] - rows[0]) if rows else None, "global_rows": total_rows if sharded else None,
                 "parallelism": f"rows{world}" if sharded else f"replicas{world}",
                 "l2": "inputs larger than L2 (no flush needed)", "graph": True},
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
@@ -335,7 +338,16 @@ def run_b200(a) -> None:
 
 
 # dram read+write bytes per launch of the dominant kernel, from the committed ncu summaries
-TRAFFIC: dict = {}
+# (profiles/*.md); cfg5's full-size launch is too large to capture, so its figure is the
+# 16384-row slice's (profiles/gemm_traffic_cfg5_cfg1.md) scaled by the 8x rows it processes
+# (x, h and the per-row-group weight re-reads all grow in proportion to the rows)
+TRAFFIC: dict = {
+    ("cfg1", "tj_matmul_2"): 33.06e6,
+    ("cfg2", "tj_row_0"): 365.4e6,
+    ("cfg3", "tj_matmul_0"): 1132.0e6,
+    ("cfg4", "tj_attention_4"): 116.7e6,
+    ("cfg5", "tj_matmul_1"): 8 * 1727.9e6,
+}
 
 
 def main():
@@ -347,6 +359,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=None,
+                    help="cfg5 only: run a leading slice of this many rows (for small profiling captures)")
     a = ap.parse_args()
     if a.warmup < 3 and a.impl == "b200":
         a.warmup = 3

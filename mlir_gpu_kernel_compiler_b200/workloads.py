@@ -117,11 +117,12 @@ def make_inputs(w: Workload, device="cpu", rows: tuple[int, int] | None = None) 
     return out
 
 
-def sharded_plan_name(w: Workload, world: int) -> str:
-    """Plan fixture for one rank's row shard of ``w`` (same program, M = rows / world)."""
+def sharded_plan_name(w: Workload, world: int, total: int | None = None) -> str:
+    """Plan fixture for one rank's row shard of ``w`` (same program, M = rows / world);
+    ``total`` runs a leading row slice of that many rows instead of all of them."""
     if w.name != "cfg5":
         return w.plan
-    return f"cfg5_m{w.rows // world}"
+    return f"cfg5_m{(total or w.rows) // world}"
 
 
 def shard_rows(total: int, world: int, rank: int) -> tuple[int, int]:
