@@ -101,6 +101,21 @@ TJ_DEV void umma_commit_pair(uint32_t bar) {
           bar)
       : "memory");
 }
+// warp-converged forms (all lanes execute, one lane chosen by elect.sync issues)
+TJ_DEV void umma_f16_pair_elect(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n elect.sync _|e, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n"
+      " @e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+TJ_DEV void umma_commit_pair_elect(uint32_t bar) {
+  asm volatile(
+      "{\n .reg .b16 m;\n .reg .pred e;\n mov.b16 m, 3;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n}\n" ::"r"(
+          bar)
+      : "memory");
+}
 TJ_DEV void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
                : "memory");
@@ -213,47 +228,50 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {
-      // ---------------- MMA issuer (leader CTA) ----------------
+    if (rank == 0) {
+      // ---------------- MMA issuer (leader CTA; the warp runs the loop converged) ----------------
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
       bool issued_any = false;
+      const uint64_t da0 = desc_sw128(smem_u32(sA), 16, 1024);
+      const uint64_t db0 = desc_sw128(smem_u32(sB), 16, 1024);
+      auto wait_all = [&](uint32_t bar, uint32_t parity, int where) {
+        return __all_sync(0xffffffffu, mbar_wait_pair(bar, parity, abort_flag, peer_abort, status, where));
+      };
       for (long t = cluster_id; t < num_tiles && ok; t += num_clusters, ++it) {
         const int buf = it & 1;
-        if (!mbar_wait_pair(smem_u32(&tempty[buf]), ((it >> 1) & 1) ^ 1u, abort_flag, peer_abort, status,
-                            kernel_id * 16 + 2)) {
+        if (!wait_all(smem_u32(&tempty[buf]), ((it >> 1) & 1) ^ 1u, kernel_id * 16 + 2)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN);
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait_pair(smem_u32(&full[stage]), phase, abort_flag, peer_abort, status, kernel_id * 16 + 3)) {
+          if (!wait_all(smem_u32(&full[stage]), phase, kernel_id * 16 + 3)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+          const uint64_t a0 = da0 + ((stage * A_BYTES) >> 4);
+          const uint64_t b0 = db0 + ((stage * B_BYTES) >> 4);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            umma_f16_pair(d, desc_sw128(a0 + kk * 32, 16, 1024), desc_sw128(b0 + kk * 32, 16, 1024), IDESC,
-                          (kb | kk) != 0 ? 1u : 0u);
-          umma_commit_pair(smem_u32(&empty[stage]));
+            umma_f16_pair_elect(d, a0 + 2 * kk, b0 + 2 * kk, IDESC, (kb | kk) != 0 ? 1u : 0u);
+          umma_commit_pair_elect(smem_u32(&empty[stage]));
           issued_any = true;
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        if (ok) umma_commit_pair(smem_u32(&tfull[buf]));
+        if (ok) umma_commit_pair_elect(smem_u32(&tfull[buf]));
       }
       if (!ok && issued_any) {
-        umma_commit_pair(smem_u32(drain));
+        umma_commit_pair_elect(smem_u32(drain));
         volatile int no_abort = 0;
-        mbar_wait(smem_u32(drain), 0, &no_abort, status, kernel_id * 16 + 6, 200000000ull);
+        mbar_wait_warp(smem_u32(drain), 0, &no_abort, status, kernel_id * 16 + 6, 200000000ull);
       }
     }
   } else {
