@@ -70,6 +70,18 @@ def register(make_default: bool = True) -> None:
 
     C.compile_graph = compile_graph
     C.pick_backend = pick_backend
+    # modules that imported the two functions by name keep their own bindings: the package
+    # re-exports (tensorjit/__init__.py:17) and the torch.compile backend
+    # (tensorjit/frontend/torch_backend.py:22), which calls them in torch_compile_backend
+    import sys
+
+    for mod in ("tensorjit", "tensorjit.frontend.torch_backend"):
+        m = sys.modules.get(mod)
+        if m is not None:
+            if getattr(m, "compile_graph", None) is orig_compile_graph:
+                m.compile_graph = compile_graph
+            if getattr(m, "pick_backend", None) is orig_pick:
+                m.pick_backend = pick_backend
     C._b200_registered = True
 
 

@@ -34,6 +34,64 @@ def test_register_adds_backend_and_keeps_the_plan():
     assert live.to_dict()["kernels"] == fixture.to_dict()["kernels"]
 
 
+def test_register_reaches_the_torch_compile_backend():
+    """torch_backend.py:22 imports compile_graph / pick_backend by name; register() rebinds
+    those names too, so torch.compile(..., backend=tj.torch_compile_backend) picks b200."""
+    import tensorjit.frontend.torch_backend as TB
+
+    tjb.register()
+    assert TB.pick_backend("cuda") == "b200" and TB.pick_backend("cpu") == "c"
+    assert TB.compile_graph is tj.compile_graph
+    import tensorjit.compiler as C
+
+    assert TB.compile_graph is C.compile_graph and tj.pick_backend is C.pick_backend
+
+
+@pytest.mark.gpu
+def test_torch_compile_on_cuda_runs_b200(monkeypatch):
+    """tests/test_mlir_and_torch.py:71-80 of the reference, on CUDA tensors: the FX graph
+    goes through torch_compile_backend -> pick_backend -> compile_graph -> b200."""
+    import torch.nn.functional as F
+
+    monkeypatch.setenv("TENSORJIT_STRICT", "1")
+    tjb.register()
+    torch._dynamo.reset()
+
+    class Block(torch.nn.Module):
+        def __init__(self, d=32, h=64):
+            super().__init__()
+            self.ln = torch.nn.LayerNorm(d)
+            self.fc1 = torch.nn.Linear(d, h)
+            self.fc2 = torch.nn.Linear(h, d)
+
+        def forward(self, x):
+            h = F.gelu(self.fc1(self.ln(x)))
+            y = x + self.fc2(h)
+            return torch.softmax(y, dim=-1) * 2 + y.mean(dim=-1, keepdim=True)
+
+    torch.manual_seed(0)
+    m = Block().cuda().eval()
+    x = torch.randn(16, 32, device="cuda")
+    seen = []
+    orig = tjb.compile_program
+
+    def spy(program, **kw):
+        cp = orig(program, **kw)
+        seen.append(cp)
+        return cp
+
+    monkeypatch.setattr(tjb, "compile_program", spy)
+    import mlir_gpu_kernel_compiler_b200 as pkg
+
+    monkeypatch.setattr(pkg, "compile_program", spy)
+    c = torch.compile(m, backend=tj.torch_compile_backend)
+    with torch.no_grad():
+        y = c(x)
+        ref = m(x)
+    assert seen and all(isinstance(cp, tjb.B200Program) for cp in seen)
+    torch.testing.assert_close(y, ref, atol=1e-4, rtol=1e-4)
+
+
 @pytest.mark.gpu
 def test_jit_on_cuda_tensors_runs_b200():
     tjb.register()
