@@ -71,31 +71,51 @@ def x3_eligible(k: PKernel) -> bool:
     return a.dtype == b.dtype == "f32" and tb and K >= 4 and K % 4 == 0 and M > 0 and N > 0
 
 
-def gen_split_tf32(symbol: str, numel: int, src: tuple, hi_off: int, lo_off: int) -> KernelSource:
+def gen_split_tf32(symbol: str, segments: list[tuple]) -> KernelSource:
     """x -> (hi, lo) with hi = x with its 13 low mantissa bits cleared (exactly a TF32 value)
     and lo = x - hi (exact in f32): the operand split of 3xTF32 (hi*hi + hi*lo + lo*hi keeps
-    ~21 mantissa bits of every product)."""
-    n4 = numel // 4
-    L = [HEADER, params_struct(3, 0),
+    ~21 mantissa bits of every product).  ``segments`` = [(numel, src, hi_off, lo_off), ...]:
+    the operands of one GEMM are split by one grid-stride launch."""
+    bounds, acc = [], 0
+    for numel, _src, _hi, _lo in segments:
+        acc += numel // 4
+        bounds.append(acc)
+    nseg = len(segments)
+    L = [HEADER, params_struct(3 * nseg, 0),
          f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{',
-         "  const float4* __restrict__ x = (const float4*)prm.p[0];",
-         "  float4* __restrict__ hi = (float4*)prm.p[1];",
-         "  float4* __restrict__ lo = (float4*)prm.p[2];",
-         f"  for (long i = (long)blockIdx.x * 256 + threadIdx.x; i < {n4}L; i += (long)gridDim.x * 256) {{",
-         "    const float4 v = __ldg(x + i);",
-         "    float4 h;",
-         "    h.x = __uint_as_float(__float_as_uint(v.x) & 0xffffe000u);",
-         "    h.y = __uint_as_float(__float_as_uint(v.y) & 0xffffe000u);",
-         "    h.z = __uint_as_float(__float_as_uint(v.z) & 0xffffe000u);",
-         "    h.w = __uint_as_float(__float_as_uint(v.w) & 0xffffe000u);",
-         "    hi[i] = h;",
-         "    lo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);",
-         "  }",
-         "}"]
-    grid = max(1, min((n4 + 255) // 256, NUM_SMS * 8))
-    ks = KernelSource(symbol, "split", "\n".join(L), (grid, 1, 1), (256, 1, 1),
-                      [src, ("scratch", hi_off), ("scratch", lo_off)],
-                      info={"bytes": numel * 12, "numel": numel})
+         f"  for (long g = (long)blockIdx.x * 256 + threadIdx.x; g < {acc}L; g += (long)gridDim.x * 256) {{",
+         "    int s = 0;",
+         "    long i = g;"]
+    for j in range(nseg - 1):
+        n = bounds[j] - (bounds[j - 1] if j else 0)
+        L.append(f"    if (s == {j} && i >= {n}L) {{ i -= {n}L; s = {j + 1}; }}")
+
+    def pick(slot: int) -> str:   # select the segment's pointer without indexing the params at run time
+        e = f"prm.p[{3 * (nseg - 1) + slot}]"
+        for j in range(nseg - 2, -1, -1):
+            e = f"(s == {j} ? prm.p[{3 * j + slot}] : {e})"
+        return e
+
+    L += [f"    const float4* __restrict__ x = (const float4*){pick(0)};",
+          f"    float4* __restrict__ hi = (float4*){pick(1)};",
+          f"    float4* __restrict__ lo = (float4*){pick(2)};",
+          "    const float4 v = __ldg(x + i);",
+          "    float4 h;",
+          "    h.x = __uint_as_float(__float_as_uint(v.x) & 0xffffe000u);",
+          "    h.y = __uint_as_float(__float_as_uint(v.y) & 0xffffe000u);",
+          "    h.z = __uint_as_float(__float_as_uint(v.z) & 0xffffe000u);",
+          "    h.w = __uint_as_float(__float_as_uint(v.w) & 0xffffe000u);",
+          "    hi[i] = h;",
+          "    lo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);",
+          "  }",
+          "}"]
+    grid = max(1, min((acc + 255) // 256, NUM_SMS * 8))
+    args = []
+    for _numel, src, hi_off, lo_off in segments:
+        args += [src, ("scratch", hi_off), ("scratch", lo_off)]
+    total = sum(sg[0] for sg in segments)
+    ks = KernelSource(symbol, "split", "\n".join(L), (grid, 1, 1), (256, 1, 1), args,
+                      info={"bytes": total * 12, "numel": total})
     ks.finalize_params()
     return ks
 
@@ -105,19 +125,18 @@ def _align(x: int, a: int = 256) -> int:
 
 
 def gen_matmul_tc_x3(k: PKernel, symbol: str, kernel_id: int, tile: dict | None) -> list[KernelSource]:
-    """f32 matmul as [split(A), split(B), 3xTF32 tcgen05 GEMM]; the hi/lo copies live in
-    the program's workspace (arena space after the planned intermediates)."""
+    """f32 matmul as [split(A and B), 3xTF32 tcgen05 GEMM]; the hi/lo copies live in the
+    program's workspace (arena space after the planned intermediates)."""
     mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
     a_hi, a_lo = 0, _align(a.nbytes)
     b_hi = a_lo + _align(a.nbytes)
     b_lo = b_hi + _align(b.nbytes)
     ws = b_lo + _align(b.nbytes)
-    sa = gen_split_tf32(f"{symbol}_split_a", a.numel, ("node", a), a_hi, a_lo)
-    sb = gen_split_tf32(f"{symbol}_split_b", b.numel, ("node", b), b_hi, b_lo)
+    sp = gen_split_tf32(f"{symbol}_split", [(a.numel, ("node", a), a_hi, a_lo), (b.numel, ("node", b), b_hi, b_lo)])
     g = gen_gemm_tc(k, symbol, kernel_id, tile, x3_scratch=(a_hi, b_hi, a_lo, b_lo))
-    for ks in (sa, sb, g):
+    for ks in (sp, g):
         ks.info["scratch_bytes"] = ws
-    return [sa, sb, g]
+    return [sp, g]
 
 
 # ---------------------------------------------------------------------------

@@ -45,9 +45,9 @@ def test_launch_geometry_and_kernel_families():
     p = FX.load_plan("cuda_mlp__f32")
     assert [k.kind for k in p.kernels] == ["row", "matmul", "matmul"]
     ks = generate(p)
-    # f32 matmuls with a K-major B run as 3xTF32: two operand-split launches + the tcgen05 GEMM
-    assert [k.family for k in ks] == ["row", "split", "split", "gemm_tc", "split", "split", "gemm_tc"]
-    assert [k.info["index"] for k in ks] == [0, 1, 1, 1, 2, 2, 2]
+    # f32 matmuls with a K-major B run as 3xTF32: one launch splitting both operands + the tcgen05 GEMM
+    assert [k.family for k in ks] == ["row", "split", "gemm_tc", "split", "gemm_tc"]
+    assert [k.info["index"] for k in ks] == [0, 1, 1, 2, 2]
     assert all(k.info.get("tf32x3") for k in ks if k.family == "gemm_tc")
     # one row group per row, 256-thread CTAs
     assert ks[0].block[0] == 256 and ks[0].grid[0] * ks[0].info["rpc"] >= 64
