@@ -298,6 +298,11 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
         const int s = j % STAGES;
         const uint32_t ph = (j / STAGES) & 1;
         if (!mbar_wait(smem_u32(&kv_empty[s]), ph ^ 1u, abort_flag, status, kernel_id * 16 + 1)) break;
+#ifdef TJ_TEST_STALL_FIRST_LOAD
+        // Failure-path test build only: K_0 / V_0 are never loaded, so the MMA warps' bounded
+        // wait on them must run out and report through the status words.
+        if (j == 0) continue;
+#endif
         mbar_expect_tx(smem_u32(&k_full[s]), K_BYTES);
         Cfg::k_coords(bh, j * BN, c);
         tma_load_nd<Cfg::KR>(smem_u32(sK + s * K_BYTES), &prm.tm[1], smem_u32(&k_full[s]), c);

@@ -43,3 +43,27 @@ def test_bounded_wait_timeout_reports_status_and_context_survives():
     good.check()
     ref = evaluate(plan, [t.cpu() for t in ins], round_stored=True)[0]
     assert normwise_error(y, ref) <= 2e-2
+
+
+def test_attention_bounded_wait_timeout_reports_status_and_context_survives():
+    """The same for the fused attention kernel: its test build never loads the first K/V
+    block, so the MMA warps (and then every other role) must give up, report, drain and
+    return."""
+    from mlir_gpu_kernel_compiler_b200 import B200Program
+
+    case = "attention_core__bf16"
+    plan = FX.load_plan(case)
+    ins = [t.cuda() for t in FX.case_inputs(case)]
+    bad = B200Program(plan, use_graph=False, nvcc_flags=("-DTJ_TEST_STALL_FIRST_LOAD", "-DTJ_WAIT_NS=20000000ull"))
+    assert [ks.family for ks in bad.kernel_sources] == ["attention"]
+    outs = [torch.empty(s, dtype=d, device="cuda") for s, d in bad.output_specs()]
+    bad.run_into(ins, outs)
+    torch.cuda.synchronize()
+    code, where = bad.native.check_status()
+    assert code == 1 and where // 16 == 0  # TJ_STATUS_WAIT_TIMEOUT in plan kernel 0
+    bad.close()
+    good = B200Program(plan)
+    y = good(*ins)[0]
+    good.check()
+    ref = evaluate(plan, [t.cpu() for t in ins])[0]
+    assert normwise_error(y, ref) <= 2e-2
