@@ -23,9 +23,10 @@ from .common import CTYPE, ITEM, HEADER, KernelSource, TMapSpec, decompose_stmts
 LOG2E = 1.4426950408889634
 # Softmax tuning: EMU of every 16 exponential pairs on the FMA pipe (polynomial) instead of
 # MUFU; DESYNC staggers the two query tiles by one key block; STAGES is the depth of the
-# K/V ring.
+# K/V ring; SPEC starts a block's exponentials with the current row max (speculation, redone
+# when the max moved past the rescale threshold).
 # ``TENSORJIT_B200_ATTN="EMU=4,DESYNC=1"`` overrides.
-ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3}
+ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3, "SPEC": 0}
 
 
 def attention_knobs() -> dict:
@@ -88,6 +89,7 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     L.append(f"  static constexpr bool BF16 = {'true' if dt == 'bf16' else 'false'};")
     L.append(f"  static constexpr int EMU = {kn['EMU']};")
     L.append(f"  static constexpr bool DESYNC = {'true' if kn['DESYNC'] else 'false'};")
+    L.append(f"  static constexpr bool SPEC = {'true' if kn['SPEC'] else 'false'};")
     c = float(a["scale"]) * LOG2E
     L.append(f"  static constexpr float C = {c!r}f;")
     tmaps = []

@@ -183,6 +183,27 @@ TJ_DEV void exp_pairs(const float (&x)[64], float c, float m, uint32_t (&pk)[16]
   }
 }
 
+// exp_pairs that also tracks the maximum of the 32 scores it reads (two chains, h0 / h1)
+template <int I0, class T, int EMU>
+TJ_DEV void exp_pairs_max(const float (&x)[64], float c, float m, uint32_t (&pk)[16], float& l0, float& l1,
+                          float& h0, float& h1) {
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int i = I0 + k;
+    if (k & 1)
+      h1 = fmax3(h1, x[2 * i], x[2 * i + 1]);
+    else
+      h0 = fmax3(h0, x[2 * i], x[2 * i + 1]);
+    const float a0 = fmaf(x[2 * i], c, -m), a1 = fmaf(x[2 * i + 1], c, -m);
+    const bool emu = (i & 15) < EMU;
+    const float p0 = emu ? ex2_poly(a0) : ex2_approx(a0);
+    const float p1 = emu ? ex2_poly(a1) : ex2_approx(a1);
+    l0 += p0;
+    l1 += p1;
+    pk[k] = pack2<T>(p0, p1);
+  }
+}
+
 // 16 consecutive 32-bit columns of one lane quadrant from registers into TMEM, then wait.
 TJ_DEV void tmem_st16_wait(uint32_t taddr, const uint32_t (&v)[16]) {
   asm volatile(
@@ -198,6 +219,8 @@ TJ_DEV void tmem_st16_wait(uint32_t taddr, const uint32_t (&v)[16]) {
 //   static constexpr int SQ, SK, D, DV, STAGES, QR, KR, VR (tensor-map ranks);
 //   static constexpr int EMU (exponentials of every 16 column pairs computed by ex2_poly, 0..16);
 //   static constexpr bool DESYNC (tile 1 starts one key block behind tile 0);
+//   static constexpr bool SPEC (exponentials with the current row max while the block's max is
+//   exchanged; recomputed when it moved by more than the rescale threshold);
 //   static constexpr long BATCH;  static constexpr bool BF16;  static constexpr float C (scale * log2 e, > 0);
 //   using T = element type (__nv_bfloat16 / __half);
 //   static __device__ void q_coords(long bh, int s0, int (&c)[5]);   (and k_coords, v_coords)
@@ -413,53 +436,94 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
           for (int i = 0; i < 64; ++i)
             if (h * 64 + i >= LAST_VALID) x[i] = -INFINITY;
         }
-        // half-row max: four independent chains of 3-input maxima
-        float mx0 = x[0], mx1 = x[1], mx2 = x[2], mx3 = x[3];
-#pragma unroll
-        for (int i = 4; i < 60; i += 8) {
-          mx0 = fmax3(mx0, x[i], x[i + 4]);
-          mx1 = fmax3(mx1, x[i + 1], x[i + 5]);
-          mx2 = fmax3(mx2, x[i + 2], x[i + 6]);
-          mx3 = fmax3(mx3, x[i + 3], x[i + 7]);
-        }
-        mx0 = fmax3(mx0, x[60], x[61]);
-        mx1 = fmax3(mx1, x[62], x[63]);
-        const float hmax = fmax3(mx0, mx1, fmaxf(mx2, mx3));
-        // row max = max of the two halves (shared memory, double-buffered by block parity;
-        // the arrive releases the store, the completed phase acquires the partner's)
-        my_max[(j & 1) * 4 * BM] = hmax;
-        mbar_arrive(pair_bar);
-        ok = mbar_wait(pair_bar, j & 1, abort_flag, status, kernel_id * 16 + 12);
-        if (!__all_sync(0xffffffffu, ok)) {
-          ok = false;
-          break;
-        }
-        const float mblk = fmaxf(hmax, other_max[(j & 1) * 4 * BM]) * Cfg::C;
-        float alpha = 1.0f;
-        bool rescale = false;
-        if (j == 0) {
-          m = mblk;
-        } else if (mblk > m + RESCALE_THRESHOLD) {
-          alpha = ex2_approx(m - mblk);
-          l *= alpha;
-          m = mblk;
-          rescale = true;
-        }
         float l0 = 0.f, l1 = 0.f;
         uint32_t pk[16];
-        exp_pairs<0, T, Cfg::EMU>(x, Cfg::C, m, pk, l0, l1);
+        float alpha = 1.0f;
+        bool rescale = false;
+        // exchange of the half-row maxima (shared memory, double-buffered by block parity;
+        // the arrive releases the store, the completed phase acquires the partner's)
+        auto row_max = [&](float hmax, float& mblk) -> bool {
+          my_max[(j & 1) * 4 * BM] = hmax;
+          mbar_arrive(pair_bar);
+          const bool w = mbar_wait(pair_bar, j & 1, abort_flag, status, kernel_id * 16 + 12);
+          if (!__all_sync(0xffffffffu, w)) return false;
+          mblk = fmaxf(hmax, other_max[(j & 1) * 4 * BM]) * Cfg::C;
+          return true;
+        };
         // P_t and O_t are operands of the previous P V MMA: wait until it has finished
-        if (j > 0) {
-          ok = mbar_wait(smem_u32(&o_done[t]), (j - 1) & 1, abort_flag, status, kernel_id * 16 + 8);
-          if (!__all_sync(0xffffffffu, ok)) {
+        auto wait_prev_pv = [&]() -> bool {
+          if (j == 0) return true;
+          const bool w = mbar_wait(smem_u32(&o_done[t]), (j - 1) & 1, abort_flag, status, kernel_id * 16 + 8);
+          if (!__all_sync(0xffffffffu, w)) return false;
+          tc_fence_after();
+          return true;
+        };
+        if (!Cfg::SPEC || j == 0) {
+          // half-row max first: four independent chains of 3-input maxima
+          float mx0 = x[0], mx1 = x[1], mx2 = x[2], mx3 = x[3];
+#pragma unroll
+          for (int i = 4; i < 60; i += 8) {
+            mx0 = fmax3(mx0, x[i], x[i + 4]);
+            mx1 = fmax3(mx1, x[i + 1], x[i + 5]);
+            mx2 = fmax3(mx2, x[i + 2], x[i + 6]);
+            mx3 = fmax3(mx3, x[i + 3], x[i + 7]);
+          }
+          mx0 = fmax3(mx0, x[60], x[61]);
+          mx1 = fmax3(mx1, x[62], x[63]);
+          float mblk;
+          if (!row_max(fmax3(mx0, mx1, fmaxf(mx2, mx3)), mblk)) {
             ok = false;
             break;
           }
-          tc_fence_after();
+          if (j == 0) {
+            m = mblk;
+          } else if (mblk > m + RESCALE_THRESHOLD) {
+            alpha = ex2_approx(m - mblk);
+            l *= alpha;
+            m = mblk;
+            rescale = true;
+          }
+          exp_pairs<0, T, Cfg::EMU>(x, Cfg::C, m, pk, l0, l1);
+          if (!wait_prev_pv()) {
+            ok = false;
+            break;
+          }
+          tmem_st16_wait(tP, pk);
+          exp_pairs<16, T, Cfg::EMU>(x, Cfg::C, m, pk, l0, l1);
+          tmem_st16_wait(tP + 16, pk);
+        } else {
+          // speculative: the exponentials use the current m while the half-row max is
+          // tracked alongside; when the exchanged row max moved by more than the threshold
+          // (rare), the block is recomputed with the new m from the scores still in registers
+          float hm0 = -INFINITY, hm1 = -INFINITY;
+          exp_pairs_max<0, T, Cfg::EMU>(x, Cfg::C, m, pk, l0, l1, hm0, hm1);
+          if (!wait_prev_pv()) {
+            ok = false;
+            break;
+          }
+          tmem_st16_wait(tP, pk);
+          exp_pairs_max<16, T, Cfg::EMU>(x, Cfg::C, m, pk, l0, l1, hm0, hm1);
+          tmem_st16_wait(tP + 16, pk);
+          float mblk;
+          if (!row_max(fmaxf(hm0, hm1), mblk)) {
+            ok = false;
+            break;
+          }
+          if (mblk > m + RESCALE_THRESHOLD) {
+            alpha = ex2_approx(m - mblk);
+            l *= alpha;
+            m = mblk;
+            rescale = true;
+          }
+          if (__any_sync(0xffffffffu, rescale)) {
+            l0 = 0.f;
+            l1 = 0.f;
+            exp_pairs<0, T, Cfg::EMU>(x, Cfg::C, m, pk, l0, l1);
+            tmem_st16_wait(tP, pk);
+            exp_pairs<16, T, Cfg::EMU>(x, Cfg::C, m, pk, l0, l1);
+            tmem_st16_wait(tP + 16, pk);
+          }
         }
-        tmem_st16_wait(tP, pk);
-        exp_pairs<16, T, Cfg::EMU>(x, Cfg::C, m, pk, l0, l1);
-        tmem_st16_wait(tP + 16, pk);
         l += l0 + l1;
         if (__any_sync(0xffffffffu, rescale)) {
           // O_t *= alpha on the rows whose running max moved (this thread's 32 columns)
