@@ -81,8 +81,8 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str)
     block = TPR * RPC
     grid = (nrows + RPC - 1) // RPC if nrows else 0
 
-    L = [HEADER, params_struct(len(ins) + len(outs), 0),
-         f'extern "C" __global__ void __launch_bounds__({block}) {symbol}(const __grid_constant__ Params prm) {{']
+    L = [HEADER, params_struct(len(ins) + len(outs), 0)]
+    entry_at = len(L)   # the entry line is added once the per-thread register arrays are known
     for j, n in enumerate(ins):
         L.append(f"  const {CTYPE[n.dtype]}* __restrict__ in{j} = (const {CTYPE[n.dtype]}*)prm.p[{j}];")
     for j, o in enumerate(outs):
@@ -117,8 +117,39 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str)
         st = vec_strides[nid]
         return offset_expr(row_idx, st[:-1])
 
-    # -- prefetch every per-element external operand into registers -----------
-    per_elem = {}   # node id -> ("arr", name) | ("rowconst", name)
+    # -- per-element external operands in registers ----------------------------
+    # Row data is loaded up front (every load in flight at once); an operand that is the same
+    # for every row (a LayerNorm / RMSNorm gain, an L2-resident vector) is loaded vector by
+    # vector inside each element loop that reads it, so it never holds a row of registers.
+    per_elem = {}   # node id -> ("arr" | "bcast" | "rowconst", name)
+
+    def bcast_load(nid: int) -> list[str]:
+        """One 16-byte vector (or one element) of a row-broadcast operand at ``vv``."""
+        j = in_idx[nid]
+        st = vec_strides[nid]
+        cond = "true" if all_valid else f"vv < {NVEC}L"
+        if VEC > 1:
+            return [f"float X{nid}v[{VEC}];",
+                    f"if ({cond}) tj_load_vec(in{j} + {vec_base(nid)} + vv * {VEC}L, X{nid}v);",
+                    f"else {{ for (int u = 0; u < {VEC}; ++u) X{nid}v[u] = 0.0f; }}"]
+        nn = "vv" if st[-1] == 1 else ("0L" if st[-1] == 0 else f"vv * {st[-1]}L")
+        return [f"float X{nid}v[1];", f"X{nid}v[0] = ({cond}) ? tj_f32(in{j}[{vec_base(nid)} + {nn}]) : 0.0f;"]
+
+    def load_loop(nid: int) -> list[str]:
+        j = in_idx[nid]
+        st = vec_strides[nid]
+        out = ["#pragma unroll", f"for (int jv = 0; jv < {VPT}; ++jv) {{", f"  const long vv = t + jv * {TPR}L;"]
+        cond = "valid" if all_valid else f"valid && vv < {NVEC}L"
+        stride_n = st[-1]
+        if VEC > 1:
+            out.append(f"  if ({cond}) tj_load_vec(in{j} + {vec_base(nid)} + vv * {VEC}L, X{nid}[jv]);")
+            out.append(f"  else {{ for (int u = 0; u < {VEC}; ++u) X{nid}[jv][u] = 0.0f; }}")
+        else:
+            nn = "vv" if stride_n == 1 else ("0L" if stride_n == 0 else f"vv * {stride_n}L")
+            out.append(f"  X{nid}[jv][0] = ({cond}) ? tj_f32(in{j}[{vec_base(nid)} + {nn}]) : 0.0f;")
+        out.append("}")
+        return out
+
     for nid, n in vec_reads.items():
         j = in_idx[nid]
         st = vec_strides[nid]
@@ -128,20 +159,12 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str)
             L.append(f"  const float X{nid} = valid ? tj_f32(in{j}[{vec_base(nid)}]) : 0.0f;")
             per_elem[nid] = ("rowconst", f"X{nid}")
             continue
+        if all(x == 0 for x in st[:-1]) and nrows > 1:
+            per_elem[nid] = ("bcast", f"X{nid}")
+            continue
         L.append(f"  float X{nid}[{VPT}][{VEC}];")
-        L.append("  #pragma unroll")
-        L.append(f"  for (int jv = 0; jv < {VPT}; ++jv) {{")
-        L.append(f"    const long vv = t + jv * {TPR}L;")
-        cond = "valid" if all_valid else f"valid && vv < {NVEC}L"
-        stride_n = st[-1]
-        if VEC > 1:
-            L.append(f"    if ({cond}) tj_load_vec(in{j} + {vec_base(nid)} + vv * {VEC}L, X{nid}[jv]);")
-            L.append(f"    else {{ for (int u = 0; u < {VEC}; ++u) X{nid}[jv][u] = 0.0f; }}")
-        else:
-            nn = "vv" if stride_n == 1 else ("0L" if stride_n == 0 else f"vv * {stride_n}L")
-            L.append(f"    X{nid}[jv][0] = ({cond}) ? tj_f32(in{j}[{vec_base(nid)} + {nn}]) : 0.0f;")
-        L.append("  }")
         per_elem[nid] = ("arr", f"X{nid}")
+        L += ["  " + x for x in load_loop(nid)]
 
     # -- values computed per element that a later stage reads: register temps --
     computed_vec: set[int] = set()     # nodes computed per element
@@ -157,9 +180,79 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str)
         for n in vnodes:
             if any(u.id in inside and stage_of.get(u.id, si) != si for u in n.users):
                 temps.add(n.id)
+    # A cheap per-element value a later stage needs is recomputed there from what is live
+    # anyway (row operands in registers, per-row scalars) instead of being kept in a per-row
+    # register array: fewer registers per thread, more rows in flight per SM.
+    node_by_id = {n.id: n for n in k.nodes}
+    cheap = {"add", "sub", "mul", "neg", "abs", "maximum", "minimum", "relu", "where"} | ({"div"} if fast else set())
+    scalar_ids = {n.id for st in stages for n in _scalar_nodes(st, is_vec_stage(st))}
+
+    def rematerialisable(nid: int, depth: int = 0) -> bool:
+        n = node_by_id.get(nid)
+        if n is None or n.op not in cheap or depth > 3:
+            return False
+        for i in n.inputs:
+            if i.op == "const" or i.id in per_elem or i.id in scalar_ids:
+                continue
+            if i.id in inside and not rematerialisable(i.id, depth + 1):
+                return False
+            if i.id not in inside and i.id not in per_elem:
+                return False
+        return True
+
+    remat = {nid for nid in temps if rematerialisable(nid)}
+    # a value inside a recomputed chain must be recomputable as well
+    changed = True
+    while changed:
+        changed = False
+        for nid in list(remat):
+            for i in node_by_id[nid].inputs:
+                if i.id in inside and i.op != "const" and i.id not in scalar_ids and i.id not in remat:
+                    remat.add(i.id)
+                    changed = True
+    temps -= remat
     for nid in sorted(temps):
         if VPT:
             L.append(f"  float T{nid}[{VPT}][{VEC}];")
+    # occupancy hint: the row arrays held across stages plus ~16 registers of addressing and
+    # scalars; asking for that many CTAs per SM keeps ptxas from spending registers that would
+    # cost a resident CTA (a memory-bound kernel needs rows in flight more than ILP)
+    # (rows of one warp or less; a cross-warp reduction needs more scratch registers)
+    live = VPT * VEC * (sum(1 for kind, _ in per_elem.values() if kind == "arr") + len(temps))
+    min_ctas = min(6, 65536 // (block * (live + 16))) if block and TPR <= 32 else 1
+    bounds = f"{block}, {min_ctas}" if min_ctas >= 2 else f"{block}"
+    L.insert(entry_at, f'extern "C" __global__ void __launch_bounds__({bounds}) {symbol}(const __grid_constant__ Params prm) {{')
+
+    def elem_name(nid: int) -> str:
+        kind, nm = per_elem[nid]
+        return {"arr": f"{nm}[jv][u]", "bcast": f"{nm}v[u]", "rowconst": nm}[kind]
+
+    def remat_expr(n: PNode) -> str:
+        mm = {}
+        for i in n.inputs:
+            if i.op == "const":
+                continue
+            if i.id in remat:
+                mm[i.id] = f"({remat_expr(node_by_id[i.id])})"
+            elif i.id in scalar_ids:
+                mm[i.id] = f"s{i.id}"
+            else:
+                mm[i.id] = elem_name(i.id)
+        return expr(n, mm, fast)
+
+    def ext_uses(nodes: list[PNode]) -> set[int]:
+        """External per-element operands read by ``nodes``, through recomputed values too."""
+        used: set[int] = set()
+
+        def walk(n: PNode):
+            for i in n.inputs:
+                if i.id in per_elem:
+                    used.add(i.id)
+                elif i.id in remat:
+                    walk(node_by_id[i.id])
+        for n in nodes:
+            walk(n)
+        return used
     scal = [n for st in stages for n in _scalar_nodes(st, is_vec_stage(st))]
     if scal:
         L.append("  float " + ", ".join(f"s{n.id} = 0.0f" for n in scal) + ";")
@@ -171,12 +264,16 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str)
                 if i.id in m or i.op == "const":
                     continue
                 if i.id in computed_vec:
-                    m[i.id] = f"T{i.id}[jv][u]" if i.id in temps else f"v{i.id}"
+                    if i.id in temps:
+                        m[i.id] = f"T{i.id}[jv][u]"
+                    elif i.id in remat:
+                        m[i.id] = f"({remat_expr(node_by_id[i.id])})"
+                    else:
+                        m[i.id] = f"v{i.id}"
                 elif i.id in computed_scalar:
                     m[i.id] = f"s{i.id}"
                 elif i.id in per_elem and per_element:
-                    kind, nm = per_elem[i.id]
-                    m[i.id] = f"{nm}[jv][u]" if kind == "arr" else nm
+                    m[i.id] = elem_name(i.id)
         return m
 
     def scalar_load(n: PNode, iter_shape: tuple) -> str:
@@ -193,6 +290,9 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str)
         out.append("#pragma unroll")
         out.append(f"for (int jv = 0; jv < {VPT}; ++jv) {{")
         out.append(f"  const long vv = t + jv * {TPR}L;")
+        for nid in sorted(nid for nid in ext_uses(nodes + ([reduce_node] if reduce_node else []))
+                          if per_elem[nid][0] == "bcast"):
+            out += ["  " + x for x in bcast_load(nid)]
         for n in esc_nodes:
             out.append(f"  float ob{n.id}[{VEC}];")
         out.append("  #pragma unroll")
