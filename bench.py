@@ -292,10 +292,13 @@ def run_b200(a) -> None:
     if _tensor_family(ks.family):
         ach = ks.info["flops"] / (kms[dom] * 1e-3) / 1e12
         peak = pk["bf16_tflops_sustained"] if a.config in ("cfg4", "cfg5") else pk["bf16_tflops"]
+        kind = ("sustained" if peak == pk["bf16_tflops_sustained"] else "burst") + " bf16"
+        if ks.info.get("tf32x3"):
+            # f32 GEMM on the TF32 tensor path: half the bf16 rate, three MMAs per product
+            peak, kind = peak / 6.0, kind + " / 2 (TF32 rate) / 3 (3xTF32 products)"
         roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
                 "kernel": ks.symbol, "ms": kms[dom],
-                "peak_kind": ("sustained" if peak == pk["bf16_tflops_sustained"] else "burst") + " bf16, "
-                + ("of measured" if pk["source"] == "measured" else "of fallback")}
+                "peak_kind": kind + (", of measured" if pk["source"] == "measured" else ", of fallback")}
     else:
         ach = ks.info["bytes"] / (kms[dom] * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],

@@ -6,13 +6,16 @@ when ``trans_b``), batch dims broadcast with stride 0 (``cuda_backend.py:330-340
 accumulate in f32, then evaluate every epilogue node per output element in f32
 and store each escaping node in its dtype.
 
-Two implementations:
+Implementations:
 
 * ``tc``   bf16/f16 operands: the persistent tcgen05 kernel of
   ``csrc/kernels/gemm_sm100.cuh`` (TMA -> 128B-swizzled smem -> tcgen05.mma ->
   TMEM -> epilogue).  Needs K % 8 == 0 (16-byte TMA row pitch) and, for an
   N-major B, N % 8 == 0.
-* ``simt`` every other case (f32 operands, odd pitches, K == 0): a 64x64 tile,
+* ``tc`` in 3xTF32 mode for f32 operands with a K-major B and K % 4 == 0: one launch
+  splits A and B into TF32 hi / lo copies, the same kernel issues hi*hi + hi*lo + lo*hi;
+  a GEMM with too few output tiles is split over K (partial sums + a finalize launch).
+* ``simt`` every other case (odd pitches, N-major f32 B, K == 0): a 64x64 tile,
   4x4 register micro-tile FFMA kernel with bounds checks, f32 accumulate.
 """
 from __future__ import annotations
@@ -124,19 +127,92 @@ def _align(x: int, a: int = 256) -> int:
     return (x + a - 1) // a * a
 
 
+def x3_ksplit(M: int, N: int, K: int, batch: int, BN: int) -> int:
+    """K slices for a 3xTF32 GEMM with too few output tiles to fill the GPU: as many as keep
+    every CTA on its own SM, each slice at least 8 k-blocks (256 of K), at most 8."""
+    tiles = batch * ((M + 127) // 128) * ((N + BN - 1) // BN)
+    k_blocks = (K + 31) // 32
+    ks = min(8, NUM_SMS // max(tiles, 1), k_blocks // 8)
+    if ks < 2:
+        return 1
+    kpb = (k_blocks + ks - 1) // ks
+    return (k_blocks + kpb - 1) // kpb   # no empty slice
+
+
+def x3_tile(M: int, N: int, K: int, batch: int, tile: dict | None) -> tuple[int, int]:
+    """(BN, K slices) of a 3xTF32 GEMM.  Its k-blocks are bound by shared-memory traffic (hi and
+    lo copies of a 128-row A tile and a BN-row B tile), so the cost of a choice is waves x
+    k-blocks per CTA x bytes per k-block, plus a fixed cost for the finalize launch of a split
+    (about 8 us, the time of 500 KB of k-block traffic)."""
+    if tile and tile.get("BN"):
+        return tile["BN"], x3_ksplit(M, N, K, batch, tile["BN"])
+    k_blocks = (K + 31) // 32
+    best = None
+    for bn in (64, 128):
+        ks = x3_ksplit(M, N, K, batch, bn)
+        ctas = batch * ((M + 127) // 128) * ((N + bn - 1) // bn) * ks
+        waves = (ctas + NUM_SMS - 1) // NUM_SMS
+        cost = waves * ((k_blocks + ks - 1) // ks) * (2 * (128 + bn) * 128 // 1024) + (500 if ks > 1 else 0)
+        if best is None or cost < best[0]:
+            best = (cost, bn, ks)
+    return best[1], best[2]
+
+
 def gen_matmul_tc_x3(k: PKernel, symbol: str, kernel_id: int, tile: dict | None) -> list[KernelSource]:
     """f32 matmul as [split(A and B), 3xTF32 tcgen05 GEMM]; the hi/lo copies live in the
-    program's workspace (arena space after the planned intermediates)."""
+    program's workspace (arena space after the planned intermediates).  With few output tiles
+    the GEMM is split over K into partial sums in the workspace and a finalize launch adds
+    them and applies the epilogue."""
     mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
     a_hi, a_lo = 0, _align(a.nbytes)
     b_hi = a_lo + _align(a.nbytes)
     b_lo = b_hi + _align(b.nbytes)
-    ws = b_lo + _align(b.nbytes)
+    part = b_lo + _align(b.nbytes)
+    batch = prod(out_shape[:-2])
+    BN, ksplit = x3_tile(M, N, K, batch, tile)
+    tile = dict(tile or {"STAGES": 4, "GROUP_M": 16}, BN=BN)
+    ws = part + (_align(ksplit * batch * M * N * 4) if ksplit > 1 else 0)
     sp = gen_split_tf32(f"{symbol}_split", [(a.numel, ("node", a), a_hi, a_lo), (b.numel, ("node", b), b_hi, b_lo)])
-    g = gen_gemm_tc(k, symbol, kernel_id, tile, x3_scratch=(a_hi, b_hi, a_lo, b_lo))
-    for ks in (sp, g):
+    g = gen_gemm_tc(k, symbol, kernel_id, tile, x3_scratch=(a_hi, b_hi, a_lo, b_lo),
+                    ksplit=ksplit, partial_scratch=part)
+    parts = [sp, g]
+    if ksplit > 1:
+        parts.append(gen_ksplit_finalize(k, f"{symbol}_finalize", g.args, ksplit))
+    for ks in parts:
         ks.info["scratch_bytes"] = ws
-    return [sp, g]
+    return parts
+
+
+def gen_ksplit_finalize(k: PKernel, symbol: str, args: list, ksplit: int) -> KernelSource:
+    """out = epilogue(sum over the K slices of the partial sums): the second half of a split-K
+    GEMM.  Takes the GEMM launch's argument list, so operand indices are the same."""
+    mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
+    ins, outs = list(k.inputs), list(k.outputs)
+    in_index = {n.id: j for j, n in enumerate(ins)}
+    out_index = {o.id: len(ins) + j for j, o in enumerate(outs)}
+    epi = Epilogue(k, in_index, out_index)
+    batch = prod(out_shape[:-2])
+    total = batch * M * N
+    part_idx = len(args) - 1
+    L = [HEADER, params_struct(len(args), 0),
+         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{',
+         f"  const float* __restrict__ part = (const float*)prm.p[{part_idx}];"]
+    L += ["  " + x for x in epi._ptr_lines()]
+    L.append(f"  for (long e = (long)blockIdx.x * 256 + threadIdx.x; e < {total}L; e += (long)gridDim.x * 256) {{")
+    L.append(f"    const long j = e % {N}L, row = e / {N}L, i = row % {M}L, b = row / {M}L;")
+    L.append("    float acc = 0.0f;")
+    L.append("    #pragma unroll")
+    L.append(f"    for (int s = 0; s < {ksplit}; ++s) acc += part[s * {total}L + e];")
+    bl, bidx = epi.batch_index_lines("b")
+    L += ["    " + x for x in bl]
+    L += ["    " + x for x in epi.scalar_element_lines(bidx, "i", "j", "acc")]
+    L.append("  }")
+    L.append("}")
+    grid = max(1, min((total + 255) // 256, NUM_SMS * 8))
+    ks = KernelSource(symbol, "ewise", "\n".join(L), (grid, 1, 1), (256, 1, 1), list(args),
+                      info={"bytes": total * 4 * (ksplit + 1), "numel": total, "ksplit": ksplit})
+    ks.finalize_params()
+    return ks
 
 
 # ---------------------------------------------------------------------------
@@ -329,6 +405,27 @@ class Epilogue:
 # ---------------------------------------------------------------------------
 # tcgen05 kernel
 # ---------------------------------------------------------------------------
+def partial_store_function(M: int, N: int, part_idx: int) -> str:
+    """``epilogue(prm, b, i, j0, acc[32])`` of a split-K GEMM: the raw f32 accumulator row
+    into partial-sum slice ``b`` (= slice * batch + batch index) of the workspace."""
+    vec = N % 4 == 0
+    L = ["  template <class P>",
+         "  static __device__ __forceinline__ void epilogue(const P& prm, long b, long i, long j0, const float (&acc)[32]) {",
+         f"    if (i >= {M}L) return;",
+         f"    float* __restrict__ row = (float*)prm.p[{part_idx}] + (b * {M}L + i) * {N}L;",
+         "    #pragma unroll",
+         "    for (int c = 0; c < 32; c += 4) {",
+         "      const long j = j0 + c;"]
+    if vec:
+        L += [f"      if (j >= {N}L) break;",
+              "      *reinterpret_cast<float4*>(row + j) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);"]
+    else:
+        L += ["      #pragma unroll",
+              f"      for (int u = 0; u < 4; ++u) if (j + u < {N}L) row[j + u] = acc[c + u];"]
+    L += ["    }", "  }"]
+    return "\n".join(L)
+
+
 def choose_tile(M: int, N: int, batch: int, b_mn_major: bool, override: dict | None = None) -> tuple[int, int, int]:
     """(BN, STAGES, GROUP_M): largest N tile that still gives every SM work."""
     if override:
@@ -351,7 +448,7 @@ def choose_tile(M: int, N: int, batch: int, b_mn_major: bool, override: dict | N
 
 
 def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = None,
-                x3_scratch: tuple | None = None) -> KernelSource:
+                x3_scratch: tuple | None = None, ksplit: int = 1, partial_scratch: int = 0) -> KernelSource:
     mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
     batch_shape = out_shape[:-2]
     batch = prod(batch_shape)
@@ -359,13 +456,13 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     in_index = {n.id: j for j, n in enumerate(ins)}
     out_index = {o.id: len(ins) + j for j, o in enumerate(outs)}
     x3 = x3_scratch is not None
-    nptr = len(ins) + len(outs) + 1 + (4 if x3 else 0)   # + status word (+ hi/lo operand copies)
+    # + status word (+ hi/lo operand copies) (+ the partial sums of a split-K GEMM)
+    nptr = len(ins) + len(outs) + 1 + (4 if x3 else 0) + (1 if ksplit > 1 else 0)
     status_idx = len(ins) + len(outs)
     epi = Epilogue(k, in_index, out_index)
     b_mn = not tb
     if x3 and not tile:
-        tile = {"BN": 64 if (M + 127) // 128 * ((N + 127) // 128) * batch < NUM_SMS else 128,
-                "STAGES": 4, "GROUP_M": 16}
+        tile = {"BN": x3_tile(M, N, K, batch, None)[0], "STAGES": 4, "GROUP_M": 16}
     BN, STAGES, GROUP_M = choose_tile(M, N, batch, b_mn, tile)
     if x3:
         STAGES = min(STAGES, max(2, (200 * 1024) // (2 * (128 * 128 + BN * 128))))
@@ -375,7 +472,7 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     a_mats = prod(a.shape[:-2])
     b_mats = prod(b.shape[:-2])
     bl, bidx = decompose_stmts("b", batch_shape, "bb") if batch_shape else ([], [])
-    tma_store = epi.tma_store_ok() and not x3
+    tma_store = epi.tma_store_ok() and not x3 and ksplit == 1
     L = [HEADER, '#include "gemm_sm100_pair.cuh"' if pair else '#include "gemm_sm100.cuh"',
          params_struct(nptr, 4 if x3 else (3 if tma_store else 2))]
     L.append("struct Cfg {")
@@ -383,7 +480,7 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     threads = 64 + 32 * epi_warps
     out_stage = epi_warps * 2 * 32 * 32 * 2 if tma_store else 0
     L.append(f"  static constexpr int BN = {BN}, STAGES = {STAGES}, M = {M}, N = {N}, K = {K}, GROUP_M = {GROUP_M};")
-    L.append(f"  static constexpr int EPI_WARPS = {epi_warps};")
+    L.append(f"  static constexpr int EPI_WARPS = {epi_warps}, KSPLIT = {ksplit};")
     L.append(f"  static constexpr bool TF32X3 = {'true' if x3 else 'false'};")
     L.append(f"  static constexpr bool TMA_STORE = {'true' if tma_store else 'false'};")
     L.append(f"  using OutT = {CTYPE[outs[0].dtype] if tma_store else 'float'};")
@@ -394,7 +491,10 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     L.append(f"    ab = {offset_expr(bidx, a_bs) if batch_shape else '0L'};")
     L.append(f"    bb_ = {offset_expr(bidx, b_bs) if batch_shape else '0L'};")
     L.append("  }")
-    L.append(epi.vals32_function() if tma_store else epi.chunk32_function())
+    if ksplit > 1:
+        L.append(partial_store_function(M, N, nptr - 1))
+    else:
+        L.append(epi.vals32_function() if tma_store else epi.chunk32_function())
     L.append("};")
     b_rows = BN // 2 if pair else BN
     smem = 1024 + STAGES * (2 if x3 else 1) * (128 * 128 + b_rows * 128) + out_stage + (2 * STAGES + 6) * 8 + 16
@@ -406,7 +506,7 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     L.append("}")
     m_tiles = (M + (255 if pair else 127)) // (256 if pair else 128)
     n_tiles = (N + BN - 1) // BN
-    num_tiles = batch * m_tiles * n_tiles
+    num_tiles = batch * m_tiles * n_tiles * ksplit
     grid = 2 * min(num_tiles, NUM_SMS // 2) if pair else min(num_tiles, NUM_SMS)
     esz = ITEM[a.dtype]
     bk = 128 // esz                      # K elements per 128-byte swizzle row
@@ -434,10 +534,13 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     if x3:
         a_hi, b_hi, a_lo, b_lo = x3_scratch
         args += [("scratch", a_hi), ("scratch", b_hi), ("scratch", a_lo), ("scratch", b_lo)]
+    if ksplit > 1:
+        args.append(("scratch", partial_scratch))
     ks = KernelSource(symbol, "gemm_tc", "\n".join(L), (grid, 1, 1), (threads, 1, 1), args, smem=smem,
                       tmaps=tmaps, cluster=(2, 1, 1) if pair else (1, 1, 1),
                       info={"M": M, "N": N, "K": K, "batch": batch, "BN": BN, "stages": STAGES,
                             "tma_store": tma_store, "epi_warps": epi_warps, "pair": pair, "tf32x3": x3,
+                            "ksplit": ksplit,
                             "flops": 2.0 * batch * M * N * K, "tiles": num_tiles,
                             "bytes": sum(n.nbytes for n in ins) + sum(o.nbytes for o in outs)})
     ks.finalize_params()

@@ -225,7 +225,7 @@ TJ_DEV void tile_coords(long t, int m_tiles, int n_tiles, int group_m, long& b, 
 }
 
 // Cfg provides:
-//   static constexpr int BN, STAGES, M, N, K, GROUP_M, EPI_WARPS; static constexpr long BATCH;
+//   static constexpr int BN, STAGES, M, N, K, GROUP_M, EPI_WARPS, KSPLIT; static constexpr long BATCH;
 //   static constexpr bool BF16, B_MN_MAJOR, TMA_STORE;  using OutT = <output element type>;
 //   static __device__ void batch_map(long b, long& a_batch, long& b_batch);
 //   template <class P> static __device__ void epilogue(const P& prm, long b, long i, long j0, const float (&acc)[32]);
@@ -250,7 +250,12 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
   constexpr int m_tiles = (Cfg::M + BM - 1) / BM;
   constexpr int n_tiles = (Cfg::N + BN - 1) / BN;
   constexpr int k_blocks = (Cfg::K + BK - 1) / BK;
-  constexpr long num_tiles = Cfg::BATCH * m_tiles * n_tiles;
+  // split-K: work item w = (tile w / KSPLIT, k slice w % KSPLIT of KPB k-blocks); the epilogue
+  // receives batch index b + slice * BATCH (a partial-sum slice of the workspace)
+  constexpr int KSPLIT = Cfg::KSPLIT;
+  constexpr int KPB = (k_blocks + KSPLIT - 1) / KSPLIT;
+  static_assert(KSPLIT >= 1 && (KSPLIT - 1) * KPB < k_blocks, "every k slice has work");
+  constexpr long num_tiles = Cfg::BATCH * m_tiles * n_tiles * KSPLIT;
   constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
   constexpr uint32_t IDESC = X3 ? idesc_tf32(BM, BN) : idesc_f16(Cfg::BF16, BM, BN, false, Cfg::B_MN_MAJOR);
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
@@ -324,7 +329,9 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
       // bounded wait on it must run out and report through the status words.
       bool stall_pending = true;
 #endif
-      for (long t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (long w = blockIdx.x; w < num_tiles && ok; w += gridDim.x) {
+        const long t = w / KSPLIT;
+        const int kb0 = static_cast<int>(w % KSPLIT) * KPB, kb1 = min(kb0 + KPB, k_blocks);
         long b;
         int mt, nt;
         tile_coords(t, m_tiles, n_tiles, Cfg::GROUP_M, b, mt, nt);
@@ -332,7 +339,7 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
         Cfg::batch_map(b, ab, bb);
         const int a_row = static_cast<int>(ab * Cfg::M + static_cast<long>(mt) * BM);
         const int n0 = nt * BN;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, status, kernel_id * 16 + 1)) {
             ok = false;
             break;
@@ -382,7 +389,8 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
     // smem descriptors of stage 0; a stage / k step adds (byte offset >> 4) to the start address
     const uint64_t da0 = desc_sw128(smem_u32(sA), 16, 1024);
     const uint64_t db0 = Cfg::B_MN_MAJOR ? desc_sw128(smem_u32(sB), BK * 128, 1024) : desc_sw128(smem_u32(sB), 16, 1024);
-    for (long t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+    for (long w = blockIdx.x; w < num_tiles && ok; w += gridDim.x, ++it) {
+      const int kb0 = static_cast<int>(w % KSPLIT) * KPB, kb1 = min(kb0 + KPB, k_blocks);
       const int buf = it & 1;
       if (!mbar_wait_warp(smem_u32(&tempty[buf]), ((it >> 1) & 1) ^ 1u, abort_flag, status, kernel_id * 16 + 2)) {
         ok = false;
@@ -390,7 +398,7 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
       }
       tc_fence_after();
       const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN);
-      for (int kb = 0; kb < k_blocks; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait_warp(smem_u32(&full[stage]), phase, abort_flag, status, kernel_id * 16 + 3)) {
           ok = false;
           break;
@@ -403,9 +411,9 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
           const uint64_t ad = a0 + 2 * kk;  // 32 bytes of K per step
           const uint64_t bd = Cfg::B_MN_MAJOR ? b0 + ((kk * UK * 128) >> 4) : b0 + 2 * kk;
           if constexpr (!X3) {
-            umma_f16_elect(d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+            umma_f16_elect(d, ad, bd, IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
           } else {
-            umma_tf32_elect(d, ad, bd, IDESC, (kb | kk) != 0 ? 1u : 0u);
+            umma_tf32_elect(d, ad, bd, IDESC, (kb != kb0 || kk != 0) ? 1u : 0u);
             umma_tf32_elect(d, ad, bd + (B_BYTES >> 4), IDESC, 1u);
             umma_tf32_elect(d, ad + (A_BYTES >> 4), bd, IDESC, 1u);
           }
@@ -432,10 +440,12 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
     uint8_t* stage_out = sOut + (warp - 2) * 2 * OUT_STAGE;
     int sbuf = 0;
     int it = 0;
-    for (long t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+    for (long w = blockIdx.x; w < num_tiles; w += gridDim.x, ++it) {
+      const long t = w / KSPLIT;
       long b;
       int mt, nt;
       tile_coords(t, m_tiles, n_tiles, Cfg::GROUP_M, b, mt, nt);
+      b += (w % KSPLIT) * Cfg::BATCH;  // partial-sum slice (KSPLIT > 1)
       const int buf = it & 1;
       const bool ok = mbar_wait(smem_u32(&tfull[buf]), (it >> 1) & 1, abort_flag, status, kernel_id * 16 + 4);
       if (!__all_sync(0xffffffffu, ok)) break;  // the warp leaves together: tcgen05.ld is warp-collective

@@ -119,6 +119,9 @@ def cases(tj):
     add("empty_rows", lambda x, b: tj.gelu(x + b), [(0, 16), (16,)], dtypes=(F32,))
     add("transpose_2d", lambda x: tj.permute(x, 1, 0) * 2.0, [(67, 129)])
     add("linear_nobias_ragged", lambda x, w: tj.linear(x, w), [(200, 136), (300, 136)], dtypes=(F32,))
+    # few output tiles and a long K: the 3xTF32 GEMM is split over K (ragged N: scalar partial stores)
+    add("linear_splitk_ragged", lambda x, w, b: tj.gelu(tj.linear(x, w, b)), [(100, 2048), (130, 2048), (130,)],
+        dtypes=(F32,))
     # attention core (QK^T * scale -> softmax -> PV), the pattern of the transformer config
     add("attention_core", lambda q, k, v: tj.matmul(tj.softmax(tj.matmul(q, tj.transpose(k, -1, -2)) * 0.125), v),
         [(2, 4, 256, 64), (2, 4, 256, 64), (2, 4, 256, 64)], dtypes=(BF16,))

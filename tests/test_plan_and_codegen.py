@@ -278,3 +278,19 @@ def test_polynomial_exp2_is_below_half_an_ulp_of_bf16_and_f16():
     # masked keys (-inf) and far-below-range arguments vanish after rounding to half precision
     tiny = _ex2_poly_f32(np.array([-np.inf, -200.0, -127.0], np.float32))
     assert np.all(tiny < 2.0 ** -125) and np.all(tiny >= 0)
+
+
+def test_x3_gemm_with_few_tiles_is_split_over_k():
+    """cfg1's second GEMM (512 x 768, K = 3072) has 24 output tiles of 128 x 128: six K slices
+    write partial sums into the workspace and a finalize launch adds them and applies the
+    epilogue; the first (K = 768, 96 tiles) fills one wave unsplit."""
+    ks = generate(FX.load_plan("cfg1"))
+    assert [k.family for k in ks] == ["row", "split", "gemm_tc", "split", "gemm_tc", "ewise"]
+    g1, g2, fin = ks[2], ks[4], ks[5]
+    assert (g1.info["BN"], g1.info["ksplit"], g1.grid[0]) == (128, 1, 96)
+    assert (g2.info["BN"], g2.info["ksplit"], g2.grid[0]) == (128, 6, 144) and "KSPLIT = 6" in g2.source
+    assert fin.info["ksplit"] == 6 and fin.args == g2.args and fin.info["index"] == g2.info["index"] == 2
+    # ragged N: scalar partial stores; 1 x 3 tiles of 128 x 64, K = 2048 -> eight slices
+    ks = generate(FX.load_plan("linear_splitk_ragged__f32"))
+    g = [k for k in ks if k.family == "gemm_tc"][0]
+    assert g.info["ksplit"] == 8 and "row[j + u] = acc[c + u]" in g.source
