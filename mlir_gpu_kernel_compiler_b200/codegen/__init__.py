@@ -6,7 +6,8 @@ elementwise/copy -> vectorised grid-stride kernel, row -> staged row kernel,
 reduce -> row kernel with one stage, matmul -> tcgen05 GEMM (bf16/f16), the
 3xTF32 tcgen05 path (f32 with a K-major B: operand split pre-passes + GEMM), or the
 SIMT GEMM (everything else); ``attention`` (the matmul -> softmax -> matmul chain
-``fuse.py`` folds into one kernel) -> the fused tcgen05 attention kernel.  A plan kernel can therefore become several launches;
+``fuse.py`` folds into one kernel) -> the fused tcgen05 attention kernel; ``matmul_multi``
+(GEMMs sharing A, also from ``fuse.py``) -> one tcgen05 GEMM over the concatenated N.  A plan kernel can therefore become several launches;
 ``KernelSource.info["index"]`` names the plan kernel each launch belongs to.
 """
 from __future__ import annotations
@@ -15,7 +16,7 @@ from ..plan import PProgram
 from .attention import gen_attention
 from .common import KernelSource
 from .ewise import gen_elementwise
-from .gemm import gen_gemm_simt, gen_gemm_tc, gen_matmul_tc_x3, tc_eligible, x3_eligible
+from .gemm import gen_gemm_multi, gen_gemm_simt, gen_gemm_tc, gen_matmul_tc_x3, tc_eligible, x3_eligible
 from .row import gen_row
 
 
@@ -32,6 +33,8 @@ def generate(plan: PProgram, tiles: dict | None = None, prefix: str = "tj") -> l
             ks = gen_row(k, [k], tuple(x.shape[:-1]), int(x.shape[-1]) if x.shape else 1, sym)
         elif k.kind == "attention":
             ks = gen_attention(k, sym, idx)
+        elif k.kind == "matmul_multi":
+            ks = gen_gemm_multi(k, sym, idx)
         elif k.kind == "matmul":
             if tc_eligible(k) and x3_eligible(k):
                 parts = gen_matmul_tc_x3(k, sym, idx, (tiles or {}).get(idx))

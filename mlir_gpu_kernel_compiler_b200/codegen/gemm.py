@@ -480,7 +480,9 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     threads = 64 + 32 * epi_warps
     out_stage = epi_warps * 2 * 32 * 32 * 2 if tma_store else 0
     L.append(f"  static constexpr int BN = {BN}, STAGES = {STAGES}, M = {M}, N = {N}, K = {K}, GROUP_M = {GROUP_M};")
-    L.append(f"  static constexpr int EPI_WARPS = {epi_warps}, KSPLIT = {ksplit};")
+    L.append(f"  static constexpr int EPI_WARPS = {epi_warps}, KSPLIT = {ksplit}, NSEG = 1;")
+    L.append("  static __device__ __forceinline__ int segment(int) { return 0; }")
+    L.append("  static __device__ __forceinline__ int seg_tile0(int) { return 0; }")
     L.append(f"  static constexpr bool TF32X3 = {'true' if x3 else 'false'};")
     L.append(f"  static constexpr bool TMA_STORE = {'true' if tma_store else 'false'};")
     L.append(f"  using OutT = {CTYPE[outs[0].dtype] if tma_store else 'float'};")
@@ -622,6 +624,75 @@ def gen_gemm_simt(k: PKernel, symbol: str) -> KernelSource:
     grid = ((N + BN_ - 1) // BN_, (M + BM_ - 1) // BM_, batch) if M and N and batch else (0, 1, 1)
     ks = KernelSource(symbol, "gemm_simt", "\n".join(L), grid, (256, 1, 1), [("node", n) for n in ins + outs],
                       info={"M": M, "N": N, "K": K, "batch": batch, "flops": 2.0 * batch * M * N * K,
+                            "bytes": sum(n.nbytes for n in ins) + sum(o.nbytes for o in outs)})
+    ks.finalize_params()
+    return ks
+
+
+# ---------------------------------------------------------------------------
+# several GEMMs sharing A (kind "matmul_multi", built by fuse.py)
+# ---------------------------------------------------------------------------
+def gen_gemm_multi(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = None) -> KernelSource:
+    """C_g = A · B_gᵀ for g = 0..G-1 as one tcgen05 GEMM over the concatenated N: the column
+    tiles of segment g read B_g through its own tensor map and store to C_g, so the A tiles
+    are read once for all G products and the GPU sees one launch with G times the tiles."""
+    parts = k.attrs["parts"]             # [(B node, output node, N)]
+    a = k.attrs["a"]
+    dt = a.dtype
+    M, K = a.shape
+    BN = 256
+    STAGES = (tile or {}).get("STAGES", 4)
+    GROUP_M = (tile or {}).get("GROUP_M", 16)
+    ins = [a] + [p_[0] for p_ in parts]
+    outs = [p_[1] for p_ in parts]
+    N = sum(p_[2] for p_ in parts)
+    status_idx = len(ins) + len(outs)
+    seg_tiles = [p_[2] // BN for p_ in parts]
+    starts = [sum(seg_tiles[:g]) for g in range(len(parts))]
+    col0 = [sum(p_[2] for p_ in parts[:g]) for g in range(len(parts))]
+    L = [HEADER, '#include "gemm_sm100.cuh"', params_struct(status_idx + 1, 1 + len(parts))]
+    L.append("struct Cfg {")
+    L.append(f"  static constexpr int BN = {BN}, STAGES = {STAGES}, M = {M}, N = {N}, K = {K}, GROUP_M = {GROUP_M};")
+    L.append(f"  static constexpr int EPI_WARPS = 8, KSPLIT = 1, NSEG = {len(parts)};")
+    L.append("  static constexpr bool TF32X3 = false, TMA_STORE = false;")
+    L.append("  using OutT = float;")
+    L.append("  static constexpr long BATCH = 1L;")
+    L.append(f"  static constexpr bool BF16 = {'true' if dt == 'bf16' else 'false'}, B_MN_MAJOR = false;")
+    L.append("  static __device__ __forceinline__ void batch_map(long, long& ab, long& bb_) { ab = 0; bb_ = 0; }")
+    seg = " : ".join(f"nt < {starts[g] + seg_tiles[g]} ? {g}" for g in range(len(parts) - 1)) + f" : {len(parts) - 1}"
+    L.append(f"  static __device__ __forceinline__ int segment(int nt) {{ return {seg}; }}")
+    st0 = " : ".join(f"g == {g} ? {starts[g]}" for g in range(len(parts) - 1)) + f" : {starts[-1]}"
+    L.append(f"  static __device__ __forceinline__ int seg_tile0(int g) {{ return {st0}; }}")
+    L.append("  template <class P>")
+    L.append("  static __device__ __forceinline__ void epilogue(const P& prm, long, long i, long j0, const float (&acc)[32]) {")
+    L.append(f"    if (i >= {M}L) return;")
+    for g, (bnode, onode, ng) in enumerate(parts):
+        if g == len(parts) - 1:
+            L.append("    else {")
+        else:
+            L.append(f"    {'if' if g == 0 else 'else if'} (j0 < {col0[g] + ng}L) {{")
+        L.append(f"      {CTYPE[onode.dtype]}* __restrict__ dst = ({CTYPE[onode.dtype]}*)prm.p[{len(ins) + g}] + "
+                 f"i * {ng}L + (j0 - {col0[g]}L);")
+        L.append("      #pragma unroll")
+        L.append("      for (int c = 0; c < 32; c += 8) tj_store_vec(dst + c, acc + c);")
+        L.append("    }")
+    L.append("  }")
+    L.append("};")
+    smem = 1024 + STAGES * (128 * 128 + BN * 128) + (2 * STAGES + 6) * 8 + 16
+    L.append(f'extern "C" __global__ void __launch_bounds__(320, 1) {symbol}(const __grid_constant__ Params prm) {{')
+    L.append(f"  tjg::gemm_sm100<Cfg>(prm, (int*)prm.p[{status_idx}], {kernel_id});")
+    L.append("}")
+    esz = ITEM[dt]
+    tmaps = [TMapSpec(arg=0, dtype=dt, dims=[K, M], strides=[K * esz], box=[128 // esz, 128], swizzle=3)]
+    for g, (bnode, _o, ng) in enumerate(parts):
+        tmaps.append(TMapSpec(arg=1 + g, dtype=dt, dims=[K, ng], strides=[K * esz], box=[128 // esz, BN], swizzle=3))
+    num_tiles = ((M + 127) // 128) * (N // BN)
+    args = [("node", n) for n in ins] + [("node", o) for o in outs] + [("status", None)]
+    ks = KernelSource(symbol, "gemm_tc", "\n".join(L), (min(num_tiles, NUM_SMS), 1, 1), (320, 1, 1), args, smem=smem,
+                      tmaps=tmaps,
+                      info={"M": M, "N": N, "K": K, "batch": 1, "BN": BN, "stages": STAGES, "tma_store": False,
+                            "epi_warps": 8, "pair": False, "tf32x3": False, "ksplit": 1, "segments": len(parts),
+                            "flops": 2.0 * M * N * K, "tiles": num_tiles,
                             "bytes": sum(n.nbytes for n in ins) + sum(o.nbytes for o in outs)})
     ks.finalize_params()
     return ks

@@ -225,7 +225,8 @@ TJ_DEV void tile_coords(long t, int m_tiles, int n_tiles, int group_m, long& b, 
 }
 
 // Cfg provides:
-//   static constexpr int BN, STAGES, M, N, K, GROUP_M, EPI_WARPS, KSPLIT; static constexpr long BATCH;
+//   static constexpr int BN, STAGES, M, N, K, GROUP_M, EPI_WARPS, KSPLIT, NSEG; static constexpr long BATCH;
+//   (NSEG > 1: static __device__ int segment(int nt), seg_tile0(int g) map a column tile to its B operand)
 //   static constexpr bool BF16, B_MN_MAJOR, TMA_STORE;  using OutT = <output element type>;
 //   static __device__ void batch_map(long b, long& a_batch, long& b_batch);
 //   template <class P> static __device__ void epilogue(const P& prm, long b, long i, long j0, const float (&acc)[32]);
@@ -298,7 +299,7 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch(tmA);
-    tma_prefetch(tmB);
+    for (int g = 0; g < Cfg::NSEG; ++g) tma_prefetch(&prm.tm[1 + g]);
     if constexpr (Cfg::TMA_STORE || X3) tma_prefetch(&prm.tm[2]);
     if constexpr (X3) tma_prefetch(&prm.tm[3]);
   }
@@ -338,7 +339,15 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
         long ab, bb;
         Cfg::batch_map(b, ab, bb);
         const int a_row = static_cast<int>(ab * Cfg::M + static_cast<long>(mt) * BM);
-        const int n0 = nt * BN;
+        // several B operands side by side along N (GEMMs sharing A): segment g owns the
+        // column tiles from seg_tile0(g), its B rows start at 0 in its own tensor map
+        const CUtensorMap* tb = tmB;
+        int n0 = nt * BN;
+        if constexpr (Cfg::NSEG > 1) {
+          const int g = Cfg::segment(nt);
+          tb = &prm.tm[1 + g];
+          n0 = (nt - Cfg::seg_tile0(g)) * BN;
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, status, kernel_id * 16 + 1)) {
             ok = false;
@@ -360,7 +369,7 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
           uint8_t* b_st = sB + stage * OPC * B_BYTES;
           tma_load_2d(smem_u32(a_st), tmA, fb, kb * BK, a_row);
           if constexpr (!Cfg::B_MN_MAJOR) {
-            tma_load_2d(smem_u32(b_st), tmB, fb, kb * BK, static_cast<int>(bb * Cfg::N + n0));
+            tma_load_2d(smem_u32(b_st), tb, fb, kb * BK, static_cast<int>(bb * Cfg::N + n0));
           } else {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c)

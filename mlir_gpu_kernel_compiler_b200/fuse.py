@@ -13,7 +13,10 @@ them and after O.  ``fuse_attention`` replaces such a chain by one kernel of kin
 transpose that only feeds Q, K or V (or only consumes O) into that kernel's
 addressing, so the copy kernel disappears as well.
 
-The rewrite is semantic-preserving for the plan's outputs only: S and P must not
+``fuse_shared_a_gemms`` merges consecutive bare GEMMs that read the same A operand (the
+q / k / v projections of a transformer block) into one ``matmul_multi`` kernel.
+
+The attention rewrite is semantic-preserving for the plan's outputs only: S and P must not
 escape (not graph outputs, no user outside the chain), otherwise the chain is left
 as it is (e.g. a graph that returns the attention probabilities).  The memory plan
 of the rewritten program no longer holds S, P or the folded transposes.
@@ -212,8 +215,65 @@ def fuse_attention(plan: PProgram) -> PProgram:
                     aliases=plan.aliases, meta=dict(plan.meta, fused_attention=len(matches)))
 
 
+def _plain_shared_a_matmul(k: PKernel):
+    """(A, B, N) of a kernel that is a bare bf16/f16 ``A @ Bᵀ`` (2-D, no epilogue), else None."""
+    if k.kind != "matmul" or len(k.nodes) != 1 or k.outputs != [k.anchor]:
+        return None
+    mm = k.anchor
+    if mm.op != "matmul" or not mm.attrs.get("trans_b"):
+        return None
+    a, b = mm.inputs
+    if len(a.shape) != 2 or len(b.shape) != 2 or a.dtype not in ("bf16", "f16") or b.dtype != a.dtype:
+        return None
+    if mm.dtype != a.dtype or a.shape[1] != b.shape[1] or a.shape[1] % 8:
+        return None
+    return a, b, b.shape[0]
+
+
+def fuse_shared_a_gemms(plan: PProgram) -> PProgram:
+    """Consecutive bare GEMMs ``A @ B_gᵀ`` with the same A (q/k/v or gate/up projections)
+    become one kernel of kind ``matmul_multi`` over the concatenated N (every N_g a multiple
+    of the 256-column tile, so no tile straddles two products).  Outputs are unchanged."""
+    ks = plan.kernels
+    out: list[PKernel] = []
+    i = 0
+    changed = False
+    while i < len(ks):
+        first = _plain_shared_a_matmul(ks[i])
+        run = [i]
+        if first is not None and first[2] % 256 == 0:
+            j = i + 1
+            while j < len(ks):
+                nxt = _plain_shared_a_matmul(ks[j])
+                if nxt is None or nxt[0] is not first[0] or nxt[2] % 256 or nxt[0].dtype != first[0].dtype:
+                    break
+                run.append(j)
+                j += 1
+        if len(run) < 2:
+            out.append(ks[i])
+            i += 1
+            continue
+        parts = []
+        for kj in run:
+            a, b, n = _plain_shared_a_matmul(ks[kj])
+            parts.append((b, ks[kj].anchor, n))
+        a = first[0]
+        fk = PKernel(kind="matmul_multi", nodes=[ks[kj].anchor for kj in run], anchor=ks[run[0]].anchor,
+                     inputs=[a] + [p_[0] for p_ in parts], outputs=[p_[1] for p_ in parts],
+                     iter_shape=(a.shape[0], sum(p_[2] for p_ in parts)))
+        fk.attrs = {"a": a, "parts": parts}
+        out.append(fk)
+        i = run[-1] + 1
+        changed = True
+    if not changed:
+        return plan
+    return PProgram(name=plan.name, nodes=plan.nodes, inputs=plan.inputs, outputs=plan.outputs, kernels=out,
+                    aliases=plan.aliases, meta=dict(plan.meta, fused_shared_a=True))
+
+
 def fuse(plan: PProgram) -> PProgram:
-    """All backend rewrites (``TENSORJIT_B200_FUSE=0`` disables them)."""
+    """All backend rewrites (``TENSORJIT_B200_FUSE=0`` disables them): attention chains, then
+    GEMMs that share their A operand."""
     if os.environ.get("TENSORJIT_B200_FUSE", "1") == "0":
         return plan
-    return fuse_attention(plan)
+    return fuse_shared_a_gemms(fuse_attention(plan))

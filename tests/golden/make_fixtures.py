@@ -119,6 +119,9 @@ def cases(tj):
     add("empty_rows", lambda x, b: tj.gelu(x + b), [(0, 16), (16,)], dtypes=(F32,))
     add("transpose_2d", lambda x: tj.permute(x, 1, 0) * 2.0, [(67, 129)])
     add("linear_nobias_ragged", lambda x, w: tj.linear(x, w), [(200, 136), (300, 136)], dtypes=(F32,))
+    # three bare GEMMs reading the same A (a q/k/v-style projection): one GEMM over the concatenated N
+    add("shared_a_projections", lambda x, w1, w2, w3: (tj.linear(x, w1), tj.linear(x, w2), tj.linear(x, w3)),
+        [(300, 128), (256, 128), (512, 128), (256, 128)], dtypes=(BF16,))
     # few output tiles and a long K: the 3xTF32 GEMM is split over K (ragged N: scalar partial stores)
     add("linear_splitk_ragged", lambda x, w, b: tj.gelu(tj.linear(x, w, b)), [(100, 2048), (130, 2048), (130,)],
         dtypes=(F32,))

@@ -294,3 +294,22 @@ def test_x3_gemm_with_few_tiles_is_split_over_k():
     ks = generate(FX.load_plan("linear_splitk_ragged__f32"))
     g = [k for k in ks if k.family == "gemm_tc"][0]
     assert g.info["ksplit"] == 8 and "row[j + u] = acc[c + u]" in g.source
+
+
+def test_gemms_sharing_a_become_one_launch():
+    from mlir_gpu_kernel_compiler_b200.fuse import fuse
+
+    p = fuse(FX.load_plan("shared_a_projections__bf16"))
+    assert [k.kind for k in p.kernels] == ["matmul_multi"]
+    k = p.kernels[0]
+    assert [n for _b, _o, n in k.attrs["parts"]] == [256, 512, 256] and len(k.outputs) == 3
+    ks = generate(p)[0]
+    assert ks.family == "gemm_tc" and ks.info["segments"] == 3 and ks.info["N"] == 1024
+    assert len(ks.tmaps) == 4 and [t.dims[1] for t in ks.tmaps[1:]] == [256, 512, 256]
+    # cfg4: the q, k, v projections (same LayerNorm output) -> one launch; 16 plan kernels -> 8
+    p4 = fuse(FX.load_plan("cfg4"))
+    assert [k.kind for k in p4.kernels] == ["row", "matmul_multi", "attention", "matmul", "row", "matmul",
+                                           "matmul", "elementwise"]
+    # a GEMM with an epilogue, or N not a multiple of the 256-column tile, is left alone
+    p5 = fuse(FX.load_plan("attention_heads__bf16"))
+    assert "matmul_multi" not in [k.kind for k in p5.kernels]
