@@ -48,9 +48,11 @@ EXPR = {
 # Half-precision programs round every stored value to bf16/f16 (relative step
 # 2^-8 / 2^-11), so their kernels use the hardware approximations where those are
 # orders of magnitude tighter than that rounding: __expf (ex2.approx based, rel.
-# error ~1e-6 for the arguments seen here) and __fdividef (rcp.approx * a).  f32
-# programs keep the IEEE-accurate library functions.
+# error ~1e-6 for the arguments seen here), __fdividef (rcp.approx * a) and a GELU whose
+# erf is the Abramowitz & Stegun 7.1.26 approximation (|error| <= 1.5e-7).  f32 programs
+# keep the IEEE-accurate library functions.
 EXPR_FAST = dict(EXPR, exp="__expf({0})", sigmoid="tj_sigmoid_fast({0})", silu="tj_silu_fast({0})",
+                 gelu="tj_gelu_fast({0})",
                  div="__fdividef({0}, {1})")
 
 

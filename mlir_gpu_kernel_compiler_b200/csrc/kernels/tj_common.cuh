@@ -96,6 +96,17 @@ TJ_DEV float tj_rsqrt(float x) { return 1.0f / sqrtf(x); }
 TJ_DEV float tj_relu(float x) { return fmaxf(x, 0.0f); }
 TJ_DEV float tj_where(float c, float a, float b) { return c != 0.0f ? a : b; }
 TJ_DEV float tj_sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+// GELU for half-precision outputs: erf by Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7, the
+// approximation the reference's C backend uses) with the fast exponential and reciprocal;
+// a few FMAs and two MUFU operations instead of erff, far below bf16 / f16 rounding.
+TJ_DEV float tj_gelu_fast(float x) {
+  const float z = fminf(fabsf(x) * 0.70710678118654752f, 4.0f);
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+  const float poly = fmaf(fmaf(fmaf(fmaf(1.061405429f, t, -1.453152027f), t, 1.421413741f), t, -0.284496736f), t,
+                          0.254829592f);
+  const float e = 1.0f - poly * t * __expf(-z * z);  // erf(|x| / sqrt 2)
+  return 0.5f * x * (1.0f + copysignf(e, x));
+}
 TJ_DEV float tj_silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // ---------------------------------------------------------------------------

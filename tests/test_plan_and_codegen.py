@@ -313,3 +313,26 @@ def test_gemms_sharing_a_become_one_launch():
     # a GEMM with an epilogue, or N not a multiple of the 256-column tile, is left alone
     p5 = fuse(FX.load_plan("attention_heads__bf16"))
     assert "matmul_multi" not in [k.kind for k in p5.kernels]
+
+
+def test_fast_gelu_for_half_precision_outputs_tracks_erf_gelu():
+    """numpy float32 restatement of tj_gelu_fast (csrc/kernels/tj_common.cuh) against the
+    exact erf GELU: the error stays far below half an ulp of bf16 (2^-9 relative)."""
+    import math
+
+    x = np.linspace(-8.0, 8.0, 40001).astype(np.float32)
+    z = np.minimum(np.abs(x) * np.float32(0.70710678118654752), np.float32(4.0))
+    t = np.float32(1.0) / (np.float32(0.3275911) * z + np.float32(1.0))
+    poly = ((((np.float32(1.061405429) * t - np.float32(1.453152027)) * t + np.float32(1.421413741)) * t
+             - np.float32(0.284496736)) * t + np.float32(0.254829592))
+    e = np.float32(1.0) - poly * t * np.exp(-z * z)
+    y = np.float32(0.5) * x * (np.float32(1.0) + np.copysign(e, x))
+    ref = np.array([0.5 * v * (1.0 + math.erf(v / math.sqrt(2.0))) for v in x.astype(np.float64)])
+    assert np.abs(y - ref).max() < 1e-6
+    # relative error (where 1 + erf cancels for x < -3 the absolute error dominates)
+    err = np.abs(y - ref) / np.maximum(np.abs(ref), 1e-2)
+    assert err.max() < 1e-4
+    # used only where every stored value is half precision
+    from mlir_gpu_kernel_compiler_b200.codegen.common import EXPR, EXPR_FAST
+
+    assert "fast" in EXPR_FAST["gelu"] and "erff" not in EXPR_FAST["gelu"] and EXPR["gelu"] == "tj_gelu({0})"
