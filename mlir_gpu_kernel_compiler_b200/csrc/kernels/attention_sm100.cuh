@@ -23,9 +23,10 @@
 //               by two threads in warps w and w+4 (same lane quadrant), one per half of the
 //               128 key columns: tcgen05.ld of its 64 scores, half-row max, the two halves'
 //               maxima exchanged through shared memory (one 64-arrival mbarrier per warp pair,
-//               one phase per key block, so the wait stays bounded), lazy rescale, p = 2^(s*c - m) (c = scale * log2 e), the
-//               half-row sum, 64 P values -> its 32 P columns in TMEM; at the end the two
-//               half sums are combined and each thread stores its 32 columns of O / l.
+//               one phase per key block, so the wait stays bounded), lazy rescale,
+//               p = 2^(s*c - m) (c = scale * log2 e), the half-row sum, 64 P values -> its 32
+//               P columns in TMEM; at the end the two half sums are combined and each thread
+//               stores its 32 columns of O / l.
 // Two threads per row gives 16 softmax warps (4 per SM sub-partition), enough independent
 // work to keep the MUFU busy through the TMEM-load and row-max phases of the other warps.
 // Lazy rescale: the running max m moves only when a block's max exceeds it by more than
@@ -39,8 +40,6 @@
 #include "gemm_sm100.cuh"
 
 namespace tja {
-using namespace tjg;
-
 using namespace tjg;
 
 TJ_DEV void tma_load_4d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int c1, int c2, int c3) {
