@@ -24,9 +24,10 @@ LOG2E = 1.4426950408889634
 # Softmax tuning: EMU of every 16 exponential pairs on the FMA pipe (polynomial) instead of
 # MUFU; DESYNC staggers the two query tiles by one key block; STAGES is the depth of the
 # K/V ring; SPEC starts a block's exponentials with the current row max (speculation, redone
-# when the max moved past the rescale threshold).
+# when the max moved past the rescale threshold); ALT makes the two query tiles take turns on the
+# MUFU (exponential phases alternate).
 # ``TENSORJIT_B200_ATTN="EMU=4,DESYNC=1"`` overrides.
-ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3, "SPEC": 0}
+ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3, "SPEC": 0, "ALT": 1}
 
 
 def attention_knobs() -> dict:
@@ -90,6 +91,7 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     L.append(f"  static constexpr int EMU = {kn['EMU']};")
     L.append(f"  static constexpr bool DESYNC = {'true' if kn['DESYNC'] else 'false'};")
     L.append(f"  static constexpr bool SPEC = {'true' if kn['SPEC'] else 'false'};")
+    L.append(f"  static constexpr bool ALT = {'true' if kn['ALT'] else 'false'};")
     c = float(a["scale"]) * LOG2E
     L.append(f"  static constexpr float C = {c!r}f;")
     tmaps = []
@@ -128,8 +130,8 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     q_bytes, kv_bytes = BM * d * esz, BN * d * esz
     # + half-row maxima (2 parities x 2 tiles x 2 halves x 128 f32) and sums (2 x 2 x 128 f32)
     # + mbarriers (q_full, k/v_full and kv_empty per stage, s_full/s_free/p_ready/o_done/drain
-    # per tile, 8 half-row exchange barriers) + TMEM slot and abort flag
-    smem = 1024 + 2 * q_bytes + STAGES * 2 * kv_bytes + 4096 + 2048 + (19 + 3 * STAGES) * 8 + 8
+    # per tile, 8 half-row exchange barriers, 2 turn tokens) + TMEM slot and abort flag
+    smem = 1024 + 2 * q_bytes + STAGES * 2 * kv_bytes + 4096 + 2048 + (21 + 3 * STAGES) * 8 + 8
     args = [("node", n) for n in ins] + [("node", out_node), ("status", None)]
     flops = 2.0 * bh_total * sq * sk * (d + dv)
     nbytes = sum(n.nbytes for n in ins) + out_node.nbytes

@@ -218,6 +218,7 @@ TJ_DEV void tmem_st16_wait(uint32_t taddr, const uint32_t (&v)[16]) {
 //   static constexpr int SQ, SK, D, DV, STAGES, QR, KR, VR (tensor-map ranks);
 //   static constexpr int EMU (exponentials of every 16 column pairs computed by ex2_poly, 0..16);
 //   static constexpr bool DESYNC (tile 1 starts one key block behind tile 0);
+//   static constexpr bool ALT (the two tiles' exponential phases alternate, one mbarrier token each);
 //   static constexpr bool SPEC (exponentials with the current row max while the block's max is
 //   exchanged; recomputed when it moved by more than the rescale threshold);
 //   static constexpr long BATCH;  static constexpr bool BF16;  static constexpr float C (scale * log2 e, > 0);
@@ -264,7 +265,8 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
   uint64_t* o_done = p_ready + 2;        // [2]
   uint64_t* drain = o_done + 2;          // [2]
   uint64_t* xbar = drain + 2;            // [2 tiles x 4 lane quadrants]: half-row exchange
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 8);
+  uint64_t* turn = xbar + 8;             // [2] (ALT): tile t may start its exponentials
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -287,6 +289,8 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
       mbar_init(smem_u32(&drain[t]), 1);
     }
     for (int i = 0; i < 8; ++i) mbar_init(smem_u32(&xbar[i]), 64);
+    mbar_init(smem_u32(&turn[0]), SM_THREADS);
+    mbar_init(smem_u32(&turn[1]), SM_THREADS);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch(&prm.tm[0]);
@@ -412,7 +416,9 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
       const float* other_max = xmax + (t * 2 + (h ^ 1)) * BM + r;
       float m = 0.0f, l = 0.0f;
       bool ok = true;
-      if (Cfg::DESYNC && t == 1) {
+      static_assert(!(Cfg::ALT && Cfg::SPEC), "ALT and SPEC are exclusive");
+      const bool alt = Cfg::ALT && ntiles == 2;
+      if (Cfg::DESYNC && !alt && t == 1) {
         // start tile 1 one key block behind tile 0
         ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&p_ready[0]), 0, abort_flag, status, kernel_id * 16 + 11));
       }
@@ -482,6 +488,16 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
             m = mblk;
             rescale = true;
           }
+          // ALT: the two tiles take turns on the MUFU, so one tile's exponentials overlap the
+          // other's TMEM load / row max / exchange instead of both contending at once
+          if (alt && (t == 1 || j > 0)) {
+            const bool w = mbar_wait(smem_u32(&turn[t]), (t == 1 ? j : j - 1) & 1, abort_flag, status,
+                                     kernel_id * 16 + 13);
+            if (!__all_sync(0xffffffffu, w)) {
+              ok = false;
+              break;
+            }
+          }
           exp_pairs<0, T, Cfg::EMU>(x, Cfg::C, m, pk, l0, l1);
           if (!wait_prev_pv()) {
             ok = false;
@@ -489,6 +505,7 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
           }
           tmem_st16_wait(tP, pk);
           exp_pairs<16, T, Cfg::EMU>(x, Cfg::C, m, pk, l0, l1);
+          if (alt) mbar_arrive(smem_u32(&turn[t ^ 1]));
           tmem_st16_wait(tP + 16, pk);
         } else {
           // speculative: the exponentials use the current m while the half-row max is
