@@ -5,8 +5,10 @@ tiles with a roofline-style cost model, times the top-k and persists the winner;
 its CUDA backend ignores it (fixed 64x64x16 tiles, ``cuda_backend.py:556-557``).
 Here the same three steps run over the sm_100a space:
 
-* candidates: accumulator tile 128 x BN with BN in {64, 128, 256}, the number of
-  shared-memory stages that fit in ~200 KB, and the L2 raster group GROUP_M;
+* candidates: accumulator tile 128 x BN with BN in {32, 64, 128, 256}, or 256 x BN
+  (BN in {128, 256}) on a CTA pair (``cta_group::2``: two SMs share one MMA stream and
+  each loads half of B), the number of shared-memory stages that fit in ~200 KB, and
+  the L2 raster group GROUP_M;
 * cost model: tensor time at the tile's MMA shape efficiency + wave
   quantisation over 148 SMs + the epilogue's HBM traffic;
 * timing: ``autotune_plan`` compiles the top-k candidates and times them with
@@ -16,6 +18,7 @@ Here the same three steps run over the sm_100a space:
   (consulted after the local store, before the cost model).
 
     python -m mlir_gpu_kernel_compiler_b200.autotune plan.json [...] [--out tuned_tiles.json]
+    python -m mlir_gpu_kernel_compiler_b200.autotune --compare M N K --tile 256:4:16:0 --tile 256:5:16:1
 """
 from __future__ import annotations
 
@@ -48,9 +51,9 @@ SMEM_BUDGET = 232448 - 1024 - STAGING - 256
 
 def candidates(N: int, b_mn_major: bool) -> list[TileConfig]:
     out = []
-    # CTA-pair (cta_group::2) tiles are correct but measured ~1.8x slower than single-CTA
-    # 128 x 256 tiles on B200 (cfg3: 1.52 ms vs 0.83 ms); they are searched only on request.
-    pairs = (False, True) if os.environ.get("TENSORJIT_B200_PAIR") == "1" else (False,)
+    # CTA-pair (cta_group::2) 256-row tiles need a K-major B; TENSORJIT_B200_PAIR=0 leaves
+    # them out of the search
+    pairs = (False,) if os.environ.get("TENSORJIT_B200_PAIR") == "0" else (False, True)
     for pair in pairs:
         if pair and b_mn_major:
             continue
@@ -77,7 +80,7 @@ def cost_model(cfg: TileConfig, M: int, N: int, K: int, batch: int) -> float:
     tiles = batch * m_tiles * n_tiles
     waves = math.ceil(tiles / (NUM_SMS // 2 if cfg.PAIR else NUM_SMS))
     # MMA issue efficiency per tile: wider N amortises the A operand and the per-k overheads
-    eff = {256: 1.0, 128: 0.93, 64: 0.8, 32: 0.6}[cfg.BN]
+    eff = {256: 1.0, 128: 0.85, 64: 0.75, 32: 0.55}[cfg.BN]
     # work per wave in units of a full 128 x 256 x K tile per SM
     tile_work = (128 * cfg.BN * K) / (128 * 256 * max(K, 1))
     t = waves * tile_work / eff
@@ -246,9 +249,7 @@ def tiles_for_plan(plan) -> dict:
                 out[idx] = cfg.as_dict()
             continue
         if env:
-            parts = [int(x) for x in env.split(":")]
-            cfg = TileConfig(parts[0], parts[1], parts[2] if len(parts) > 2 else 16,
-                             bool(parts[3]) if len(parts) > 3 else False)
+            cfg = parse_tile(env)
             if cfg.PAIR and not tb:
                 cfg = TileConfig(cfg.BN, cfg.STAGES, cfg.GROUP_M, False)
         else:
@@ -257,16 +258,165 @@ def tiles_for_plan(plan) -> dict:
     return out
 
 
+def parse_tile(s: str) -> TileConfig:
+    """``BN:STAGES[:GROUP_M[:PAIR]]`` (the ``TENSORJIT_B200_TILE`` syntax)."""
+    parts = [int(x) for x in s.split(":")]
+    return TileConfig(parts[0], parts[1], parts[2] if len(parts) > 2 else 16, bool(parts[3]) if len(parts) > 3 else False)
+
+
+def plain_gemm_plan(M: int, N: int, K: int, dtype: str = "bf16"):
+    """A one-kernel plan ``y[M, N] = a[M, K] @ b[N, K]^T`` with no epilogue: the bare
+    tcgen05 GEMM, for comparing tiles with a library GEMM on identical operands."""
+    from .plan import PProgram
+
+    nodes = [{"id": 0, "op": "input", "name": "a", "inputs": [], "shape": [M, K], "dtype": dtype, "attrs": {}},
+             {"id": 1, "op": "input", "name": "b", "inputs": [], "shape": [N, K], "dtype": dtype, "attrs": {}},
+             {"id": 2, "op": "matmul", "name": "y", "inputs": [0, 1], "shape": [M, N], "dtype": dtype,
+              "attrs": {"trans_b": True}}]
+    return PProgram.from_dict({
+        "format": "tensorjit-plan/1", "name": f"gemm_{M}x{N}x{K}_{dtype}", "nodes": nodes, "inputs": [0, 1],
+        "outputs": [2], "aliases": {}, "meta": {"dtype": dtype},
+        "kernels": [{"kind": "matmul", "nodes": [2], "anchor": 2, "inputs": [0, 1], "outputs": [2],
+                     "iter_shape": [M, N]}]})
+
+
+def compare_with_library(M: int, N: int, K: int, tiles: list[TileConfig], rounds: int = 4, seconds: float = 1.0,
+                         dtype: str = "bf16", device: str = "cuda") -> dict:
+    """Time the bare GEMM with each tile and torch's library GEMM (``F.linear``, cuBLAS) on
+    the same operands.  The arms take turns (order reversed every round) for ``rounds``
+    rounds of about ``seconds`` each, so drift of temperature and power-capped clocks
+    reaches every arm alike; the median SM clock and board power over each arm's rounds
+    are sampled through NVML.  ``rounds=0`` runs every arm twice, untimed (a short
+    command to profile).  Returns {arm: {"ms", "tflops", "sm_mhz", "watts"}}."""
+    import statistics
+    import time
+
+    import torch
+
+    from .program import TORCH_DTYPE, B200Program
+
+    dt = TORCH_DTYPE[dtype]
+    g = torch.Generator(device=device).manual_seed(1)
+    a = torch.randn((M, K), generator=g, device=device).to(dt)
+    b = (torch.randn((N, K), generator=g, device=device) * 0.02).to(dt)
+    out = torch.empty((M, N), dtype=dt, device=device)
+    arms = {}
+    for cfg in tiles:
+        prog = B200Program(plain_gemm_plan(M, N, K, dtype), device=device, use_graph=False,
+                           tiles={0: cfg.as_dict()})
+        arms[f"{cfg.BN}:{cfg.STAGES}:{cfg.GROUP_M}:{int(cfg.PAIR)}"] = prog
+
+    def run(name, iters):
+        if name == "library":
+            for _ in range(iters):
+                torch.nn.functional.linear(a, b)
+        else:
+            for _ in range(iters):
+                arms[name].run_into([a, b], [out])
+
+    names = list(arms) + ["library"]
+    if rounds <= 0:
+        for n in names:
+            run(n, 2)
+        torch.cuda.synchronize()
+        for prog in arms.values():
+            prog.check()
+        return {}
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    run(names[0], 2)
+    ev0.record()
+    run(names[0], 3)
+    ev1.record()
+    torch.cuda.synchronize()
+    iters = max(3, int(seconds * 1000 / max(ev0.elapsed_time(ev1) / 3, 1e-3)))
+    samples = []
+    sampler = _PowerSampler(torch.cuda.current_device(), samples)
+    res = {n: [] for n in names}
+    with sampler:
+        for r in range(rounds):
+            for n in (names if r % 2 == 0 else names[::-1]):
+                run(n, 1)
+                torch.cuda.synchronize()
+                t0 = time.time()
+                ev0.record()
+                run(n, iters)
+                ev1.record()
+                torch.cuda.synchronize()
+                t1 = time.time()
+                sel = [s for s in samples if t0 <= s[0] <= t1]
+                res[n].append((ev0.elapsed_time(ev1) / iters, statistics.median(s[1] for s in sel) if sel else None,
+                               statistics.median(s[2] for s in sel) if sel else None))
+    for prog in arms.values():
+        prog.check()
+    summary = {}
+    for n, v in res.items():
+        ms = statistics.median(x[0] for x in v)
+        clk = [x[1] for x in v if x[1] is not None]
+        pw = [x[2] for x in v if x[2] is not None]
+        summary[n] = {"ms": ms, "tflops": 2.0 * M * N * K / ms / 1e9,
+                      "sm_mhz": statistics.median(clk) if clk else None, "watts": statistics.median(pw) if pw else None}
+    return summary
+
+
+class _PowerSampler:
+    """(time, SM MHz, board W) every ~5 ms from NVML while the ``with`` block runs."""
+
+    def __init__(self, index: int, out: list):
+        self.index, self.out, self._stop, self._t = index, out, threading.Event(), None
+
+    def _run(self):
+        import time
+
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+        except Exception:
+            return
+        try:
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            while not self._stop.is_set():
+                self.out.append((time.time(), pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                 pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0))
+                self._stop.wait(0.005)
+        finally:
+            pynvml.nvmlShutdown()
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+
 def main(argv=None):
     import argparse
 
     from .plan import PProgram
 
     ap = argparse.ArgumentParser(description="time tcgen05 GEMM tile candidates for plans on the GPU")
-    ap.add_argument("plans", nargs="+")
+    ap.add_argument("plans", nargs="*")
     ap.add_argument("--top-k", type=int, default=6)
     ap.add_argument("--out", default=None, help="also merge the winners into this JSON file")
+    ap.add_argument("--compare", type=int, nargs=3, metavar=("M", "N", "K"), default=None,
+                    help="time the bare GEMM of this shape with each --tile against the library GEMM")
+    ap.add_argument("--tile", action="append", default=[], help="BN:STAGES[:GROUP_M[:PAIR]] (repeatable)")
+    ap.add_argument("--rounds", type=int, default=4)
+    ap.add_argument("--dtype", default="bf16", choices=["bf16", "f16"])
     a = ap.parse_args(argv)
+    if a.compare:
+        M, N, K = a.compare
+        tiles = [parse_tile(t) for t in a.tile] or [pick(M, N, K, 1, False)]
+        res = compare_with_library(M, N, K, tiles, rounds=a.rounds, dtype=a.dtype)
+        for n, r in res.items():
+            print(f"{M}x{N}x{K} {n:12s} {r['ms']:.4f} ms  {r['tflops']:7.1f} TFLOP/s  "
+                  f"SM {r['sm_mhz']} MHz  {r['watts']} W")
+        if a.rounds <= 0:
+            print("ran every arm twice")
+        return
     allres = {}
     for p in a.plans:
         print(p)

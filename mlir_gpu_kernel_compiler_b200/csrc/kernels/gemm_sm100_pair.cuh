@@ -9,8 +9,11 @@
 //   single-CTA kernel for the same tile width, which is what lets BN = 256 run 6 stages deep.
 //
 // Synchronisation (all waits bounded; TJ_WAIT_NS):
-//   full[s]    leader only, 2 arrivals: each CTA's producer arrive.expect_tx's its own bytes
-//              on the leader's barrier and its TMA loads (.cta_group::2) complete there.
+//   full[s]    leader only, 1 arrival: the leader's producer arrive.expect_tx's the bytes of
+//              both CTAs on its own barrier; each CTA's TMA loads (.cta_group::2) complete
+//              there.  The peer's producer only issues loads: a remote arrive with
+//              release.cluster semantics on every k-block serialised each iteration behind
+//              the previous loads (about 0.8 us per k-block).
 //   empty[s]   in both CTAs; the leader's tcgen05.commit multicasts to both (mask 0b11).
 //   tfull[b]   in both CTAs; commit multicast after the last k-block of a tile.
 //   tempty[b]  leader only, 2 x EPI_WARPS arrivals (one elected lane per epilogue warp of
@@ -43,16 +46,6 @@ TJ_DEV void mbar_expect_tx_remote(uint32_t cluster_addr, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_addr),
                "r"(bytes)
                : "memory");
-}
-TJ_DEV bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
 }
 TJ_DEV void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
@@ -173,7 +166,7 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(smem_u32(&full[s]), 2);
+      mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -217,7 +210,7 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
             break;
           }
           const uint32_t leader_full = mapa_shared(smem_u32(&full[stage]), 0);
-          mbar_expect_tx_remote(leader_full, STAGE_BYTES);
+          if (rank == 0) mbar_expect_tx(smem_u32(&full[stage]), 2 * STAGE_BYTES);
           tma_load_2d_pair(smem_u32(sA + stage * A_BYTES), tmA, leader_full, kb * BK, a_row);
           tma_load_2d_pair(smem_u32(sB + stage * B_BYTES), tmB, leader_full, kb * BK, b_row);
           if (++stage == STAGES) {

@@ -132,6 +132,26 @@ def test_autotune_space_and_cost_model():
     assert set(tiles) == {1, 2}
 
 
+def test_pair_tiles_in_search_space_and_plain_gemm_plan(monkeypatch):
+    from mlir_gpu_kernel_compiler_b200 import autotune as AT
+
+    assert any(c.PAIR for c in AT.candidates(16384, False))
+    assert not any(c.PAIR for c in AT.candidates(16384, True))      # N-major B: one CTA only
+    monkeypatch.setenv("TENSORJIT_B200_PAIR", "0")
+    assert not any(c.PAIR for c in AT.candidates(16384, False))
+    monkeypatch.delenv("TENSORJIT_B200_PAIR")
+    assert AT.parse_tile("256:5:16:1") == AT.TileConfig(256, 5, 16, True)
+    assert AT.parse_tile("128:6") == AT.TileConfig(128, 6, 16, False)
+    plan = AT.plain_gemm_plan(512, 1024, 256)
+    ks = generate(plan, tiles={0: AT.parse_tile("256:5:16:1").as_dict()})
+    assert [k.family for k in ks] == ["gemm_tc"]
+    assert ks[0].cluster == (2, 1, 1) and ks[0].info["pair"] and ks[0].info["stages"] == 5
+    assert ks[0].grid[0] == 2 * (512 // 256) * (1024 // 256)
+    # shared memory of the deepest pair pipeline stays under the 227 KB opt-in limit
+    deep = generate(AT.plain_gemm_plan(8192, 16384, 4096), tiles={0: AT.parse_tile("256:6:16:1").as_dict()})[0]
+    assert deep.smem <= 232448
+
+
 def test_output_pool_reuses_only_dropped_buffers():
     """tests/test_backends.py:190-206 semantics, on host tensors."""
     import torch
