@@ -374,13 +374,14 @@ def run_b200(a) -> None:
 
 # dram read+write bytes per launch of the dominant kernel, from the committed ncu summaries
 # (profiles/*.md); cfg5's full-size launch is too large to capture, so its figure is the
-# 16384-row slice's (profiles/gemm_traffic_cfg5_cfg1.md) scaled by the 8x rows it processes
-# (x, h and the per-row-group weight re-reads all grow in proportion to the rows)
+# 16384-row slice's (profiles/gemm_traffic_cfg5_cfg1.md, captured with the single-CTA tile the
+# full size runs) scaled by the 8x rows it processes (x, h and the per-row-group weight re-reads
+# all grow in proportion to the rows)
 TRAFFIC: dict = {
     ("cfg1", "tj_matmul_1"): 22.1e6,
     ("cfg1", "tj_matmul_2"): 31.5e6,
     ("cfg2", "tj_row_0"): 365.4e6,
-    ("cfg3", "tj_matmul_0"): 1132.0e6,
+    ("cfg3", "tj_matmul_0"): 1097.4e6,
     ("cfg4", "tj_attention_2"): 116.7e6,
     ("cfg5", "tj_matmul_1"): 8 * 1727.9e6,
 }
