@@ -138,7 +138,7 @@ def compile_cubin(source: str, name: str = "kernel", extra_flags: tuple = ()) ->
         if r.returncode != 0:
             raise BuildError(f"nvcc failed for {name}:\n{r.stderr[-4000:]}\n--- source ---\n{source[:6000]}")
         data = tmp.read_bytes()
-        part = d / f"{key}.{os.getpid()}.tmp"
+        part = d / f"{key}.{os.getpid()}.{threading.get_ident()}.tmp"
         part.write_bytes(data)
         os.replace(part, out)
         (d / f"{key}.cu").write_text(source)
@@ -149,12 +149,17 @@ def compile_cubins(sources: list[tuple[str, str]], extra_flags: tuple = ()) -> l
     """Compile ``[(name, source), ...]`` in parallel; returns the cubin images in order."""
     if not sources:
         return []
-    workers = max(1, min(len(sources), os.cpu_count() or 4, 16))
+    unique: dict[str, str] = {}            # each distinct source is compiled once
+    for n, s in sources:
+        unique.setdefault(s, n)
+    workers = max(1, min(len(unique), os.cpu_count() or 4, 16))
     if workers == 1:
-        return [compile_cubin(s, n, extra_flags) for n, s in sources]
-    with ThreadPoolExecutor(max_workers=workers) as ex:
-        futs = [ex.submit(compile_cubin, s, n, extra_flags) for n, s in sources]
-        return [f.result() for f in futs]
+        done = {s: compile_cubin(s, n, extra_flags) for s, n in unique.items()}
+    else:
+        with ThreadPoolExecutor(max_workers=workers) as ex:
+            futs = {s: ex.submit(compile_cubin, s, n, extra_flags) for s, n in unique.items()}
+            done = {s: f.result() for s, f in futs.items()}
+    return [done[s] for _, s in sources]
 
 
 def build_runtime(force: bool = False) -> Path:

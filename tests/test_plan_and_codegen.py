@@ -337,22 +337,46 @@ def test_gemms_sharing_a_become_one_launch():
 
 def test_fast_gelu_for_half_precision_outputs_tracks_erf_gelu():
     """numpy float32 restatement of tj_gelu_fast (csrc/kernels/tj_common.cuh) against the
-    exact erf GELU: the error stays far below half an ulp of bf16 (2^-9 relative)."""
+    exact erf GELU: relative error below half an ulp of bf16 (2^-9) wherever the output is
+    not negligible, the negative tail included; saturation to x / -0 for large |x|."""
     import math
 
-    x = np.linspace(-8.0, 8.0, 40001).astype(np.float32)
-    z = np.minimum(np.abs(x) * np.float32(0.70710678118654752), np.float32(4.0))
-    t = np.float32(1.0) / (np.float32(0.3275911) * z + np.float32(1.0))
-    poly = ((((np.float32(1.061405429) * t - np.float32(1.453152027)) * t + np.float32(1.421413741)) * t
-             - np.float32(0.284496736)) * t + np.float32(0.254829592))
-    e = np.float32(1.0) - poly * t * np.exp(-z * z)
-    y = np.float32(0.5) * x * (np.float32(1.0) + np.copysign(e, x))
+    c = [np.float32(v) for v in (2.2976467609405518, 0.10939675569534302, -0.0014235572889447212,
+                                 1.303200679103611e-05)]
+
+    def gelu_fast(x):
+        x = x.astype(np.float32)
+        y = x * x
+        p = ((c[3] * y + c[2]) * y + c[1]) * y + c[0]
+        with np.errstate(over="ignore"):
+            return (x / (np.float32(1.0) + np.exp2(-(x * p)))).astype(np.float32)
+
+    x = np.linspace(-12.0, 12.0, 60001).astype(np.float32)
+    y = gelu_fast(x).astype(np.float64)
     ref = np.array([0.5 * v * (1.0 + math.erf(v / math.sqrt(2.0))) for v in x.astype(np.float64)])
-    assert np.abs(y - ref).max() < 1e-6
-    # relative error (where 1 + erf cancels for x < -3 the absolute error dominates)
-    err = np.abs(y - ref) / np.maximum(np.abs(ref), 1e-2)
-    assert err.max() < 1e-4
+    assert np.abs(y - ref).max() < 1.7e-4
+    big = np.abs(ref) > 1e-6
+    assert (np.abs(y - ref)[big] / np.abs(ref[big])).max() < 1.4e-3 < 2.0 ** -9
+    # the exponent polynomial is increasing, so Phi is monotone and saturates correctly
+    xs = np.linspace(0.0, 40.0, 100001).astype(np.float32)
+    g = xs * (((c[3] * xs * xs + c[2]) * xs * xs + c[1]) * xs * xs + c[0])
+    assert np.all(np.diff(g) > 0)
+    assert list(gelu_fast(np.array([-1e30, -50.0, 50.0, 1e30], np.float32))) == [0.0, 0.0, 50.0, 1e30]
     # used only where every stored value is half precision
     from mlir_gpu_kernel_compiler_b200.codegen.common import EXPR, EXPR_FAST
 
     assert "fast" in EXPR_FAST["gelu"] and "erff" not in EXPR_FAST["gelu"] and EXPR["gelu"] == "tj_gelu({0})"
+
+
+def test_compile_batch_with_repeated_source(tmp_path, monkeypatch):
+    """A batch naming one kernel source twice (the fused and the plan-as-given program often
+    share kernels) compiles it once; both entries get the same cubin, the cache holds no
+    temporary files."""
+    from mlir_gpu_kernel_compiler_b200 import toolchain as TC
+
+    monkeypatch.setenv("TENSORJIT_B200_CACHE_DIR", str(tmp_path))
+    src = 'extern "C" __global__ void tj_probe(float* p) { p[threadIdx.x] += 1.0f; }\n'
+    a, b, c = TC.compile_cubins([("x", src), ("y", src), ("z", src.replace("1.0f", "2.0f"))])
+    assert a == b and a[:4] == b"\x7fELF" and c != a
+    suffixes = [p.suffix for p in tmp_path.iterdir()]
+    assert suffixes.count(".cubin") == 2 and ".tmp" not in suffixes
