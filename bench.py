@@ -304,7 +304,7 @@ def run_b200(a) -> None:
         roof = {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
                 "kernel": ks.symbol, "ms": kms[dom],
                 "peak_kind": "copy bandwidth, " + ("of measured" if pk["source"] == "measured" else "of fallback")}
-    roof["traffic"] = TRAFFIC.get((a.config, ks.symbol))
+    roof["traffic"] = traffic_per_launch(a.config, ks)
     per_kernel = [{"kernel": k.symbol, "family": k.family, "ms": round(m, 4),
                    "rate": round((k.info["flops"] / (m * 1e-3) / 1e12) if _tensor_family(k.family)
                                  else (k.info["bytes"] / (m * 1e-3) / 1e9), 1) if m > 0 else None,
@@ -373,18 +373,31 @@ def run_b200(a) -> None:
 
 
 # dram read+write bytes per launch of the dominant kernel, from the committed ncu summaries
-# (profiles/*.md); cfg5's full-size launch is too large to capture, so its figure is the
-# 16384-row slice's (profiles/gemm_traffic_cfg5_cfg1.md, captured with the single-CTA tile the
-# full size runs) scaled by the 8x rows it processes (x, h and the per-row-group weight re-reads
-# all grow in proportion to the rows)
+# (profiles/*.md)
 TRAFFIC: dict = {
     ("cfg1", "tj_matmul_1"): 22.1e6,
     ("cfg1", "tj_matmul_2"): 31.5e6,
     ("cfg2", "tj_row_0"): 365.4e6,
     ("cfg3", "tj_matmul_0"): 1097.4e6,
     ("cfg4", "tj_attention_2"): 116.7e6,
-    ("cfg5", "tj_matmul_1"): 8 * 1727.9e6,
 }
+# cfg5's launches (131072 rows at one GPU, 131072 / N per rank) are too large to capture, so
+# its GEMMs were captured on 16384-row programs (profiles/gemm_traffic_cfg5_cfg1.md), once per
+# tile kind (single CTA / CTA pair); a launch of M rows moves M / 16384 times those bytes (x, h
+# and the per-row-group weight re-reads all grow in proportion to the rows)
+CFG5_TRAFFIC_16K: dict = {
+    ("tj_matmul_1", False): 1727.9e6,
+    ("tj_matmul_2", False): 2822.8e6,
+    ("tj_matmul_1", True): 1555.1e6,
+    ("tj_matmul_2", True): 3272.9e6,
+}
+
+
+def traffic_per_launch(config: str, ks):
+    if config == "cfg5":
+        per = CFG5_TRAFFIC_16K.get((ks.symbol, bool(ks.info.get("pair"))))
+        return per * ks.info["M"] / 16384 if per is not None and "M" in ks.info else None
+    return TRAFFIC.get((config, ks.symbol))
 
 
 def main():
