@@ -34,7 +34,7 @@ def generate(plan: PProgram, tiles: dict | None = None, prefix: str = "tj") -> l
         elif k.kind == "attention":
             ks = gen_attention(k, sym, idx)
         elif k.kind == "matmul_multi":
-            ks = gen_gemm_multi(k, sym, idx)
+            ks = gen_gemm_multi(k, sym, idx, (tiles or {}).get(idx))
         elif k.kind == "matmul":
             if tc_eligible(k) and x3_eligible(k):
                 parts = gen_matmul_tc_x3(k, sym, idx, (tiles or {}).get(idx))

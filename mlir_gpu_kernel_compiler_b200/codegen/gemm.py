@@ -641,7 +641,10 @@ def gen_gemm_multi(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = 
     dt = a.dtype
     M, K = a.shape
     BN = 256
-    STAGES = (tile or {}).get("STAGES", 4)
+    # CTA pair (256 x 256 tiles, each CTA loading half of every B tile) unless the tile says
+    # otherwise or there is less than one 256-row tile
+    pair = bool((tile or {}).get("PAIR", os.environ.get("TENSORJIT_B200_PAIR") != "0")) and M >= 256
+    STAGES = (tile or {}).get("STAGES", 6 if pair else 4)
     GROUP_M = (tile or {}).get("GROUP_M", 16)
     ins = [a] + [p_[0] for p_ in parts]
     outs = [p_[1] for p_ in parts]
@@ -650,7 +653,8 @@ def gen_gemm_multi(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = 
     seg_tiles = [p_[2] // BN for p_ in parts]
     starts = [sum(seg_tiles[:g]) for g in range(len(parts))]
     col0 = [sum(p_[2] for p_ in parts[:g]) for g in range(len(parts))]
-    L = [HEADER, '#include "gemm_sm100.cuh"', params_struct(status_idx + 1, 1 + len(parts))]
+    L = [HEADER, '#include "gemm_sm100_pair.cuh"' if pair else '#include "gemm_sm100.cuh"',
+         params_struct(status_idx + 1, 1 + len(parts))]
     L.append("struct Cfg {")
     L.append(f"  static constexpr int BN = {BN}, STAGES = {STAGES}, M = {M}, N = {N}, K = {K}, GROUP_M = {GROUP_M};")
     L.append(f"  static constexpr int EPI_WARPS = 8, KSPLIT = 1, NSEG = {len(parts)};")
@@ -678,20 +682,25 @@ def gen_gemm_multi(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = 
         L.append("    }")
     L.append("  }")
     L.append("};")
-    smem = 1024 + STAGES * (128 * 128 + BN * 128) + (2 * STAGES + 6) * 8 + 16
+    b_rows = BN // 2 if pair else BN
+    smem = 1024 + STAGES * (128 * 128 + b_rows * 128) + (2 * STAGES + 6) * 8 + 16
+    if smem > 232448:
+        raise ValueError(f"shared-A GEMM STAGES={STAGES} pair={pair} needs {smem} B of shared memory")
     L.append(f'extern "C" __global__ void __launch_bounds__(320, 1) {symbol}(const __grid_constant__ Params prm) {{')
-    L.append(f"  tjg::gemm_sm100<Cfg>(prm, (int*)prm.p[{status_idx}], {kernel_id});")
+    L.append(f"  tjg::{'gemm_sm100_pair' if pair else 'gemm_sm100'}<Cfg>(prm, (int*)prm.p[{status_idx}], {kernel_id});")
     L.append("}")
     esz = ITEM[dt]
     tmaps = [TMapSpec(arg=0, dtype=dt, dims=[K, M], strides=[K * esz], box=[128 // esz, 128], swizzle=3)]
     for g, (bnode, _o, ng) in enumerate(parts):
-        tmaps.append(TMapSpec(arg=1 + g, dtype=dt, dims=[K, ng], strides=[K * esz], box=[128 // esz, BN], swizzle=3))
-    num_tiles = ((M + 127) // 128) * (N // BN)
+        tmaps.append(TMapSpec(arg=1 + g, dtype=dt, dims=[K, ng], strides=[K * esz], box=[128 // esz, b_rows],
+                              swizzle=3))
+    num_tiles = ((M + (255 if pair else 127)) // (256 if pair else 128)) * (N // BN)
+    grid = 2 * min(num_tiles, NUM_SMS // 2) if pair else min(num_tiles, NUM_SMS)
     args = [("node", n) for n in ins] + [("node", o) for o in outs] + [("status", None)]
-    ks = KernelSource(symbol, "gemm_tc", "\n".join(L), (min(num_tiles, NUM_SMS), 1, 1), (320, 1, 1), args, smem=smem,
-                      tmaps=tmaps,
+    ks = KernelSource(symbol, "gemm_tc", "\n".join(L), (grid, 1, 1), (320, 1, 1), args, smem=smem,
+                      tmaps=tmaps, cluster=(2, 1, 1) if pair else (1, 1, 1),
                       info={"M": M, "N": N, "K": K, "batch": 1, "BN": BN, "stages": STAGES, "tma_store": False,
-                            "epi_warps": 8, "pair": False, "tf32x3": False, "ksplit": 1, "segments": len(parts),
+                            "epi_warps": 8, "pair": pair, "tf32x3": False, "ksplit": 1, "segments": len(parts),
                             "flops": 2.0 * M * N * K, "tiles": num_tiles,
                             "bytes": sum(n.nbytes for n in ins) + sum(o.nbytes for o in outs)})
     ks.finalize_params()

@@ -177,7 +177,7 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch(tmA);
-    tma_prefetch(tmB);
+    for (int g = 0; g < Cfg::NSEG; ++g) tma_prefetch(&prm.tm[1 + g]);
     if constexpr (Cfg::TMA_STORE) tma_prefetch(&prm.tm[2]);
   }
   if (warp == 1) {
@@ -202,7 +202,15 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
         long ab, bb;
         Cfg::batch_map(b, ab, bb);
         const int a_row = static_cast<int>(ab * Cfg::M + static_cast<long>(mt) * BM + rank * 128);
-        const int b_row = static_cast<int>(bb * Cfg::N + static_cast<long>(nt) * BN + rank * BN_HALF);
+        int b_row = static_cast<int>(bb * Cfg::N + static_cast<long>(nt) * BN + rank * BN_HALF);
+        const CUtensorMap* tmBt = tmB;
+        if constexpr (Cfg::NSEG > 1) {
+          // several B operands side by side along N (GEMMs sharing A): segment g owns the
+          // column tiles from seg_tile0(g), its B rows start at 0 in its own tensor map
+          const int g = Cfg::segment(nt);
+          tmBt = &prm.tm[1 + g];
+          b_row = (nt - Cfg::seg_tile0(g)) * BN + static_cast<int>(rank) * BN_HALF;
+        }
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait_pair(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, peer_abort, status,
                               kernel_id * 16 + 1)) {
@@ -212,7 +220,7 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
           const uint32_t leader_full = mapa_shared(smem_u32(&full[stage]), 0);
           if (rank == 0) mbar_expect_tx(smem_u32(&full[stage]), 2 * STAGE_BYTES);
           tma_load_2d_pair(smem_u32(sA + stage * A_BYTES), tmA, leader_full, kb * BK, a_row);
-          tma_load_2d_pair(smem_u32(sB + stage * B_BYTES), tmB, leader_full, kb * BK, b_row);
+          tma_load_2d_pair(smem_u32(sB + stage * B_BYTES), tmBt, leader_full, kb * BK, b_row);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;

@@ -326,6 +326,12 @@ def test_gemms_sharing_a_become_one_launch():
     ks = generate(p)[0]
     assert ks.family == "gemm_tc" and ks.info["segments"] == 3 and ks.info["N"] == 1024
     assert len(ks.tmaps) == 4 and [t.dims[1] for t in ks.tmaps[1:]] == [256, 512, 256]
+    # on a CTA pair (M = 300 >= one 256-row tile): each CTA loads 128 rows of every B tile;
+    # 2 row tiles x 4 column tiles of 256 -> 8 clusters
+    assert ks.info["pair"] and ks.cluster == (2, 1, 1) and ks.grid[0] == 16
+    assert all(t.box[1] == 128 for t in ks.tmaps[1:]) and "gemm_sm100_pair<Cfg>" in ks.source
+    single = generate(p, tiles={0: {"BN": 256, "STAGES": 4, "GROUP_M": 16, "PAIR": False}})[0]
+    assert not single.info["pair"] and single.cluster == (1, 1, 1) and single.tmaps[1].box[1] == 256
     # cfg4: the q, k, v projections (same LayerNorm output) -> one launch; 16 plan kernels -> 8
     p4 = fuse(FX.load_plan("cfg4"))
     assert [k.kind for k in p4.kernels] == ["row", "matmul_multi", "attention", "matmul", "row", "matmul",
