@@ -195,6 +195,11 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+#ifdef TJ_TEST_STALL_FIRST_LOAD
+      // Failure-path test build only: neither CTA fills its first stage, so the leader's MMA
+      // wait on it must run out, raise both CTAs' abort flags and report through the status.
+      bool stall_pending = true;
+#endif
       for (long t = cluster_id; t < num_tiles && ok; t += num_clusters) {
         long b;
         int mt, nt;
@@ -217,6 +222,16 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
             ok = false;
             break;
           }
+#ifdef TJ_TEST_STALL_FIRST_LOAD
+          if (stall_pending) {
+            stall_pending = false;
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
+#endif
           const uint32_t leader_full = mapa_shared(smem_u32(&full[stage]), 0);
           if (rank == 0) mbar_expect_tx(smem_u32(&full[stage]), 2 * STAGE_BYTES);
           tma_load_2d_pair(smem_u32(sA + stage * A_BYTES), tmA, leader_full, kb * BK, a_row);

@@ -45,6 +45,34 @@ def test_bounded_wait_timeout_reports_status_and_context_survives():
     assert normwise_error(y, ref) <= 2e-2
 
 
+def test_cta_pair_bounded_wait_timeout_reports_status_and_context_survives():
+    """The same for the CTA-pair GEMM (cta_group::2, 2-CTA clusters): neither CTA fills its
+    first stage, so the leader's MMA wait runs out; the abort reaches the peer CTA through
+    distributed shared memory, both leave through the final cluster barrier after a bounded
+    grace period for their copies, and the context stays usable."""
+    from mlir_gpu_kernel_compiler_b200 import B200Program
+    from mlir_gpu_kernel_compiler_b200.autotune import parse_tile, plain_gemm_plan
+
+    plan = plain_gemm_plan(512, 512, 512)
+    tiles = {0: parse_tile("256:4:16:1").as_dict()}
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.randn((512, 512), generator=g, device="cuda").to(torch.bfloat16)
+    b = (torch.randn((512, 512), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    bad = B200Program(plan, use_graph=False, tiles=tiles,
+                      nvcc_flags=("-DTJ_TEST_STALL_FIRST_LOAD", "-DTJ_WAIT_NS=20000000ull"))
+    assert bad.kernel_sources[0].cluster == (2, 1, 1) and bad.kernel_sources[0].info["pair"]
+    out = torch.empty((512, 512), dtype=torch.bfloat16, device="cuda")
+    bad.run_into([a, b], [out])
+    torch.cuda.synchronize()
+    code, where = bad.native.check_status()
+    assert code == 1 and where // 16 == 0 and where % 16 in (1, 2, 3, 4)
+    bad.close()
+    good = B200Program(plan, tiles=tiles)
+    y = good(a, b)[0]
+    good.check()
+    assert normwise_error(y, a.float() @ b.float().T) <= 1e-2
+
+
 def test_attention_bounded_wait_timeout_reports_status_and_context_survives():
     """The same for the fused attention kernel: its test build never loads the first K/V
     block, so the MMA warps (and then every other role) must give up, report, drain and
