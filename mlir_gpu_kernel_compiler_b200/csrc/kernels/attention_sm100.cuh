@@ -204,11 +204,22 @@ TJ_DEV void exp_pairs_max(const float (&x)[64], float c, float m, uint32_t (&pk)
 }
 
 // 16 consecutive 32-bit columns of one lane quadrant from registers into TMEM, then wait.
+TJ_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 TJ_DEV void tmem_st16_wait(uint32_t taddr, const uint32_t (&v)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
       "%16};\n"
       "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+// 16 columns from registers into TMEM without waiting (tcgen05.wait::st before the data is used)
+TJ_DEV void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16};" ::"r"(taddr),
       "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
       "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
       : "memory");
@@ -503,10 +514,14 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
             ok = false;
             break;
           }
-          tmem_st16_wait(tP, pk);
-          exp_pairs<16, T, Cfg::EMU>(x, Cfg::C, m, pk, l0, l1);
+          tmem_st16(tP, pk);
+          // hand the MUFU to the other tile half-way: its warps wake up while this tile's
+          // second half still keeps the unit busy
           if (alt) mbar_arrive(smem_u32(&turn[t ^ 1]));
-          tmem_st16_wait(tP + 16, pk);
+          uint32_t pk2[16];
+          exp_pairs<16, T, Cfg::EMU>(x, Cfg::C, m, pk2, l0, l1);
+          tmem_st16(tP + 16, pk2);
+          tmem_wait_st();
         } else {
           // speculative: the exponentials use the current m while the half-row max is
           // tracked alongside; when the exchanged row max moved by more than the threshold
