@@ -101,9 +101,9 @@ TJ_DEV float tj_sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x
 // (Lawson-weighted least squares for minimal maximum error; the degree-3 logistic fit of
 // Bowling et al. 2009, "A logistic approximation to the cumulative normal distribution",
 // is the starting form).  Since sigma(g) has a relative error of about |g - logit Phi|, the GELU
-// relative error stays <= 1.4e-3 wherever |GELU(x)| > 1e-6 (absolute <= 1.7e-4), below half an
-// ulp of bf16, including the negative tail; the polynomial is monotone, so large |x| give x or
-// -0.  Ten instructions (two MUFU) instead of erff's or an erf approximation's twenty; the
+// relative error is <= 3.8e-4 for x >= 0 and <= 1.4e-3 for x < 0 (below half an ulp of bf16,
+// the negative tail included; absolute error <= 1.7e-4); the polynomial is monotone, so large
+// |x| give x or -0.  Ten instructions (two MUFU) instead of erff's or an erf approximation's twenty; the
 // epilogues of GEMMs with half-precision outputs are issue-bound on this.
 TJ_DEV float tj_gelu_fast(float x) {
   const float y = x * x;

@@ -363,6 +363,8 @@ def test_fast_gelu_for_half_precision_outputs_tracks_erf_gelu():
     assert np.abs(y - ref).max() < 1.7e-4
     big = np.abs(ref) > 1e-6
     assert (np.abs(y - ref)[big] / np.abs(ref[big])).max() < 1.4e-3 < 2.0 ** -9
+    pos = x > 0                                            # below half an f16 ulp there
+    assert (np.abs(y - ref)[pos] / np.abs(ref[pos])).max() < 3.9e-4 < 2.0 ** -11
     # the exponent polynomial is increasing, so Phi is monotone and saturates correctly
     xs = np.linspace(0.0, 40.0, 100001).astype(np.float32)
     g = xs * (((c[3] * xs * xs + c[2]) * xs * xs + c[1]) * xs * xs + c[0])
