@@ -7,6 +7,8 @@
 //   each CTA's TMEM receives its own 128 accumulator rows x BN columns.  Per SM and k-block
 //   this loads 16 KB of A + BN*64 B of B for 128 x BN x 64 MACs: half the B traffic of the
 //   single-CTA kernel for the same tile width, which is what lets BN = 256 run 6 stages deep.
+//   With Cfg::NSEG > 1 (GEMMs sharing A) each column tile reads its own segment's B map, as
+//   in the single-CTA kernel.
 //
 // Synchronisation (all waits bounded; TJ_WAIT_NS):
 //   full[s]    leader only, 1 arrival: the leader's producer arrive.expect_tx's the bytes of
