@@ -378,7 +378,7 @@ TRAFFIC: dict = {
     ("cfg1", "tj_matmul_1"): 22.1e6,
     ("cfg1", "tj_matmul_2"): 31.5e6,
     ("cfg2", "tj_row_0"): 365.4e6,
-    ("cfg3", "tj_matmul_0"): 1097.4e6,
+    ("cfg3", "tj_matmul_0"): 1068.0e6,
     ("cfg4", "tj_attention_2"): 116.7e6,
 }
 # cfg5's launches (131072 rows at one GPU, 131072 / N per rank) are too large to capture, so
