@@ -379,7 +379,7 @@ TRAFFIC: dict = {
     ("cfg1", "tj_matmul_2"): 31.5e6,
     ("cfg2", "tj_row_0"): 365.4e6,
     ("cfg3", "tj_matmul_0"): 1068.0e6,
-    ("cfg4", "tj_attention_2"): 116.7e6,
+    ("cfg4", "tj_attention_2"): 114.1e6,
 }
 # cfg5's launches (131072 rows at one GPU, 131072 / N per rank) are too large to capture, so
 # its GEMMs were captured on 16384-row programs (profiles/gemm_traffic_cfg5_cfg1.md), once per
