@@ -176,18 +176,19 @@ def candidate_sources(plan, top_k: int = 6) -> list[tuple[str, str]]:
     """(name, CUDA source) of every candidate ``autotune_plan`` would time, so they can be
     compiled ahead of time (nvcc runs on the CPU)."""
     from .codegen import generate
-    from .codegen.gemm import _mm_dims, tc_eligible
+    from .codegen.gemm import _mm_dims, gemm_form
 
     out = []
     for k in plan.kernels:
-        if k.kind != "matmul" or not tc_eligible(k):
+        form = gemm_form(k) if k.kind == "matmul" else None
+        if form is None or form.mode != "f16":
             continue
         mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
         batch = math.prod(out_shape[:-2]) if len(out_shape) > 2 else 1
         sub = _single_kernel_plan(plan, k)
-        for cfg in _ranked_candidates(M, N, K, batch, not tb, top_k):
-            ks = generate(sub, tiles={0: cfg.as_dict()})[0]
-            out.append((ks.symbol, ks.source))
+        for cfg in _ranked_candidates(M, N, K, batch, form.b_mn, top_k):
+            for ks in generate(sub, tiles={0: cfg.as_dict()}):
+                out.append((ks.symbol, ks.source))
     return out
 
 
@@ -196,18 +197,19 @@ def autotune_plan(plan, device="cuda", top_k: int = 6, iters: int = 10, verbose:
     device and record the fastest (CUDA events around the kernel, inputs random)."""
     import torch
 
-    from .codegen.gemm import _mm_dims, tc_eligible
+    from .codegen.gemm import _mm_dims, gemm_form
     from .program import TORCH_DTYPE, B200Program
 
     results = {}
     for idx, k in enumerate(plan.kernels):
-        if k.kind != "matmul" or not tc_eligible(k):
+        form = gemm_form(k) if k.kind == "matmul" else None
+        if form is None or form.mode != "f16":
             continue
         mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
         batch = math.prod(out_shape[:-2]) if len(out_shape) > 2 else 1
         sub = _single_kernel_plan(plan, k)
         ins = [torch.randn(n.shape, device=device).mul_(0.05).to(TORCH_DTYPE[n.dtype]) for n in sub.inputs]
-        cands = _ranked_candidates(M, N, K, batch, not tb, top_k)
+        cands = _ranked_candidates(M, N, K, batch, form.b_mn, top_k)
         best, best_ms = None, float("inf")
         for cfg in cands:
             try:
@@ -226,34 +228,35 @@ def autotune_plan(plan, device="cuda", top_k: int = 6, iters: int = 10, verbose:
             if ms < best_ms:
                 best, best_ms = cfg, ms
         if best is not None:
-            record(M, N, K, batch, a.dtype, not tb, best, best_ms)
-            results[key(M, N, K, batch, a.dtype, not tb)] = {"config": best.as_dict(), "ms": best_ms}
+            record(M, N, K, batch, a.dtype, form.b_mn, best, best_ms)
+            results[key(M, N, K, batch, a.dtype, form.b_mn)] = {"config": best.as_dict(), "ms": best_ms}
     return results
 
 
 def tiles_for_plan(plan) -> dict:
     """Tile choice per matmul kernel index: a stored (timed) winner if there is one,
     else the cost-model pick.  ``TENSORJIT_B200_TILE=BN:STAGES[:GROUP_M[:PAIR]]`` overrides."""
-    from .codegen.gemm import _mm_dims, tc_eligible
+    from .codegen.gemm import _mm_dims, gemm_form
 
     env = os.environ.get("TENSORJIT_B200_TILE")
     out = {}
     for idx, k in enumerate(plan.kernels):
-        if k.kind != "matmul" or not tc_eligible(k):
+        form = gemm_form(k) if k.kind == "matmul" else None
+        if form is None or form.mode == "empty":
             continue
         mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
         batch = math.prod(out_shape[:-2]) if len(out_shape) > 2 else 1
-        if a.dtype == "f32":      # 3xTF32 kernels: a timed entry, else the generator's own choice
+        if form.mode == "x3":     # 3xTF32 kernels: a timed entry, else the generator's own choice
             cfg = lookup_any(M, N, K, batch, a.dtype, not tb)
             if cfg is not None:
                 out[idx] = cfg.as_dict()
             continue
         if env:
             cfg = parse_tile(env)
-            if cfg.PAIR and not tb:
+            if cfg.PAIR and form.b_mn:
                 cfg = TileConfig(cfg.BN, cfg.STAGES, cfg.GROUP_M, False)
         else:
-            cfg = lookup_any(M, N, K, batch, a.dtype, not tb) or pick(M, N, K, batch, not tb)
+            cfg = lookup_any(M, N, K, batch, a.dtype, form.b_mn) or pick(M, N, K, batch, form.b_mn)
         out[idx] = cfg.as_dict()
     return out
 

@@ -3,9 +3,9 @@
 ``generate`` walks the fused plan in order and dispatches on ``Kernel.kind``
 exactly like the reference backend (``tensorjit/backends/cuda_backend.py:437-456``):
 elementwise/copy -> vectorised grid-stride kernel, row -> staged row kernel,
-reduce -> row kernel with one stage, matmul -> tcgen05 GEMM (bf16/f16), the
-3xTF32 tcgen05 path (f32 with a K-major B: operand split pre-passes + GEMM), or the
-SIMT GEMM (everything else); ``attention`` (the matmul -> softmax -> matmul chain
+reduce -> row kernel with one stage, matmul -> the tcgen05 GEMM (bf16/f16 operands
+read in place or after a pack pre-pass; everything else as 3xTF32 after an operand split
+pre-pass; see ``gemm.gemm_form``); ``attention`` (the matmul -> softmax -> matmul chain
 ``fuse.py`` folds into one kernel) -> the fused tcgen05 attention kernel; ``matmul_multi``
 (GEMMs sharing A, also from ``fuse.py``) -> one tcgen05 GEMM over the concatenated N.  A plan kernel can therefore become several launches;
 ``KernelSource.info["index"]`` names the plan kernel each launch belongs to.
@@ -16,7 +16,7 @@ from ..plan import PProgram
 from .attention import gen_attention
 from .common import KernelSource
 from .ewise import gen_elementwise
-from .gemm import gen_gemm_multi, gen_gemm_simt, gen_gemm_tc, gen_matmul_tc_x3, tc_eligible, x3_eligible
+from .gemm import gen_gemm_multi, gen_matmul
 from .row import gen_row
 
 
@@ -36,17 +36,12 @@ def generate(plan: PProgram, tiles: dict | None = None, prefix: str = "tj") -> l
         elif k.kind == "matmul_multi":
             ks = gen_gemm_multi(k, sym, idx, (tiles or {}).get(idx))
         elif k.kind == "matmul":
-            if tc_eligible(k) and x3_eligible(k):
-                parts = gen_matmul_tc_x3(k, sym, idx, (tiles or {}).get(idx))
-                for ks in parts:
-                    ks.info["kind"] = k.kind
-                    ks.info["index"] = idx
-                out += parts
-                continue
-            if tc_eligible(k):
-                ks = gen_gemm_tc(k, sym, idx, (tiles or {}).get(idx))
-            else:
-                ks = gen_gemm_simt(k, sym)
+            parts = gen_matmul(k, sym, idx, (tiles or {}).get(idx))
+            for ks in parts:
+                ks.info["kind"] = k.kind
+                ks.info["index"] = idx
+            out += parts
+            continue
         else:
             raise NotImplementedError(f"kernel kind {k.kind!r} is not supported by the b200 backend")
         ks.info["kind"] = k.kind

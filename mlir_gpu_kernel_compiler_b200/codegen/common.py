@@ -112,7 +112,7 @@ TMAP_DTYPE = {"f16": 6, "f32": 7, "bf16": 9}
 @dataclass
 class KernelSource:
     symbol: str
-    family: str                         # ewise | copy | row | gemm_simt | gemm_tc
+    family: str                         # ewise | copy | row | split | gemm_tc | attention
     source: str
     grid: tuple
     block: tuple

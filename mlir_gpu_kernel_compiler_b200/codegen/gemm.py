@@ -6,17 +6,21 @@ when ``trans_b``), batch dims broadcast with stride 0 (``cuda_backend.py:330-340
 accumulate in f32, then evaluate every epilogue node per output element in f32
 and store each escaping node in its dtype.
 
-Implementations:
+Every matmul with work runs on the persistent tcgen05 kernel of
+``csrc/kernels/gemm_sm100.cuh`` (TMA -> 128B-swizzled smem -> tcgen05.mma -> TMEM ->
+epilogue), in one of two operand forms (``gemm_form``):
 
-* ``tc``   bf16/f16 operands: the persistent tcgen05 kernel of
-  ``csrc/kernels/gemm_sm100.cuh`` (TMA -> 128B-swizzled smem -> tcgen05.mma ->
-  TMEM -> epilogue).  Needs K % 8 == 0 (16-byte TMA row pitch) and, for an
-  N-major B, N % 8 == 0.
-* ``tc`` in 3xTF32 mode for f32 operands with a K-major B and K % 4 == 0: one launch
-  splits A and B into TF32 hi / lo copies, the same kernel issues hi*hi + hi*lo + lo*hi;
-  a GEMM with too few output tiles is split over K (partial sums + a finalize launch).
-* ``simt`` every other case (odd pitches, N-major f32 B, K == 0): a 64x64 tile,
-  4x4 register micro-tile FFMA kernel with bounds checks, f32 accumulate.
+* ``f16``  A and B both bf16 or both f16: kind::f16 MMAs.  The tensor maps read the
+  operands in place when their rows have a 16-byte pitch (K % 8 == 0, and N % 8 == 0 for an
+  N-major B); otherwise one pack launch first copies them into K-major buffers with a padded
+  pitch in the program's workspace.
+* ``x3``   anything else (f32, mixed or integer operands): 3xTF32, A_hi·B_hi + A_hi·B_lo +
+  A_lo·B_hi with kind::tf32.  One launch splits both operands into TF32 hi / lo copies in the
+  workspace (transposing an N-major B and padding K to a 16-byte pitch on the way); a GEMM
+  with too few output tiles is split over K (partial sums + a finalize launch).
+
+A matmul with K == 0 or no output element is its epilogue over a zero accumulator (one
+grid-stride launch, or none).
 """
 from __future__ import annotations
 
@@ -48,30 +52,183 @@ def _batch_strides(t: PNode, batch_shape: tuple) -> tuple:
     return tuple(st)
 
 
+class GemmForm:
+    """How a plan matmul maps onto the tcgen05 kernel.
+
+    ``mode``   "f16" (kind::f16 on bf16/f16 operands), "x3" (3xTF32) or "empty" (K == 0 or
+               no output element: epilogue only).
+    ``pack_a`` / ``pack_b``  the operand is first copied into the workspace (K-major, row pitch
+               ``pitch`` elements); for "x3" both are always split into hi / lo copies.
+    ``b_mn``   the kernel reads B N-major (an unpacked B of a plan matmul without ``trans_b``).
+    """
+
+    def __init__(self, mode: str, pack_a: bool, pack_b: bool, pitch: int, b_mn: bool):
+        self.mode, self.pack_a, self.pack_b, self.pitch, self.b_mn = mode, pack_a, pack_b, pitch, b_mn
+
+    def __repr__(self):
+        return f"GemmForm({self.mode}, pack_a={self.pack_a}, pack_b={self.pack_b}, pitch={self.pitch}, b_mn={self.b_mn})"
+
+
+def gemm_form(k: PKernel) -> GemmForm:
+    mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
+    if K == 0 or M == 0 or N == 0 or prod(out_shape[:-2]) == 0:
+        return GemmForm("empty", False, False, 0, False)
+    if a.dtype in ("bf16", "f16") and b.dtype == a.dtype:
+        pitch = (K + 7) // 8 * 8
+        pack_a = K % 8 != 0
+        pack_b = K % 8 != 0 or (not tb and N % 8 != 0)
+        return GemmForm("f16", pack_a, pack_b, pitch, not tb and not pack_b)
+    return GemmForm("x3", True, True, (K + 3) // 4 * 4, False)
+
+
 def tc_eligible(k: PKernel) -> bool:
-    mm, a, b, tb, M, N, K, _ = _mm_dims(k)
-    if os.environ.get("TENSORJIT_B200_NO_TCGEN05") == "1":
-        return False
-    if M == 0 or N == 0:
-        return False
-    if a.dtype == "f32" and b.dtype == "f32":
-        return x3_eligible(k)
-    if a.dtype not in ("bf16", "f16") or b.dtype != a.dtype:
-        return False
-    if K < 8 or K % 8 != 0:
-        return False
-    if not tb and N % 8 != 0:
-        return False
-    return True
+    """The matmul runs the tcgen05 GEMM (every matmul with work does)."""
+    return gemm_form(k).mode != "empty"
 
 
 def x3_eligible(k: PKernel) -> bool:
-    """f32 operands on the tensor cores as 3xTF32: needs a K-major B (nn.Linear weights)
-    and a 16-byte row pitch (K % 4 == 0)."""
-    mm, a, b, tb, M, N, K, _ = _mm_dims(k)
-    if os.environ.get("TENSORJIT_B200_NO_TF32X3") == "1":
-        return False
-    return a.dtype == b.dtype == "f32" and tb and K >= 4 and K % 4 == 0 and M > 0 and N > 0
+    """The matmul runs as 3xTF32 (f32, mixed or integer operands)."""
+    return gemm_form(k).mode == "x3"
+
+
+def gen_pack_operands(symbol: str, segments: list[dict]) -> KernelSource:
+    """Copy GEMM operands into K-major buffers with a 16-byte row pitch in the workspace, for
+    the cases the tensor maps cannot read in place: a K that breaks the 16-byte row pitch, an
+    N-major B whose N does, and every operand of a 3xTF32 GEMM that is not an f32 K-major
+    matrix with K % 4 == 0.  One launch packs all operands of a GEMM.  A CTA moves a 32 x 32
+    tile (32 rows x 32 of K) through shared memory, so an N-major source is read along its rows
+    and the K-major destination is written along K, both in 128-byte lines.  Columns K up to
+    the pitch are written as zeros, so the kernel's k-blocks past K add nothing.
+
+    ``segments``: dicts with ``src`` (argument ref), ``src_dtype``, ``mats`` (matrices),
+    ``rows`` (M for A, N for B), ``K``, ``pitch``, ``k_major`` (source rows run along K),
+    ``split`` (write TF32 hi / lo pairs: hi = the value with its 13 low mantissa bits cleared,
+    lo = value - hi, both exact in f32), ``dst_dtype`` and the workspace offsets ``hi`` / ``lo``
+    (``lo`` unused without ``split``)."""
+    tiles = []
+    for sg in segments:
+        kt = (sg["pitch"] + 31) // 32
+        rt = (sg["rows"] + 31) // 32
+        tiles.append(sg["mats"] * rt * kt)
+    total = sum(tiles)
+    nptr = 3 * len(segments)
+    L = [HEADER, params_struct(nptr, 0),
+         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{',
+         "  __shared__ float tile[32][33];",
+         "  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;",
+         f"  for (long t = blockIdx.x; t < {total}L; t += gridDim.x) {{",
+         "    long u = t;"]
+    acc = 0
+    for j, (sg, nt) in enumerate(zip(segments, tiles)):
+        R, K, P = sg["rows"], sg["K"], sg["pitch"]
+        kt = (P + 31) // 32
+        rt = (R + 31) // 32
+        st, dt = CTYPE[sg["src_dtype"]], CTYPE[sg["dst_dtype"]]
+        cond = f"u < {acc + nt}L" if j < len(segments) - 1 else "true"
+        L.append(f"    {'if' if j == 0 else 'else if'} ({cond}) {{")
+        L.append(f"      u -= {acc}L;")
+        L.append(f"      const long kt = u % {kt}L, rt = (u / {kt}L) % {rt}L, mat = u / {kt * rt}L;")
+        L.append(f"      const {st}* __restrict__ src = (const {st}*)prm.p[{3 * j}] + mat * {R * K}L;")
+        L.append("      for (int y = ty; y < 32; y += 8) {")
+        if sg["k_major"]:
+            L.append("        const long r = rt * 32 + y, kk = kt * 32 + tx;")
+            L.append(f"        tile[y][tx] = (r < {R}L && kk < {K}L) ? tj_f32(src[r * {K}L + kk]) : 0.0f;")
+        else:   # source [K, rows]: consecutive threads read consecutive rows
+            L.append("        const long kk = kt * 32 + y, r = rt * 32 + tx;")
+            L.append(f"        tile[tx][y] = (r < {R}L && kk < {K}L) ? tj_f32(src[kk * {R}L + r]) : 0.0f;")
+        L.append("      }")
+        L.append("      __syncthreads();")
+        L.append("      for (int y = ty; y < 32; y += 8) {")
+        L.append("        const long r = rt * 32 + y, kk = kt * 32 + tx;")
+        L.append(f"        if (r < {R}L && kk < {P}L) {{")
+        L.append("          const float v = tile[y][tx];")
+        L.append(f"          const long o = (mat * {R}L + r) * {P}L + kk;")
+        if sg["split"]:
+            L.append("          const float h = __uint_as_float(__float_as_uint(v) & 0xffffe000u);")
+            L.append(f"          ((float*)prm.p[{3 * j + 1}])[o] = h;")
+            L.append(f"          ((float*)prm.p[{3 * j + 2}])[o] = v - h;")
+        else:
+            L.append(f"          (({dt}*)prm.p[{3 * j + 1}])[o] = tj_from<{dt}>(v);")
+        L.append("        }")
+        L.append("      }")
+        L.append("      __syncthreads();")
+        L.append("    }")
+        acc += nt
+    L += ["  }", "}"]
+    args = []
+    nbytes = 0
+    for sg in segments:
+        args += [sg["src"], ("scratch", sg["hi"]), ("scratch", sg.get("lo", sg["hi"]))]
+        n_src = sg["mats"] * sg["rows"] * sg["K"]
+        n_dst = sg["mats"] * sg["rows"] * sg["pitch"]
+        nbytes += n_src * ITEM[sg["src_dtype"]] + n_dst * ITEM[sg["dst_dtype"]] * (2 if sg["split"] else 1)
+    grid = max(1, min(total, NUM_SMS * 8))
+    ks = KernelSource(symbol, "split", "\n".join(L), (grid, 1, 1), (256, 1, 1), args,
+                      info={"bytes": nbytes, "numel": sum(sg["mats"] * sg["rows"] * sg["K"] for sg in segments)})
+    ks.finalize_params()
+    return ks
+
+
+def gen_epilogue_only(k: PKernel, symbol: str) -> KernelSource:
+    """A matmul whose every dot product is empty (K == 0), or which has no output element: the
+    epilogue over a zero accumulator as one grid-stride launch (none when nothing is stored)."""
+    mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
+    ins, outs = list(k.inputs), list(k.outputs)
+    in_index = {n.id: j for j, n in enumerate(ins)}
+    out_index = {o.id: len(ins) + j for j, o in enumerate(outs)}
+    epi = Epilogue(k, in_index, out_index)
+    total = prod(out_shape[:-2]) * M * N
+    L = [HEADER, params_struct(len(ins) + len(outs), 0),
+         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{']
+    L += ["  " + x for x in epi._ptr_lines()]
+    L.append(f"  for (long e = (long)blockIdx.x * 256 + threadIdx.x; e < {total}L; e += (long)gridDim.x * 256) {{")
+    L.append(f"    const long j = e % {max(N, 1)}L, row = e / {max(N, 1)}L, i = row % {max(M, 1)}L, "
+             f"b = row / {max(M, 1)}L;")
+    bl, bidx = epi.batch_index_lines("b")
+    L += ["    " + x for x in bl]
+    L += ["    " + x for x in epi.scalar_element_lines(bidx, "i", "j", "0.0f")]
+    L += ["  }", "}"]
+    grid = min((total + 255) // 256, NUM_SMS * 8) if total else 0
+    ks = KernelSource(symbol, "ewise", "\n".join(L), (grid, 1, 1), (256, 1, 1),
+                      [("node", n) for n in ins] + [("node", o) for o in outs],
+                      info={"bytes": sum(n.nbytes for n in k.inputs if n is not a and n is not b)
+                            + sum(o.nbytes for o in outs), "numel": total, "flops": 0.0})
+    ks.finalize_params()
+    return ks
+
+
+def _operand_segment(node: PNode, rows: int, K: int, pitch: int, k_major: bool, split: bool, dst_dtype: str,
+                     hi: int, lo: int) -> dict:
+    return {"src": ("node", node), "src_dtype": node.dtype, "mats": prod(node.shape[:-2]), "rows": rows, "K": K,
+            "pitch": pitch, "k_major": k_major, "split": split, "dst_dtype": dst_dtype, "hi": hi, "lo": lo}
+
+
+def gen_matmul(k: PKernel, symbol: str, kernel_id: int, tile: dict | None) -> list[KernelSource]:
+    """The launches of one plan matmul: [pack or split pre-pass], tcgen05 GEMM, [split-K
+    finalize]; or the epilogue alone when there is nothing to multiply."""
+    form = gemm_form(k)
+    if form.mode == "empty":
+        return [gen_epilogue_only(k, symbol)]
+    if form.mode == "x3":
+        return gen_matmul_tc_x3(k, symbol, kernel_id, tile)
+    if not (form.pack_a or form.pack_b):
+        return [gen_gemm_tc(k, symbol, kernel_id, tile)]
+    mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
+    P = form.pitch
+    a_off = 0
+    b_off = _align(prod(a.shape[:-2]) * M * P * ITEM[a.dtype]) if form.pack_a else 0
+    ws = b_off + (_align(prod(b.shape[:-2]) * N * P * ITEM[b.dtype]) if form.pack_b else 0)
+    segs = []
+    if form.pack_a:
+        segs.append(_operand_segment(a, M, K, P, True, False, a.dtype, a_off, a_off))
+    if form.pack_b:
+        segs.append(_operand_segment(b, N, K, P, tb, False, b.dtype, b_off, b_off))
+    pk = gen_pack_operands(f"{symbol}_pack", segs)
+    g = gen_gemm_tc(k, symbol, kernel_id, tile, packed={"a": a_off if form.pack_a else None,
+                                                        "b": b_off if form.pack_b else None, "pitch": P})
+    for ks in (pk, g):
+        ks.info["scratch_bytes"] = ws
+    return [pk, g]
 
 
 def gen_split_tf32(symbol: str, segments: list[tuple]) -> KernelSource:
@@ -164,15 +321,24 @@ def gen_matmul_tc_x3(k: PKernel, symbol: str, kernel_id: int, tile: dict | None)
     the GEMM is split over K into partial sums in the workspace and a finalize launch adds
     them and applies the epilogue."""
     mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
-    a_hi, a_lo = 0, _align(a.nbytes)
-    b_hi = a_lo + _align(a.nbytes)
-    b_lo = b_hi + _align(b.nbytes)
-    part = b_lo + _align(b.nbytes)
+    P = (K + 3) // 4 * 4
+    a_bytes = prod(a.shape[:-2]) * M * P * 4
+    b_bytes = prod(b.shape[:-2]) * N * P * 4
+    a_hi, a_lo = 0, _align(a_bytes)
+    b_hi = a_lo + _align(a_bytes)
+    b_lo = b_hi + _align(b_bytes)
+    part = b_lo + _align(b_bytes)
     batch = prod(out_shape[:-2])
     BN, ksplit = x3_tile(M, N, K, batch, tile)
     tile = dict(tile or {"STAGES": 4, "GROUP_M": 16}, BN=BN)
     ws = part + (_align(ksplit * batch * M * N * 4) if ksplit > 1 else 0)
-    sp = gen_split_tf32(f"{symbol}_split", [(a.numel, ("node", a), a_hi, a_lo), (b.numel, ("node", b), b_hi, b_lo)])
+    if a.dtype == b.dtype == "f32" and tb and K % 4 == 0:
+        # both operands already K-major f32 with a 16-byte pitch: the vectorised split
+        sp = gen_split_tf32(f"{symbol}_split", [(a.numel, ("node", a), a_hi, a_lo),
+                                                (b.numel, ("node", b), b_hi, b_lo)])
+    else:
+        sp = gen_pack_operands(f"{symbol}_split", [_operand_segment(a, M, K, P, True, True, "f32", a_hi, a_lo),
+                                                   _operand_segment(b, N, K, P, tb, True, "f32", b_hi, b_lo)])
     g = gen_gemm_tc(k, symbol, kernel_id, tile, x3_scratch=(a_hi, b_hi, a_lo, b_lo),
                     ksplit=ksplit, partial_scratch=part)
     parts = [sp, g]
@@ -448,7 +614,12 @@ def choose_tile(M: int, N: int, batch: int, b_mn_major: bool, override: dict | N
 
 
 def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = None,
-                x3_scratch: tuple | None = None, ksplit: int = 1, partial_scratch: int = 0) -> KernelSource:
+                x3_scratch: tuple | None = None, ksplit: int = 1, partial_scratch: int = 0,
+                packed: dict | None = None) -> KernelSource:
+    """The tcgen05 GEMM launch of one plan matmul.  ``x3_scratch`` = workspace offsets of the
+    (A hi, B hi, A lo, B lo) copies of a 3xTF32 GEMM; ``packed`` = {"a": offset | None, "b":
+    offset | None, "pitch": P} for bf16/f16 operands the pack pre-pass copied into the workspace
+    (K-major, row pitch P elements), which the tensor maps then read instead of the plan's."""
     mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
     batch_shape = out_shape[:-2]
     batch = prod(batch_shape)
@@ -456,17 +627,21 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     in_index = {n.id: j for j, n in enumerate(ins)}
     out_index = {o.id: len(ins) + j for j, o in enumerate(outs)}
     x3 = x3_scratch is not None
-    # + status word (+ hi/lo operand copies) (+ the partial sums of a split-K GEMM)
-    nptr = len(ins) + len(outs) + 1 + (4 if x3 else 0) + (1 if ksplit > 1 else 0)
+    pk_a = packed is not None and packed.get("a") is not None
+    pk_b = packed is not None and packed.get("b") is not None
+    # + status word (+ hi/lo operand copies) (+ packed operands) (+ the partial sums of a split-K GEMM)
+    nptr = len(ins) + len(outs) + 1 + (4 if x3 else 0) + int(pk_a) + int(pk_b) + (1 if ksplit > 1 else 0)
     status_idx = len(ins) + len(outs)
     epi = Epilogue(k, in_index, out_index)
-    b_mn = not tb
+    # B is read N-major only in place from a plan matmul without trans_b; the workspace copies
+    # (3xTF32 hi / lo, packed operands) are always K-major
+    b_mn = not (tb or pk_b or x3)
     if x3 and not tile:
         tile = {"BN": x3_tile(M, N, K, batch, None)[0], "STAGES": 4, "GROUP_M": 16}
     BN, STAGES, GROUP_M = choose_tile(M, N, batch, b_mn, tile)
     if x3:
         STAGES = min(STAGES, max(2, (200 * 1024) // (2 * (128 * 128 + BN * 128))))
-    pair = bool(tile and tile.get("PAIR")) and tb and BN in (128, 256) and not x3
+    pair = bool(tile and tile.get("PAIR")) and not b_mn and BN in (128, 256) and not x3
     a_bs = _batch_strides(a, batch_shape)
     b_bs = _batch_strides(b, batch_shape)
     a_mats = prod(a.shape[:-2])
@@ -510,23 +685,29 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     n_tiles = (N + BN - 1) // BN
     num_tiles = batch * m_tiles * n_tiles * ksplit
     grid = 2 * min(num_tiles, NUM_SMS // 2) if pair else min(num_tiles, NUM_SMS)
-    esz = ITEM[a.dtype]
+    op_dt = "f32" if x3 else a.dtype
+    esz = ITEM[op_dt]
     bk = 128 // esz                      # K elements per 128-byte swizzle row
-    a_arg = in_index[a.id] if not x3 else status_idx + 1
-    b_arg = in_index[b.id] if not x3 else status_idx + 2
-    tmA = TMapSpec(arg=a_arg, dtype=a.dtype, dims=[K, a_mats * M], strides=[K * esz], box=[bk, 128], swizzle=3)
-    if tb:
-        tmB = TMapSpec(arg=b_arg, dtype=b.dtype, dims=[K, b_mats * N], strides=[K * esz],
+    # row pitch (elements) of each operand as the tensor maps read it
+    pitch = (K + 3) // 4 * 4 if x3 else (packed["pitch"] if (pk_a or pk_b) else K)
+    a_pitch = pitch if (x3 or pk_a) else K
+    b_pitch = pitch if (x3 or pk_b) else K
+    pk_arg = status_idx + 1
+    a_arg = status_idx + 1 if x3 else (pk_arg if pk_a else in_index[a.id])
+    b_arg = status_idx + 2 if x3 else (pk_arg + int(pk_a) if pk_b else in_index[b.id])
+    tmA = TMapSpec(arg=a_arg, dtype=op_dt, dims=[K, a_mats * M], strides=[a_pitch * esz], box=[bk, 128], swizzle=3)
+    if not b_mn:
+        tmB = TMapSpec(arg=b_arg, dtype=op_dt, dims=[K, b_mats * N], strides=[b_pitch * esz],
                        box=[bk, BN // 2 if pair else BN], swizzle=3)
     else:
-        tmB = TMapSpec(arg=in_index[b.id], dtype=b.dtype, dims=[N, K, b_mats], strides=[N * esz, K * N * esz],
+        tmB = TMapSpec(arg=b_arg, dtype=op_dt, dims=[N, K, b_mats], strides=[N * esz, K * N * esz],
                        box=[64, 64, 1], swizzle=3)
     tmaps = [tmA, tmB]
     if x3:
-        tmaps.append(TMapSpec(arg=status_idx + 3, dtype="f32", dims=[K, a_mats * M], strides=[K * 4], box=[32, 128],
-                              swizzle=3))
-        tmaps.append(TMapSpec(arg=status_idx + 4, dtype="f32", dims=[K, b_mats * N], strides=[K * 4], box=[32, BN],
-                              swizzle=3))
+        tmaps.append(TMapSpec(arg=status_idx + 3, dtype="f32", dims=[K, a_mats * M], strides=[pitch * 4],
+                              box=[32, 128], swizzle=3))
+        tmaps.append(TMapSpec(arg=status_idx + 4, dtype="f32", dims=[K, b_mats * N], strides=[pitch * 4],
+                              box=[32, BN], swizzle=3))
     if tma_store:
         o = outs[0]
         oe = ITEM[o.dtype]
@@ -536,94 +717,18 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     if x3:
         a_hi, b_hi, a_lo, b_lo = x3_scratch
         args += [("scratch", a_hi), ("scratch", b_hi), ("scratch", a_lo), ("scratch", b_lo)]
+    if pk_a:
+        args.append(("scratch", packed["a"]))
+    if pk_b:
+        args.append(("scratch", packed["b"]))
     if ksplit > 1:
         args.append(("scratch", partial_scratch))
     ks = KernelSource(symbol, "gemm_tc", "\n".join(L), (grid, 1, 1), (threads, 1, 1), args, smem=smem,
                       tmaps=tmaps, cluster=(2, 1, 1) if pair else (1, 1, 1),
                       info={"M": M, "N": N, "K": K, "batch": batch, "BN": BN, "stages": STAGES,
                             "tma_store": tma_store, "epi_warps": epi_warps, "pair": pair, "tf32x3": x3,
-                            "ksplit": ksplit,
+                            "ksplit": ksplit, "packed": [x for x, f in (("a", pk_a), ("b", pk_b)) if f],
                             "flops": 2.0 * batch * M * N * K, "tiles": num_tiles,
-                            "bytes": sum(n.nbytes for n in ins) + sum(o.nbytes for o in outs)})
-    ks.finalize_params()
-    return ks
-
-
-# ---------------------------------------------------------------------------
-# SIMT fallback
-# ---------------------------------------------------------------------------
-def gen_gemm_simt(k: PKernel, symbol: str) -> KernelSource:
-    mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
-    batch_shape = out_shape[:-2]
-    batch = prod(batch_shape)
-    ins, outs = list(k.inputs), list(k.outputs)
-    in_index = {n.id: j for j, n in enumerate(ins)}
-    out_index = {o.id: len(ins) + j for j, o in enumerate(outs)}
-    epi = Epilogue(k, in_index, out_index)
-    a_bs = _batch_strides(a, batch_shape)
-    b_bs = _batch_strides(b, batch_shape)
-    ia, ib = in_index[a.id], in_index[b.id]
-    BM_, BN_, BK_ = 64, 64, 16
-    L = [HEADER, params_struct(len(ins) + len(outs), 0)]
-    L.append(f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{')
-    L.append(f"  const {CTYPE[a.dtype]}* __restrict__ A = (const {CTYPE[a.dtype]}*)prm.p[{ia}];")
-    L.append(f"  const {CTYPE[b.dtype]}* __restrict__ B = (const {CTYPE[b.dtype]}*)prm.p[{ib}];")
-    L += ["  " + s for s in epi._ptr_lines()]
-    L.append("  const long bz = blockIdx.z;")
-    bl, bidx = decompose_stmts("bz", batch_shape, "bb") if batch_shape else ([], [])
-    L += ["  " + s for s in bl]
-    L.append(f"  const long aoff = ({offset_expr(bidx, a_bs) if batch_shape else '0L'}) * {M * K}L;")
-    L.append(f"  const long boff = ({offset_expr(bidx, b_bs) if batch_shape else '0L'}) * {N * K}L;")
-    L.append(f"  __shared__ float As[{BK_}][{BM_} + 4];")
-    L.append(f"  __shared__ float Bs[{BK_}][{BN_} + 4];")
-    L.append(f"  const int tid = threadIdx.x, tr = tid / 16, tc = tid % 16;")
-    L.append(f"  const long i0 = (long)blockIdx.y * {BM_}, j0 = (long)blockIdx.x * {BN_};")
-    L.append("  float acc[4][4];")
-    L.append("  #pragma unroll")
-    L.append("  for (int x = 0; x < 4; ++x) for (int y = 0; y < 4; ++y) acc[x][y] = 0.0f;")
-    L.append(f"  for (long k0 = 0; k0 < {K}L; k0 += {BK_}) {{")
-    L.append(f"    for (int t = tid; t < {BM_ * BK_}; t += 256) {{")
-    L.append(f"      const int r = t / {BK_}, c = t % {BK_};")
-    L.append("      const long gi = i0 + r, gk = k0 + c;")
-    L.append(f"      As[c][r] = (gi < {M}L && gk < {K}L) ? tj_f32(A[aoff + gi * {K}L + gk]) : 0.0f;")
-    L.append("    }")
-    L.append(f"    for (int t = tid; t < {BK_ * BN_}; t += 256) {{")
-    if tb:
-        L.append(f"      const int c = t / {BN_}, r = t % {BN_};")
-        L.append("      const long gk = k0 + c, gj = j0 + r;")
-        L.append(f"      Bs[c][r] = (gk < {K}L && gj < {N}L) ? tj_f32(B[boff + gj * {K}L + gk]) : 0.0f;")
-    else:
-        L.append(f"      const int r = t / {BN_}, c = t % {BN_};")
-        L.append("      const long gk = k0 + r, gj = j0 + c;")
-        L.append(f"      Bs[r][c] = (gk < {K}L && gj < {N}L) ? tj_f32(B[boff + gk * {N}L + gj]) : 0.0f;")
-    L.append("    }")
-    L.append("    __syncthreads();")
-    L.append("    #pragma unroll")
-    L.append(f"    for (int kk = 0; kk < {BK_}; ++kk) {{")
-    L.append("      float av[4], bv[4];")
-    L.append("      #pragma unroll")
-    L.append("      for (int x = 0; x < 4; ++x) av[x] = As[kk][tr * 4 + x];")
-    L.append("      #pragma unroll")
-    L.append("      for (int y = 0; y < 4; ++y) bv[y] = Bs[kk][tc * 4 + y];")
-    L.append("      #pragma unroll")
-    L.append("      for (int x = 0; x < 4; ++x) for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(av[x], bv[y], acc[x][y]);")
-    L.append("    }")
-    L.append("    __syncthreads();")
-    L.append("  }")
-    L.append("  #pragma unroll")
-    L.append("  for (int x = 0; x < 4; ++x) {")
-    L.append("    #pragma unroll")
-    L.append("    for (int y = 0; y < 4; ++y) {")
-    L.append("      const long i = i0 + tr * 4 + x, j = j0 + tc * 4 + y;")
-    L.append(f"      if (i < {M}L && j < {N}L) {{")
-    L += ["        " + s for s in epi.scalar_element_lines(bidx, "i", "j", "acc[x][y]")]
-    L.append("      }")
-    L.append("    }")
-    L.append("  }")
-    L.append("}")
-    grid = ((N + BN_ - 1) // BN_, (M + BM_ - 1) // BM_, batch) if M and N and batch else (0, 1, 1)
-    ks = KernelSource(symbol, "gemm_simt", "\n".join(L), grid, (256, 1, 1), [("node", n) for n in ins + outs],
-                      info={"M": M, "N": N, "K": K, "batch": batch, "flops": 2.0 * batch * M * N * K,
                             "bytes": sum(n.nbytes for n in ins) + sum(o.nbytes for o in outs)})
     ks.finalize_params()
     return ks

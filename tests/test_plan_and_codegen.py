@@ -58,16 +58,45 @@ def test_launch_geometry_and_kernel_families():
         assert k.block[0] in (192, 320) and len(k.tmaps) in (2, 3) and k.grid[0] <= 148
 
 
-def test_tensor_core_path_only_for_half_precision_with_aligned_pitch():
-    """tests/test_cuda_backend.py:50-57 analogue: tcgen05 for bf16/f16 when TMA pitches allow."""
-    fam = lambda n: [k.family for k in generate(FX.load_plan(n)) if k.family.startswith("gemm")]
+def test_every_matmul_runs_on_the_tensor_cores():
+    """tests/test_cuda_backend.py:50-57 analogue (which matmuls reach the tensor cores): on B200
+    all of them do.  Operands the tensor maps can read in place go straight to the tcgen05
+    GEMM; a pitch that breaks the 16-byte TMA rule, or f32 / N-major operands on the 3xTF32
+    path, get one pack / split launch first."""
+    fam = lambda n: [k.family for k in generate(FX.load_plan(n)) if k.family in ("gemm_tc", "split")]
     assert fam("cuda_wmma__f16") == ["gemm_tc"]
     assert fam("cuda_wmma__bf16") == ["gemm_tc"]
-    assert fam("cuda_wmma__f32") == ["gemm_tc"]                 # f32, K-major B: 3xTF32
-    assert fam("gemm_tc_nn_batched__f32") == ["gemm_simt"]      # f32 with an N-major B
-    assert fam("matmul_epi_7x13x5__bf16") == ["gemm_simt"]       # K % 8 != 0
-    assert fam("matmul_epi_33x128x65__bf16") == ["gemm_simt"]    # N-major B with N % 8 != 0
-    assert fam("gemm_tc_nn_batched__bf16") == ["gemm_tc"]
+    assert fam("cuda_wmma__f32") == ["split", "gemm_tc"]        # f32, K-major B: 3xTF32
+    assert fam("gemm_tc_nn_batched__f32") == ["split", "gemm_tc"]   # f32 N-major B: transposed by the split
+    assert fam("matmul_epi_7x13x5__bf16") == ["split", "gemm_tc"]   # K % 8 != 0: both packed
+    assert fam("matmul_epi_33x128x65__bf16") == ["split", "gemm_tc"]  # N-major B with N % 8 != 0: B packed
+    assert fam("gemm_tc_nn_batched__bf16") == ["gemm_tc"]       # N-major B read in place
+    for case in FX.cases("case") + FX.cases("config"):
+        for k in generate(FX.load_plan(case)):
+            assert k.family in ("ewise", "copy", "row", "split", "gemm_tc", "attention"), (case, k.family)
+
+
+def test_pack_prepass_layout():
+    """The packed operands are K-major with the padded pitch, and the GEMM's tensor maps read
+    them (not the plan's buffers) with that pitch."""
+    from mlir_gpu_kernel_compiler_b200.codegen.gemm import gemm_form
+
+    p = FX.load_plan("matmul_epi_7x13x5__bf16")          # A[7,13] @ B[13,5]: K = 13
+    mm = [k for k in p.kernels if k.kind == "matmul"][0]
+    f = gemm_form(mm)
+    assert (f.mode, f.pack_a, f.pack_b, f.pitch, f.b_mn) == ("f16", True, True, 16, False)
+    pk, g = generate(p)
+    assert pk.args[1] == ("scratch", 0) and pk.args[4][0] == "scratch"
+    assert pk.info["scratch_bytes"] == g.info["scratch_bytes"] > 0
+    ta, tb = g.tmaps[0], g.tmaps[1]
+    assert ta.dims == [13, 7] and ta.strides == [16 * 2] and tb.dims == [13, 5] and tb.strides == [16 * 2]
+    n_in, n_out = len(mm.inputs), len(mm.outputs)
+    assert g.args[ta.arg] == ("scratch", 0) and g.args[tb.arg] == pk.args[4]
+    assert g.info["packed"] == ["a", "b"]
+    # an N-major f32 B is transposed by the split into K-major hi / lo copies
+    p2 = FX.load_plan("gemm_tc_nn_batched__f32")
+    sp, g2 = generate(p2)
+    assert "tile[tx][y]" in sp.source and g2.info["tf32x3"] and g2.tmaps[1].dims == [192, 6 * 64]
 
 
 def test_vectorised_paths_selected():
