@@ -158,6 +158,15 @@ TJ_API int tj_b200_destroy(void* program);
 TJ_API int tj_b200_linear_f32_noalloc(const float* A, const float* B, float* C, int32_t M, int32_t N, int32_t K,
                                       void* stream);
 
+/* The failure record of tj_b200_linear_f32_noalloc on the current device.  Its GEMM's
+ * waits are bounded: one that runs out makes the kernel give up and leave (code, site) in
+ * status words that, like the scratch array, are static and shared by every call (each call
+ * clears them when it starts).  This waits for `stream`, copies the words back, clears them
+ * and returns TJ_OK with *code = 0 if the calls since the last read finished normally, else
+ * TJ_ERR_DEVICE_STATUS with *code = 1 (wait timeout) and *where = the wait site.  Allocates
+ * nothing.  No counterpart in the reference (its kernels have no bounded waits). */
+TJ_API int tj_b200_linear_f32_noalloc_status(int32_t* code, int32_t* where, void* stream);
+
 /* Message of the last failure on this thread ("" if none). */
 TJ_API const char* tj_b200_last_error(void);
 

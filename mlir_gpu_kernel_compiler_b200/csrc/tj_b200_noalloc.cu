@@ -131,6 +131,11 @@ __global__ void __launch_bounds__(192, 1) noalloc_gemm(const __grid_constant__ N
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+#ifdef TJ_TEST_STALL_FIRST_LOAD
+      // Failure-path test build only: the first stage is never filled, so the MMA warp's
+      // bounded wait on it runs out and the status words report it.
+      bool stall_pending = true;
+#endif
       for (long t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         const int mt = static_cast<int>(t % m_tiles), nt = static_cast<int>(t / m_tiles);
         for (int kb = 0; kb < k_blocks; ++kb) {
@@ -138,6 +143,16 @@ __global__ void __launch_bounds__(192, 1) noalloc_gemm(const __grid_constant__ N
             ok = false;
             break;
           }
+#ifdef TJ_TEST_STALL_FIRST_LOAD
+          if (stall_pending) {
+            stall_pending = false;
+            if (++stage == NA_STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
+#endif
           const uint32_t fb = smem_u32(&full[stage]);
           mbar_expect_tx(fb, NA_STAGE_BYTES);
           uint8_t* a_st = sA + stage * 2 * NA_A_BYTES;
@@ -259,6 +274,7 @@ struct DeviceSetup {
   std::string why;
   float* scratch = nullptr;
   int* status = nullptr;
+  int num_sms = 0;
 };
 DeviceSetup g_setup[TJ_NOALLOC_MAX_DEVICES];
 EncodeFn g_encode = nullptr;
@@ -286,7 +302,28 @@ void setup_device(DeviceSetup& s) {
   if (e != cudaSuccess) {
     s.rc = TJ_ERR_CUDA;
     s.why = std::string("cudaFuncSetAttribute failed: ") + cudaGetErrorString(e);
+    return;
   }
+  int dev = 0;
+  e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess || s.num_sms <= 0) {
+    s.rc = TJ_ERR_CUDA;
+    s.why = std::string("multiprocessor count query failed: ") + cudaGetErrorString(e);
+  }
+}
+
+// The calling thread's device, with its set-up done (first use on a device runs it).
+int current_setup(DeviceSetup** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return na_fail(TJ_ERR_CUDA, cudaGetErrorString(e));
+  if (dev < 0 || dev >= TJ_NOALLOC_MAX_DEVICES) return na_fail(TJ_ERR_INVALID, "device index out of range");
+  DeviceSetup& s = g_setup[dev];
+  std::call_once(s.once, [&] { setup_device(s); });
+  if (s.rc != TJ_OK) return na_fail(s.rc, s.why.c_str());
+  *out = &s;
+  return TJ_OK;
 }
 
 bool encode(CUtensorMap* m, float* base, int rows, int K, int box_rows) {
@@ -312,10 +349,6 @@ extern "C" int tj_b200_linear_f32_noalloc(const float* A, const float* B, float*
                    "be <= 2097152 elements)");
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) & 15)
     return na_fail(TJ_ERR_INVALID, "tj_b200_linear_f32_noalloc: A, B and C must be 16-byte aligned");
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return na_fail(TJ_ERR_CUDA, cudaGetErrorString(e));
-  if (dev < 0 || dev >= TJ_NOALLOC_MAX_DEVICES) return na_fail(TJ_ERR_INVALID, "device index out of range");
   std::call_once(g_encode_once, [] {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -324,9 +357,10 @@ extern "C" int tj_b200_linear_f32_noalloc(const float* A, const float* B, float*
       g_encode = reinterpret_cast<EncodeFn>(fn);
   });
   if (!g_encode) return na_fail(TJ_ERR_NO_DRIVER, "cuTensorMapEncodeTiled is unavailable");
-  DeviceSetup& s = g_setup[dev];
-  std::call_once(s.once, [&] { setup_device(s); });
-  if (s.rc != TJ_OK) return na_fail(s.rc, s.why.c_str());
+  DeviceSetup* sp = nullptr;
+  const int rc = current_setup(&sp);
+  if (rc != TJ_OK) return rc;
+  DeviceSetup& s = *sp;
 
   float* a_hi = s.scratch;
   float* a_lo = s.scratch + TJ_NOALLOC_MAX_OPERAND;
@@ -342,16 +376,41 @@ extern "C" int tj_b200_linear_f32_noalloc(const float* A, const float* B, float*
       !encode(&prm.tm[2], a_lo, M, K, NA_BM) || !encode(&prm.tm[3], b_lo, N, K, NA_BN))
     return na_fail(TJ_ERR_CUDA, "cuTensorMapEncodeTiled failed");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  e = cudaMemsetAsync(s.status, 0, sizeof(int) * 4, st);  // status words start at zero every call
+  cudaError_t e = cudaMemsetAsync(s.status, 0, sizeof(int) * 4, st);  // status words start at zero every call
   if (e != cudaSuccess) return na_fail(TJ_ERR_CUDA, cudaGetErrorString(e));
   const long na4 = static_cast<long>(M) * K / 4, nb4 = static_cast<long>(N) * K / 4;
-  noalloc_split<<<static_cast<int>(std::min<long>((na4 + 255) / 256, 148 * 8)), 256, 0, st>>>(
+  const long split_ctas = 8L * s.num_sms;
+  noalloc_split<<<static_cast<int>(std::min<long>((na4 + 255) / 256, split_ctas)), 256, 0, st>>>(
       reinterpret_cast<const float4*>(A), reinterpret_cast<float4*>(a_hi), reinterpret_cast<float4*>(a_lo), na4);
-  noalloc_split<<<static_cast<int>(std::min<long>((nb4 + 255) / 256, 148 * 8)), 256, 0, st>>>(
+  noalloc_split<<<static_cast<int>(std::min<long>((nb4 + 255) / 256, split_ctas)), 256, 0, st>>>(
       reinterpret_cast<const float4*>(B), reinterpret_cast<float4*>(b_hi), reinterpret_cast<float4*>(b_lo), nb4);
   const long tiles = static_cast<long>((M + NA_BM - 1) / NA_BM) * ((N + NA_BN - 1) / NA_BN);
-  noalloc_gemm<<<static_cast<int>(std::min<long>(tiles, 148)), 192, NA_SMEM, st>>>(prm);
+  noalloc_gemm<<<static_cast<int>(std::min<long>(tiles, s.num_sms)), 192, NA_SMEM, st>>>(prm);
   e = cudaGetLastError();
   if (e != cudaSuccess) return na_fail(TJ_ERR_CUDA, cudaGetErrorString(e));
   return TJ_OK;
+}
+
+// The failure record of the allocation-free GEMM: a bounded wait in it that ran out leaves
+// its (code, site) in the shared status words instead of stopping the GPU.  This waits for
+// `stream`, copies the words back, clears them, and reports code 0 when nothing failed.
+extern "C" int tj_b200_linear_f32_noalloc_status(int32_t* code, int32_t* where, void* stream) {
+  if (!code || !where) return na_fail(TJ_ERR_INVALID, "tj_b200_linear_f32_noalloc_status: NULL pointer");
+  *code = 0;
+  *where = 0;
+  DeviceSetup* sp = nullptr;
+  const int rc = current_setup(&sp);
+  if (rc != TJ_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int words[4] = {0, 0, 0, 0};
+  cudaError_t e = cudaMemcpyAsync(words, sp->status, sizeof(words), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && words[0] != 0) {
+    e = cudaMemsetAsync(sp->status, 0, sizeof(words), st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  }
+  if (e != cudaSuccess) return na_fail(TJ_ERR_CUDA, cudaGetErrorString(e));
+  *code = words[0];
+  *where = words[1];
+  return words[0] != 0 ? TJ_ERR_DEVICE_STATUS : TJ_OK;
 }

@@ -23,6 +23,7 @@ EXPORTS = (
     "tj_b200_program_create", "tj_b200_run", "tj_b200_set_graph", "tj_b200_check_status",
     "tj_b200_program_info", "tj_b200_destroy", "tj_b200_last_error", "tj_b200_abi_version",
     "tj_b200_driver_available", "tj_b200_time_kernels", "tj_b200_linear_f32_noalloc",
+    "tj_b200_linear_f32_noalloc_status",
 )
 
 
@@ -92,6 +93,8 @@ def library(path: str | Path | None = None) -> ctypes.CDLL:
         lib.tj_b200_time_kernels.restype = ctypes.c_int
         lib.tj_b200_linear_f32_noalloc.argtypes = [vp, vp, vp, i32, i32, i32, vp]
         lib.tj_b200_linear_f32_noalloc.restype = ctypes.c_int
+        lib.tj_b200_linear_f32_noalloc_status.argtypes = [ctypes.POINTER(i32), ctypes.POINTER(i32), vp]
+        lib.tj_b200_linear_f32_noalloc_status.restype = ctypes.c_int
         lib.tj_b200_set_graph.argtypes = [vp, i32]
         lib.tj_b200_set_graph.restype = ctypes.c_int
         lib.tj_b200_check_status.argtypes = [vp, ctypes.POINTER(i32), ctypes.POINTER(i32)]

@@ -32,6 +32,10 @@ LIB_PATH = PKG / "_lib" / "libtj_b200.so"
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr", "-Xptxas=-warn-spills"]
 
+# the failure-path test build: the GEMM producers skip their first stage and every bounded
+# wait gives up after 20 ms, so the timeout reporting can be tested without a GPU fault
+STALL_TEST_FLAGS = ("-DTJ_TEST_STALL_FIRST_LOAD", "-DTJ_WAIT_NS=20000000ull")
+
 _lock = threading.Lock()
 
 
@@ -162,26 +166,30 @@ def compile_cubins(sources: list[tuple[str, str]], extra_flags: tuple = ()) -> l
     return [done[s] for _, s in sources]
 
 
-def build_runtime(force: bool = False) -> Path:
+def build_runtime(force: bool = False, extra_flags: tuple = (), variant: str = "") -> Path:
     """Compile ``libtj_b200.so`` in-tree: the driver-API runtime (host C++; libcuda is opened
     at run time) plus the allocation-free linear entry point (``tj_b200_noalloc.cu``, sm_100a,
-    static CUDA runtime).  The library loads on machines without a GPU."""
+    static CUDA runtime).  The library loads on machines without a GPU.  ``variant`` names a
+    separately built copy with ``extra_flags`` (``libtj_b200_<variant>.so``; e.g. the
+    failure-path test build); the product library is the one without."""
     with _lock:
         src = CSRC / "tj_b200_runtime.cpp"
         na = CSRC / "tj_b200_noalloc.cu"
         hdr = INCLUDE / "tj_b200.h"
-        stamp = LIB_PATH.with_suffix(".hash")
-        h = hashlib.sha256(src.read_bytes() + na.read_bytes() + hdr.read_bytes() + _headers_hash().encode()).hexdigest()
-        if not force and LIB_PATH.exists() and stamp.exists() and stamp.read_text() == h:
-            return LIB_PATH
-        LIB_PATH.parent.mkdir(parents=True, exist_ok=True)
-        tmp = LIB_PATH.with_suffix(f".{os.getpid()}.tmp")
+        out = LIB_PATH if not variant else LIB_PATH.with_name(f"libtj_b200_{variant}.so")
+        stamp = out.with_suffix(".hash")
+        h = hashlib.sha256(src.read_bytes() + na.read_bytes() + hdr.read_bytes() + _headers_hash().encode()
+                           + " ".join(extra_flags).encode()).hexdigest()
+        if not force and out.exists() and stamp.exists() and stamp.read_text() == h:
+            return out
+        out.parent.mkdir(parents=True, exist_ok=True)
+        tmp = out.with_suffix(f".{os.getpid()}.tmp")
         cmd = [nvcc(), "-O2", "-std=c++17", "-shared", *ARCH_FLAGS, "-Xcompiler", "-fPIC,-fvisibility=hidden,-Wall",
-               "--expt-relaxed-constexpr", f"-I{INCLUDE}", f"-I{KDIR}", str(src), str(na), "-o", str(tmp),
-               "-ldl", "-lpthread"]
+               "--expt-relaxed-constexpr", *extra_flags, f"-I{INCLUDE}", f"-I{KDIR}", str(src), str(na), "-o",
+               str(tmp), "-ldl", "-lpthread"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise BuildError(f"runtime build failed:\n{r.stderr[-4000:]}")
-        os.replace(tmp, LIB_PATH)
+        os.replace(tmp, out)
         stamp.write_text(h)
-        return LIB_PATH
+        return out
