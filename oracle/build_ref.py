@@ -34,6 +34,8 @@ OUT = HERE / "_ref"
 REPO = HERE.parent
 sys.path.insert(0, str(REPO))
 
+from oracle import reference_checkout  # noqa: E402
+
 # (name, workload, rows of the row-sharded arguments or None for the full program)
 SAMPLES = [("cfg1", "cfg1", None), ("cfg2", "cfg2", None), ("cfg3_m512", "cfg3", 512), ("cfg4", "cfg4", None),
            ("cfg5_m1024", "cfg5", 1024)]
@@ -41,7 +43,7 @@ SAMPLES = [("cfg1", "cfg1", None), ("cfg2", "cfg2", None), ("cfg3_m512", "cfg3",
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("TJ_REF", "/root/reference"))
+    ap.add_argument("--ref", default=str(reference_checkout()))
     a = ap.parse_args()
     if not Path(a.ref).exists():
         print(f"reference not found at {a.ref}; nothing to do")

@@ -98,3 +98,66 @@ def check_against_golden(y, exp: dict, tol: float) -> float:
     if not err <= tol:
         raise AssertionError(f"normwise error {err:.3e} > tol {tol:.1e}")
     return err
+
+
+def case_dense(name: str) -> dict | None:
+    """Dense golden data of a full-size config (per-row checksums of every output row and whole
+    rows; written by ``tests/golden/make_fixtures.py``), or None if the config has none."""
+    entry = index()[name]
+    if "dense" not in entry:
+        return None
+    data = np.load(GOLDEN / entry["dense"])
+    return {k: data[k] for k in data.files}
+
+
+def check_rows_dense(y, dense: dict, i: int, tol: float) -> dict:
+    """Output ``i`` against the dense golden data, row by row.
+
+    * whole rows (``out{i}_dense_idx`` / ``out{i}_dense``): normwise error per row ≤ tol;
+    * every row: with S = Σ|ref| over the row, |Σy − Σref| ≤ tol·S, |Σ|y| − Σ|ref|| ≤ tol·S,
+      |Σ(j+1)/n·y − the same of ref| ≤ tol·S (a permuted row fails) and
+      |Σy² − Σref²| ≤ 2·tol·Σref² (a row with the right sum but the wrong spread fails).
+    These are the normwise tolerance applied to row-level L1 / L2 measures.  Returns the worst
+    value of each measure."""
+    y = y.detach().to("cpu", torch.float32).numpy() if isinstance(y, torch.Tensor) else np.asarray(y, np.float32)
+    m = y.reshape(-1, y.shape[-1]).astype(np.float64)
+    worst = {}
+    if f"out{i}_dense" in dense:
+        idx = dense[f"out{i}_dense_idx"]
+        ref = dense[f"out{i}_dense"].astype(np.float64)
+        got = m[idx]
+        scale = np.maximum(np.abs(ref).max(1), 1e-30)
+        e = np.abs(got - ref).max(1) / scale
+        worst["rows"] = float(e.max())
+        if not worst["rows"] <= tol:
+            raise AssertionError(f"out{i} row {int(idx[e.argmax()])}: normwise error {e.max():.3e} > {tol:.1e}")
+    w = (np.arange(m.shape[1], dtype=np.float64) + 1.0) / m.shape[1]
+    S = np.maximum(dense[f"out{i}_row_abssum"], 1e-30)
+    checks = {"sum": (np.abs(m.sum(1) - dense[f"out{i}_row_sum"]) / S, tol),
+              "abssum": (np.abs(np.abs(m).sum(1) - dense[f"out{i}_row_abssum"]) / S, tol),
+              "wsum": (np.abs(m @ w - dense[f"out{i}_row_wsum"]) / S, tol),
+              "sumsq": (np.abs((m * m).sum(1) - dense[f"out{i}_row_sumsq"])
+                        / np.maximum(dense[f"out{i}_row_sumsq"], 1e-30), 2 * tol)}
+    if m.shape[0] != S.shape[0]:
+        raise AssertionError(f"out{i}: {m.shape[0]} rows, golden has {S.shape[0]}")
+    for k, (e, t) in checks.items():
+        worst[k] = float(e.max())
+        if not worst[k] <= t:
+            raise AssertionError(f"out{i} row {int(e.argmax())}: row {k} differs by {e.max():.3e} (> {t:.1e})")
+    return worst
+
+
+# Half-precision outputs whose distance from the f32 reference exceeds the 2e-2 tolerance
+# because of the plan's own bf16 storage, not the GPU: (case, output index) -> (error of the
+# bf16-storage oracle against the f32 reference, bound the GPU output must meet).  The GPU
+# output must still match the bf16-storage oracle within 2e-2.
+#   transformer_block__bf16 output 1 (the attention probabilities): the weights are N(0, 1),
+#   so the scores reach the hundreds and their bf16 rounding (stored between the QK^T matmul
+#   and the softmax, as the plan says) moves the probabilities by 3.04e-2 on its own.
+BF16_STORAGE_EXCEPTIONS = {("transformer_block__bf16", 1): (3.04e-2, 3.5e-2)}
+
+
+def allowed_error(case: str, out_index: int, tol: float) -> float:
+    """The bound an output of ``case`` must meet against the f32 reference."""
+    ent = BF16_STORAGE_EXCEPTIONS.get((case, out_index))
+    return ent[1] if ent else tol

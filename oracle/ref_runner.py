@@ -41,6 +41,20 @@ def _host_tag() -> str:
     return hashlib.sha256(cpu.encode()).hexdigest()[:10]
 
 
+def set_threads(n: int) -> int:
+    """Give the reference kernels' OpenMP runtime ``n`` threads and return the count it then
+    reports.  Set explicitly (not only through OMP_NUM_THREADS, which a launcher such as
+    torchrun pins to 1 before the process starts): the environment variable is updated for a
+    libgomp that is not loaded yet, and ``omp_set_num_threads`` is called on the loaded one."""
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    try:
+        gomp = ctypes.CDLL("libgomp.so.1")
+        gomp.omp_set_num_threads(ctypes.c_int(n))
+        return int(gomp.omp_get_max_threads())
+    except OSError:
+        return n
+
+
 class RefProgram:
     def __init__(self, name: str):
         self.manifest = json.loads((REF / f"{name}.json").read_text())

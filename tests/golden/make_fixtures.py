@@ -40,6 +40,7 @@ sys.path.insert(0, str(REPO))
 
 from mlir_gpu_kernel_compiler_b200 import workloads as W  # noqa: E402
 from mlir_gpu_kernel_compiler_b200.plan import from_tensorjit  # noqa: E402
+from oracle import reference_checkout  # noqa: E402
 
 
 def cases(tj):
@@ -241,12 +242,46 @@ def _summary(i: int, o: np.ndarray) -> dict:
     }
 
 
+DENSE_CONFIGS = ("cfg2", "cfg4")
+
+
+def row_checksums(o: np.ndarray) -> dict:
+    """Per-row checksums of an output viewed as [rows, last dim], in f64: the sum, the sum of
+    |y|, the sum of y^2, and the position-weighted sum (j + 1) / n * y_j (which also catches
+    a permutation within the row)."""
+    m = o.reshape(-1, o.shape[-1]).astype(np.float64)
+    w = (np.arange(m.shape[1], dtype=np.float64) + 1.0) / m.shape[1]
+    return {"sum": m.sum(1), "abssum": np.abs(m).sum(1), "sumsq": (m * m).sum(1), "wsum": m @ w}
+
+
+def _dense(cname: str, outs: list[np.ndarray]) -> dict:
+    """Dense golden data of a full-size config: per-row checksums of every output row, plus
+    whole rows -- cfg4: all of batch element 0 (rows 0..2047 of y, stored as f16); cfg2: 192 rows
+    of the RMSNorm output spread over its 16384 (f16) and 64 rows of the softmax (f32: its
+    values lie below f16's normal range)."""
+    arrays = {}
+    for i, o in enumerate(outs):
+        for k, v in row_checksums(o).items():
+            arrays[f"out{i}_row_{k}"] = v
+    if cname == "cfg4":
+        arrays["out0_dense_idx"] = np.arange(2048, dtype=np.int64)
+        arrays["out0_dense"] = outs[0][:2048].astype(np.float16)
+    elif cname == "cfg2":
+        i0 = np.unique(np.linspace(0, outs[0].shape[0] - 1, 192).round().astype(np.int64))
+        i1 = np.unique(np.linspace(0, outs[1].shape[0] - 1, 64).round().astype(np.int64))
+        arrays.update(out0_dense_idx=i0, out0_dense=outs[0][i0].astype(np.float16),
+                      out1_dense_idx=i1, out1_dense=outs[1][i1].astype(np.float32))
+    return arrays
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("TJ_REF", "/root/reference"))
+    ap.add_argument("--ref", default=str(reference_checkout()))
     ap.add_argument("--only", nargs="*", default=None)
     ap.add_argument("--skip-configs", action="store_true")
     ap.add_argument("--configs-only", action="store_true")
+    ap.add_argument("--dense-only", action="store_true",
+                    help="only (re)write <cfg>.dense.npz of the configs in DENSE_CONFIGS (or --only)")
     a = ap.parse_args()
     sys.path.insert(0, a.ref)
     os.environ.setdefault("TENSORJIT_NO_AUTOTUNE", "1")
@@ -259,8 +294,20 @@ def main():
     (HERE / "plans").mkdir(exist_ok=True)
     index = {}
     idx_path = HERE / "index.json"
-    if idx_path.exists() and (a.only or a.skip_configs or a.configs_only):
+    if idx_path.exists() and (a.only or a.skip_configs or a.configs_only or a.dense_only):
         index = json.loads(idx_path.read_text())     # partial run: keep the other entries
+
+    if a.dense_only:
+        fns = config_fns(tj)
+        for cname in (a.only or DENSE_CONFIGS):
+            w = W.WORKLOADS[cname]
+            ins = [t.float() for t in W.make_inputs(w)]
+            outs = _run_c(tj, fns[cname], [tuple(t.shape) for t in ins], ins)
+            np.savez_compressed(HERE / f"{w.plan}.dense.npz", **_dense(cname, outs))
+            index[w.plan]["dense"] = f"{w.plan}.dense.npz"
+            print(f"  dense {w.plan}: {[o.shape for o in outs]}")
+        idx_path.write_text(json.dumps(index, indent=1, sort_keys=True))
+        return
 
     if not a.configs_only:
         for name, (fn, shapes, recipe, dtypes) in cases(tj).items():
@@ -331,6 +378,9 @@ def main():
                 arrays.update(_summary(i, o))
             np.savez_compressed(HERE / f"{gname}.golden.npz", **arrays)
             index[gname]["golden"] = f"{gname}.golden.npz"
+            if cname in DENSE_CONFIGS:
+                np.savez_compressed(HERE / f"{gname}.dense.npz", **_dense(cname, outs))
+                index[gname]["dense"] = f"{gname}.dense.npz"
             index[gname]["c_backend_seconds_here"] = round(el, 3)
             print(f"  golden {gname}: c backend {el:.2f}s")
 

@@ -43,13 +43,16 @@ def test_case_matches_reference(case):
             assert normwise_error(y, r) <= tol
         return
     # half precision: the plan keeps every stored intermediate in bf16/f16.  The GPU
-    # result must match the oracle that rounds stored values the same way, and the
-    # f32 reference within the stated tolerance -- or, where bf16 storage alone
-    # already moves the result further (tiny N(0,1)-weight cases), within 1.5x that.
+    # result must match the oracle that rounds stored values the same way within the
+    # stated tolerance, and the f32 reference within it too -- except for the outputs named
+    # in FX.BF16_STORAGE_EXCEPTIONS, where bf16 storage alone already moves the result
+    # further (each with its measured storage error and its own bound).
     emul = evaluate(plan, cpu_ins, round_stored=True)
-    for y, e, r, m in zip(outs, exp, ref, emul):
+    for i, (y, e, r, m) in enumerate(zip(outs, exp, ref, emul)):
         assert normwise_error(y, m) <= tol, "vs bf16-storage oracle"
-        allowed = max(tol, 1.5 * normwise_error(m, r))
+        allowed = FX.allowed_error(case, i, tol)
+        if allowed > tol:     # the named exception is still what the storage error says
+            assert normwise_error(m, r) <= FX.BF16_STORAGE_EXCEPTIONS[(case, i)][0] * 1.01
         FX.check_against_golden(y, e, allowed)
         assert normwise_error(y, r) <= allowed
 

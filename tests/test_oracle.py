@@ -32,6 +32,13 @@ def test_oracle_matches_reference_on_configs(cfg):
     outs = evaluate(plan, W.make_inputs(w))
     for y, e in zip(outs, FX.case_expected(w.plan)):
         FX.check_against_golden(torch.from_numpy(y), e, 1e-5)
+    dense = FX.case_dense(w.plan)
+    if dense is not None:
+        # every row's checksums, and the whole rows (stored as f16 where that keeps the values
+        # normal, hence 1e-3: f16 rounding is at most 2^-11 of a row's largest value)
+        for i, y in enumerate(outs):
+            worst = FX.check_rows_dense(torch.from_numpy(y), dense, i, 1e-3)
+            assert max(v for k, v in worst.items() if k != "rows") <= 1e-5
 
 
 def test_oracle_matches_reference_on_cfg5_slice():
