@@ -4,31 +4,38 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg5] [--impl b200|reference]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
-Default workload: cfg5, the large-batch MLP x + linear(gelu(linear(rms_norm(x,g),w1,b1)),w2,b2)
-in bf16 with x[131072,4096], w1[16384,4096], w2[4096,16384] — the program the
-reference's north star runs at 1/2/4/8 GPUs.  Its rows are split across ranks
-(rank p owns rows [p*R/N, (p+1)*R/N), weights replicated, no collective in the
-step), so the global batch is fixed: strong scaling.  A step is one execution
-of the whole compiled program (RMSNorm row kernel + two tcgen05 GEMMs with
-fused epilogues) over the rank's rows, as one CUDA graph.
+Headline workload: cfg5, the large-batch MLP x + linear(gelu(linear(rms_norm(x,g),w1,b1)),w2,b2)
+in bf16 with x[131072,4096], w1[16384,4096], w2[4096,16384] — the program the reference's
+north star runs at 1/2/4/8 GPUs.  Its rows are split across ranks (rank p owns rows
+[p*R/N, (p+1)*R/N), weights replicated, no collective in the step), so the global batch is
+fixed: strong scaling.  A step is one execution of the whole compiled program (RMSNorm row
+kernel + two tcgen05 GEMMs with fused epilogues) over the rank's rows, as one CUDA graph.
+Before the K timed steps every rank runs untimed steps for at least ``--soak-s`` seconds, so
+that at every N the GPUs are timed in the same power-capped steady state.
 
-``value``  whole-job algorithmic TFLOP/s with inputs resident in HBM
-           (inputs are larger than L2, so no flush is needed between steps).
-``e2e``    the same through the public call ``program(*inputs)`` with the rank's
-           rows copied from pinned host memory every step and the result copied
-           back (the weights stay resident, as a served model's would).
-``roofline`` the dominant kernel's achieved rate from CUDA events around each
-           kernel, against MEASURED_PEAKS.json.
-``cpu_baseline`` the reference's own ``c`` backend (its generated C/OpenMP kernels,
-           built for this host by oracle/ref_runner.py) on a bounded row sample.
+``value``     whole-job algorithmic TFLOP/s with inputs resident in HBM (inputs are larger
+              than L2, so no flush is needed between steps).
+``e2e``       the same through the C ABI with host buffers: the rank's rows stream in from
+              pinned host memory every step and the result streams back, overlapped with
+              compute across steps (``HostPipeline``; weights stay resident, as a served
+              model's would).  ``e2e_call`` beside it is the per-call latency of the public call
+              ``program(*inputs)`` with the copies in sequence.
+``roofline``  the dominant kernel's achieved rate from CUDA events around each kernel,
+              against MEASURED_PEAKS.json.
+``cpu_baseline`` the reference's own ``c`` backend (its generated C/OpenMP kernels, built for
+              this host by oracle/ref_runner.py) on a bounded row sample, every host core.
+``gather``    (N > 1) the optional NCCL all-gather of y to every rank, timed on its own.
+``configs``   (N = 1) cfg1-cfg4 measured the same way in the same run: program latency (graph
+              replay), the dominant kernel's roofline, the reference baseline and clocks.
 
-``--impl reference`` times that reference implementation alone, on the same
-metric, and prints its own line (rank 0 only under torchrun).
+``--impl reference`` times that reference implementation alone, on the same metric, and
+prints its own line (rank 0 only under torchrun).
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import subprocess
 import sys
@@ -40,11 +47,19 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "program latency; GEMM TFLOP/s and row-kernel HBM GB/s vs B200 peak, 1/2/4/8 GPU"
+# reference sample per config: (oracle/_ref program, rows of the row-sharded arguments or None = all)
 REF_SAMPLE = {"cfg1": ("cfg1", None), "cfg2": ("cfg2", None), "cfg3": ("cfg3_m512", 512), "cfg4": ("cfg4", None),
               "cfg5": ("cfg5_m1024", 1024)}
-
+SIDE_CONFIGS = ("cfg1", "cfg2", "cfg3", "cfg4")
 
 L2_BYTES = 126 * 1024 * 1024  # B200 L2
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
 
 
 def _tensor_family(family: str) -> bool:
@@ -143,8 +158,12 @@ def _dist():
     return world, rank, local
 
 
-def reference_baseline(cfg: str, steps: int, warmup: int, threads: int | None = None) -> dict | None:
-    """Time the reference c backend's kernels on a bounded sample; None if unavailable."""
+# ---------------------------------------------------------------------------------------------
+# the reference c backend on the host cores
+# ---------------------------------------------------------------------------------------------
+def reference_baseline(cfg: str, steps: int, warmup: int) -> dict | None:
+    """Time the reference c backend's kernels on a bounded sample with every host core;
+    None if its kernels were not prepared (oracle/_ref)."""
     import numpy as np
 
     from mlir_gpu_kernel_compiler_b200 import workloads as W
@@ -153,13 +172,14 @@ def reference_baseline(cfg: str, steps: int, warmup: int, threads: int | None = 
     name, rows = REF_SAMPLE[cfg]
     if not ref_runner.available(name):
         return None
+    threads = ref_runner.set_threads(host_cores())
     w = W.WORKLOADS[cfg]
     ins = [t.float().numpy() for t in W.make_inputs(w, rows=(0, rows) if rows else None)]
     prog = ref_runner.RefProgram(name)
     for _ in range(max(warmup, 1)):
         prog.run(ins)
     ts = []
-    for _ in range(steps):
+    for _ in range(max(steps, 1)):
         t0 = time.perf_counter()
         prog.run(ins)
         ts.append(time.perf_counter() - t0)
@@ -167,18 +187,22 @@ def reference_baseline(cfg: str, steps: int, warmup: int, threads: int | None = 
     frac = (rows / w.rows) if rows else 1.0
     work = (w.flops or w.hbm_bytes) * frac
     unit_scale = 1e12 if w.flops else 1e9
-    return {"value": work / sec / unit_scale, "unit": "TFLOP/s" if w.flops else "GB/s",
-            "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)), "kind": "reference",
-            "sample": f"{name}: reference c backend (generated C/OpenMP, -O3 -march=native -fopenmp) on "
-                      f"{rows or 'all'} rows, median of {steps} runs, {sec * 1e3:.1f} ms per sample",
-            "ms_per_sample": sec * 1e3}
+    out = {"value": work / sec / unit_scale, "unit": "TFLOP/s" if w.flops else "GB/s", "cores": threads,
+           "kind": "reference",
+           "sample": f"{name}: reference c backend (generated C/OpenMP, -O3 -march=native -fopenmp) on "
+                     f"{rows or 'all'} rows, {threads} OpenMP threads, median of {len(ts)} runs, "
+                     f"{sec * 1e3:.1f} ms per sample",
+           "ms_per_sample": sec * 1e3}
+    if rows:
+        # rows are independent: the rate of a row slice is the rate of the whole program
+        out.update(extrapolated=True, sample_rows=rows, program_rows=w.rows)
+    return out
 
 
 def run_reference(a) -> None:
     world, rank, _ = _dist()
     if rank != 0:
         return
-    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
     res = reference_baseline(a.config, a.steps, a.warmup)
     if res is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref has no generated reference kernels "
@@ -200,7 +224,212 @@ def run_reference(a) -> None:
                        "sample": res["sample"]},
             "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": res["value"], "unit": res["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if res.get("extrapolated"):
+        line["cpu_baseline"].update(extrapolated=True, sample_rows=res["sample_rows"])
     print(json.dumps(line))
+
+
+# ---------------------------------------------------------------------------------------------
+# DRAM traffic of the dominant kernels, from ncu captures (dram__bytes_read.sum + write.sum)
+# ---------------------------------------------------------------------------------------------
+# Keyed by (config, kernel symbol, tile signature); a run whose kernel has another signature (a
+# different tile table) reports no traffic rather than a stale figure.  cfg5's launches are too
+# large to capture, so its GEMMs were captured on 16384-row programs; a launch of M rows moves
+# M / 16384 times those bytes (x, h and the per-row-group weight re-reads grow with the rows).
+TRAFFIC: dict = {
+    ("cfg1", "tj_matmul_1", "x3:BN128"): (22.1e6, None),
+    ("cfg1", "tj_matmul_2", "x3:BN128"): (31.5e6, None),
+    ("cfg2", "tj_row_0", "row"): (365.4e6, None),
+    ("cfg3", "tj_matmul_0", "pair:BN256"): (1068.0e6, None),
+    ("cfg4", "tj_attention_2", "attention"): (114.1e6, None),
+    ("cfg5", "tj_matmul_1", "single:BN256"): (1727.9e6, 16384),
+    ("cfg5", "tj_matmul_2", "single:BN256"): (2822.8e6, 16384),
+    ("cfg5", "tj_matmul_1", "pair:BN256"): (1555.1e6, 16384),
+    ("cfg5", "tj_matmul_2", "pair:BN256"): (3272.9e6, 16384),
+}
+
+
+def tile_signature(ks) -> str:
+    if ks.family == "gemm_tc":
+        kind = "x3" if ks.info.get("tf32x3") else ("pair" if ks.info.get("pair") else "single")
+        return f"{kind}:BN{ks.info.get('BN')}"
+    return ks.family
+
+
+def traffic_per_launch(config: str, ks) -> tuple[float | None, str]:
+    ent = TRAFFIC.get((config, ks.symbol, tile_signature(ks)))
+    if ent is None:
+        return None, f"no ncu capture of {ks.symbol} with tile {tile_signature(ks)}"
+    per, rows = ent
+    if rows is None:
+        return per, f"ncu capture of this launch ({tile_signature(ks)})"
+    return per * ks.info["M"] / rows, f"ncu capture at {rows} rows ({tile_signature(ks)}), scaled by M / {rows}"
+
+
+# ---------------------------------------------------------------------------------------------
+# one program, device-resident inputs
+# ---------------------------------------------------------------------------------------------
+def roofline_of(cfg: str, prog, kms: list[float], sustained: bool) -> tuple[dict, list[dict]]:
+    pk = peaks()
+    dom = max(range(len(kms)), key=lambda i: kms[i])
+    ks = prog.kernel_sources[dom]
+    of = ", of measured" if pk["source"] == "measured" else ", of fallback"
+    if _tensor_family(ks.family):
+        ach = ks.info["flops"] / (kms[dom] * 1e-3) / 1e12
+        peak = pk["bf16_tflops_sustained"] if sustained else pk["bf16_tflops"]
+        kind = ("sustained" if sustained else "burst") + " bf16"
+        if ks.info.get("tf32x3"):
+            # f32 GEMM on the TF32 tensor path: half the bf16 rate, three MMAs per product
+            peak, kind = peak / 6.0, kind + " / 2 (TF32 rate) / 3 (3xTF32 products)"
+        roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                "kernel": ks.symbol, "ms": kms[dom], "peak_kind": kind + of}
+    else:
+        ach = ks.info["bytes"] / (kms[dom] * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
+                "kernel": ks.symbol, "ms": kms[dom], "peak_kind": "copy bandwidth" + of}
+    roof["traffic"], roof["traffic_source"] = traffic_per_launch(cfg, ks)
+    roof["tile"] = tile_signature(ks)
+    per_kernel = [{"kernel": k.symbol, "family": k.family, "ms": round(m, 4),
+                   "rate": round((k.info["flops"] / (m * 1e-3) / 1e12) if _tensor_family(k.family)
+                                 else (k.info["bytes"] / (m * 1e-3) / 1e9), 1) if m > 0 else None,
+                   "rate_unit": "TFLOP/s" if _tensor_family(k.family) else "GB/s"}
+                  for k, m in zip(prog.kernel_sources, kms)]
+    return roof, per_kernel
+
+
+def time_program(prog, ins, outs, steps: int, warmup: int, soak_s: float, dev, barrier) -> dict:
+    """Warm up, soak (untimed steps for soak_s seconds), then time exactly ``steps`` graph
+    replays with CUDA events on the launching stream.  A program whose inputs, outputs and
+    intermediates fit in L2 is timed step by step with L2 flushed before each step by a write
+    of twice its size, outside the events."""
+    import torch
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(warmup):
+        prog.run_into(ins, outs)
+    torch.cuda.synchronize(dev)
+    prog.check()
+    footprint = sum(t.numel() * t.element_size() for t in ins + outs) + prog.arena_bytes
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if footprint < L2_BYTES else None
+    soaked = 0
+    if soak_s > 0:
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < soak_s:
+            for _ in range(8):
+                if flush is not None:
+                    flush.fill_(1.0)
+                prog.run_into(ins, outs)
+                soaked += 1
+            torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    clk = Clocks(dev.index or 0)
+    with clk:
+        if flush is None:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            for _ in range(steps):
+                prog.run_into(ins, outs)
+            end.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = start.elapsed_time(end) / steps
+        else:
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+            for s0, s1 in evs:
+                flush.fill_(1.0)
+                s0.record(stream)
+                prog.run_into(ins, outs)
+                s1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = sum(s0.elapsed_time(s1) for s0, s1 in evs) / steps
+    l2 = ("inputs, outputs and intermediates of a step exceed L2 (no flush needed)" if flush is None
+          else f"L2 flushed before every timed step ({2 * L2_BYTES >> 20} MiB write, outside the events)")
+    return {"ms": ms, "clocks": clk.summary(), "l2": l2, "soak_steps": soaked, "soak_s": soak_s if soaked else 0.0}
+
+
+def e2e_call(prog, host_ins: list, stream_idx: list[int], resident: dict, calls: int, dev) -> dict:
+    """Per-call latency of the public call with host data: copy the streamed inputs from
+    pinned host memory, ``program(*inputs)``, copy the outputs back; in sequence, one call at a
+    time (CUDA events on the current stream around the whole call)."""
+    import torch
+
+    stream = torch.cuda.current_stream(dev)
+    d_in = {i: torch.empty_like(host_ins[i], device=dev) for i in stream_idx}
+    host_out = None
+    h2d = sum(host_ins[i].numel() * host_ins[i].element_size() for i in stream_idx)
+
+    def one():
+        nonlocal host_out
+        for i in stream_idx:
+            d_in[i].copy_(host_ins[i], non_blocking=True)
+        ins = [d_in[i] if i in d_in else resident[i] for i in range(len(host_ins))]
+        outs = prog(*ins)
+        if host_out is None:
+            host_out = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+        for h, o in zip(host_out, outs):
+            h.copy_(o, non_blocking=True)
+
+    one()
+    torch.cuda.synchronize(dev)
+    ts = []
+    for _ in range(calls):
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        one()
+        s1.record(stream)
+        torch.cuda.synchronize(dev)
+        ts.append(s0.elapsed_time(s1))
+    ts.sort()
+    d2h = sum(h.numel() * h.element_size() for h in host_out)
+    return {"ms_per_call": ts[len(ts) // 2], "calls": calls, "h2d_bytes_per_call": h2d, "d2h_bytes_per_call": d2h,
+            "how": "program(*inputs) with the streamed inputs copied from pinned host memory and the outputs "
+                   "copied back, in sequence (median call)"}
+
+
+def measure_side_config(cfg: str, a, dev) -> dict:
+    """cfg1-cfg4 on one GPU: program latency (graph replay), dominant-kernel roofline, per-call
+    latency with host data, the reference c backend on the host cores, clocks."""
+    import torch
+
+    from mlir_gpu_kernel_compiler_b200 import B200Program
+    from mlir_gpu_kernel_compiler_b200 import workloads as W
+    from mlir_gpu_kernel_compiler_b200.plan import PProgram
+
+    w = W.WORKLOADS[cfg]
+    plan = PProgram.load(ROOT / "tests" / "golden" / "plans" / f"{w.plan}.json")
+    host = W.make_inputs(w)
+    ins = [t.to(dev) for t in host]
+    prog = B200Program(plan, device=dev, use_graph=True)
+    outs = [torch.empty(s, dtype=d, device=dev) for s, d in prog.output_specs()]
+    t = time_program(prog, ins, outs, a.steps, a.warmup, 0.0, dev, lambda: None)
+    ms = t["ms"]
+    work = w.flops or w.hbm_bytes
+    unit_scale, unit = (1e12, "TFLOP/s") if w.flops else (1e9, "GB/s")
+    kms = prog.time_kernels(ins, outs, iters=max(3, min(a.steps, 10)))
+    roof, per_kernel = roofline_of(cfg, prog, kms, sustained=False)
+    rec = {"workload": f"{cfg}: {w.description}", "plan": w.plan, "value": work / (ms * 1e-3) / unit_scale,
+           "unit": unit, "ms_per_step": ms, "steps": a.steps, "warmup": a.warmup, "l2": t["l2"], "graph": True,
+           "dtype": "bf16" if w.dtype == torch.bfloat16 else "f32", "roofline": roof, "kernels": per_kernel,
+           "clocks": t["clocks"],
+           "gpu_launches": sum(1 for L in prog.launches if all(g > 0 for g in L["grid"])) * a.steps}
+    if not a.no_e2e:
+        pinned = [h.pin_memory() for h in host]
+        stream_idx = list(w.row_args) or list(range(len(host)))
+        resident = {i: x for i, x in enumerate(ins) if i not in stream_idx}
+        c = e2e_call(prog, pinned, stream_idx, resident, max(3, min(a.steps, 10)), dev)
+        c["value"] = work / (c["ms_per_call"] * 1e-3) / unit_scale
+        c["unit"] = unit
+        rec["e2e_call"] = c
+    prog.check()
+    prog.close()
+    del ins, outs, host
+    torch.cuda.empty_cache()
+    if not a.no_cpu_baseline:
+        try:
+            rec["cpu_baseline"] = reference_baseline(cfg, steps=3, warmup=1)
+        except Exception as ex:  # the baseline is reported, never required
+            rec["cpu_baseline"] = {"error": str(ex)[:200]}
+    return rec
 
 
 def run_b200(a) -> None:
@@ -234,96 +463,71 @@ def run_b200(a) -> None:
     prog = B200Program(plan, device=dev, use_graph=True)
     outs = [torch.empty(s, dtype=d, device=dev) for s, d in prog.output_specs()]
     _trace("run")
-    stream = torch.cuda.current_stream(dev)
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
 
-    for _ in range(a.warmup):
-        prog.run_into(ins, outs)
-    torch.cuda.synchronize(dev)
-    prog.check()
+    t = time_program(prog, ins, outs, a.steps, a.warmup, a.soak_s, dev, barrier)
     barrier()
-    torch.cuda.synchronize(dev)
-    # A step whose inputs, outputs and intermediates together exceed L2 evicts the previous
-    # step's data by itself; a smaller one (cfg1) is timed step by step with L2 flushed before
-    # each step by a write of twice its size, outside the timed events.
-    footprint = sum(t.numel() * t.element_size() for t in ins + outs) + prog.arena_bytes
-    flush = None
-    if footprint < L2_BYTES:
-        flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
-    clk = Clocks(local)
-    with clk:
-        if flush is None:
-            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            start.record(stream)
-            for _ in range(a.steps):
-                prog.run_into(ins, outs)
-            end.record(stream)
-            torch.cuda.synchronize(dev)
-            ms = start.elapsed_time(end) / a.steps
-        else:
-            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
-            for s0, s1 in evs:
-                flush.fill_(1.0)
-                s0.record(stream)
-                prog.run_into(ins, outs)
-                s1.record(stream)
-            torch.cuda.synchronize(dev)
-            ms = sum(s0.elapsed_time(s1) for s0, s1 in evs) / a.steps
-    l2_note = ("inputs, outputs and intermediates of a step exceed L2 (no flush needed)" if flush is None
-               else f"L2 flushed before every timed step ({2 * L2_BYTES >> 20} MiB write, outside the events)")
-    barrier()
-    t = torch.tensor([ms], device=dev)
+    ms_t = torch.tensor([t["ms"]], device=dev)
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
     frac_rows = ((rows[1] - rows[0]) * world / w.rows) if sharded else world
     total_work = (w.flops or w.hbm_bytes) * frac_rows
     unit_scale, unit = (1e12, "TFLOP/s") if w.flops else (1e9, "GB/s")
     value = total_work / (ms_max * 1e-3) / unit_scale
+    clocks_all = [t["clocks"]]
+    if world > 1:
+        clocks_all = [None] * world
+        dist.all_gather_object(clocks_all, t["clocks"])
 
     # per-kernel device times (events around every kernel, same stream) -> dominant kernel roofline
     kms = prog.time_kernels(ins, outs, iters=max(3, min(a.steps, 10)))
-    pk = peaks()
-    dom = max(range(len(kms)), key=lambda i: kms[i])
-    ks = prog.kernel_sources[dom]
-    if _tensor_family(ks.family):
-        ach = ks.info["flops"] / (kms[dom] * 1e-3) / 1e12
-        peak = pk["bf16_tflops_sustained"] if a.config in ("cfg4", "cfg5") else pk["bf16_tflops"]
-        kind = ("sustained" if peak == pk["bf16_tflops_sustained"] else "burst") + " bf16"
-        if ks.info.get("tf32x3"):
-            # f32 GEMM on the TF32 tensor path: half the bf16 rate, three MMAs per product
-            peak, kind = peak / 6.0, kind + " / 2 (TF32 rate) / 3 (3xTF32 products)"
-        roof = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
-                "kernel": ks.symbol, "ms": kms[dom],
-                "peak_kind": kind + (", of measured" if pk["source"] == "measured" else ", of fallback")}
-    else:
-        ach = ks.info["bytes"] / (kms[dom] * 1e-3) / 1e9
-        roof = {"bound": "hbm", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
-                "kernel": ks.symbol, "ms": kms[dom],
-                "peak_kind": "copy bandwidth, " + ("of measured" if pk["source"] == "measured" else "of fallback")}
-    roof["traffic"] = traffic_per_launch(a.config, ks)
-    per_kernel = [{"kernel": k.symbol, "family": k.family, "ms": round(m, 4),
-                   "rate": round((k.info["flops"] / (m * 1e-3) / 1e12) if _tensor_family(k.family)
-                                 else (k.info["bytes"] / (m * 1e-3) / 1e9), 1) if m > 0 else None,
-                   "rate_unit": "TFLOP/s" if _tensor_family(k.family) else "GB/s"}
-                  for k, m in zip(prog.kernel_sources, kms)]
+    roof, per_kernel = roofline_of(a.config, prog, kms, sustained=a.soak_s > 0 or a.config in ("cfg4", "cfg5"))
 
-    # end to end through the public API with host data every step: HostPipeline streams the
-    # row inputs in from pinned host memory and the result out, overlapping both copy
-    # directions with compute across consecutive steps (weights stay resident)
-    e2e = None
+    # the optional all-gather of y to every rank (N > 1), outside the compute step
+    gather = None
+    if world > 1 and sharded and not a.no_gather:
+        from mlir_gpu_kernel_compiler_b200.distributed import gather_rows
+
+        y = outs[0]
+        for _ in range(2):
+            gather_rows(y)
+        torch.cuda.synchronize(dev)
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        g0.record()
+        for _ in range(reps):
+            full = gather_rows(y)
+        g1.record()
+        torch.cuda.synchronize(dev)
+        gms = torch.tensor([g0.elapsed_time(g1) / reps], device=dev)
+        dist.all_reduce(gms, op=dist.ReduceOp.MAX)
+        gms = float(gms.item())
+        total_bytes = full.numel() * full.element_size()
+        gather = {"ms": gms, "bytes_gathered": total_bytes,
+                  "algbw_gbs": total_bytes / (gms * 1e-3) / 1e9,
+                  "busbw_gbs": total_bytes * (world - 1) / world / (gms * 1e-3) / 1e9,
+                  "how": "NCCL all_gather_into_tensor of every rank's y rows (bf16) to every rank, mean of "
+                         f"{reps}, max over ranks; busbw = bytes x (N-1)/N / time, the bytes each GPU receives"}
+        del full
+
+    # end to end through the C ABI with host data every step: HostPipeline streams the row
+    # inputs in from pinned host memory and the result out, overlapping both copy directions
+    # with compute across consecutive steps (weights stay resident)
+    e2e, e2e_c = None, None
     if not a.no_e2e:
         from mlir_gpu_kernel_compiler_b200.pipeline import HostPipeline
 
         stream_idx = list(w.row_args) or list(range(len(ins)))
-        resident = {i: t for i, t in enumerate(ins) if i not in stream_idx}
+        resident = {i: x for i, x in enumerate(ins) if i not in stream_idx}
         host_in = {i: ins[i].cpu().pin_memory() for i in stream_idx}
         host_out = [[torch.empty(s, dtype=d).pin_memory() for s, d in prog.output_specs()] for _ in range(2)]
-        h2d = sum(t.numel() * t.element_size() for t in host_in.values())
-        d2h = sum(t.numel() * t.element_size() for t in host_out[0])
+        h2d = sum(x.numel() * x.element_size() for x in host_in.values())
+        d2h = sum(x.numel() * x.element_size() for x in host_out[0])
         pipe = HostPipeline(prog, stream_idx, resident, depth=2)
         for k in range(max(2, min(a.warmup, 3))):
             pipe.submit(host_in, host_out[k % 2])
@@ -344,15 +548,42 @@ def run_b200(a) -> None:
         e2e = {"value": total_work / (ems * 1e-3) / unit_scale, "unit": unit, "ms_per_step": ems,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "how": "HostPipeline: pinned host rows in, result out, copies overlapped with compute across steps"}
+        del pipe
+        # per-call latency of the public call with host data, copies in sequence
+        host_full = [ins[i].cpu().pin_memory() if i in stream_idx else ins[i] for i in range(len(ins))]
+        barrier()
+        e2e_c = e2e_call(prog, host_full, stream_idx, resident, max(3, min(a.steps, 5)), dev)
+        ct = torch.tensor([e2e_c["ms_per_call"]], device=dev)
+        if world > 1:
+            dist.all_reduce(ct, op=dist.ReduceOp.MAX)
+        e2e_c["ms_per_call"] = float(ct.item())
+        e2e_c["value"] = total_work / (e2e_c["ms_per_call"] * 1e-3) / unit_scale
+        e2e_c["unit"] = unit
+        del host_full, host_in, host_out
     prog.check()
+    launches = sum(1 for L in prog.launches if all(g > 0 for g in L["grid"])) * a.steps
+    prog.close()
+    del ins, outs
+    torch.cuda.empty_cache()
+
+    # cfg1-cfg4 in the same run (one GPU; rank 0 of a 1-GPU run)
+    configs = None
+    if world == 1 and a.side_configs:
+        configs = {}
+        for c in [x for x in a.side_configs.split(",") if x and x != a.config]:
+            _trace("side config", c)
+            try:
+                configs[c] = measure_side_config(c, a, dev)
+            except Exception as ex:  # a side record must not take the headline line with it
+                configs[c] = {"error": f"{type(ex).__name__}: {str(ex)[:300]}"}
 
     cpu = None
-    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+    if rank == 0 and not a.no_cpu_baseline:
         try:
-            cpu = reference_baseline(a.config, steps=2, warmup=1)
+            cpu = reference_baseline(a.config, steps=3, warmup=1)
         except Exception as ex:  # the baseline is reported, never required
             cpu = {"error": str(ex)[:200]}
-    launches = sum(1 for L in prog.launches if all(g > 0 for g in L["grid"])) * a.steps
+    barrier()
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
@@ -362,42 +593,18 @@ def run_b200(a) -> None:
             "config": {"workload": f"{a.config}: {w.description}", "plan": plan_name, "rows_per_rank": (
                 rows[1] - rows[0]) if rows else None, "global_rows": total_rows if sharded else None,
                 "parallelism": f"rows{world}" if sharded else f"replicas{world}",
-                "l2": l2_note, "graph": True},
-            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-            "clocks": clk.summary(), "kernels": per_kernel,
+                "l2": t["l2"], "graph": True, "soak_s": t["soak_s"], "soak_steps_rank0": t["soak_steps"]},
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "e2e_call": e2e_c, "gpu_launches": launches,
+            "clocks": t["clocks"], "kernels": per_kernel,
         }
+        if world > 1:
+            line["clocks_per_rank"] = clocks_all
+            line["gather"] = gather
+        if configs is not None:
+            line["configs"] = configs
         print(json.dumps(line))
-    del prog
     if world > 1:
         dist.destroy_process_group()
-
-
-# dram read+write bytes per launch of the dominant kernel, from the committed ncu summaries
-# (profiles/*.md)
-TRAFFIC: dict = {
-    ("cfg1", "tj_matmul_1"): 22.1e6,
-    ("cfg1", "tj_matmul_2"): 31.5e6,
-    ("cfg2", "tj_row_0"): 365.4e6,
-    ("cfg3", "tj_matmul_0"): 1068.0e6,
-    ("cfg4", "tj_attention_2"): 114.1e6,
-}
-# cfg5's launches (131072 rows at one GPU, 131072 / N per rank) are too large to capture, so
-# its GEMMs were captured on 16384-row programs (profiles/gemm_traffic_cfg5_cfg1.md), once per
-# tile kind (single CTA / CTA pair); a launch of M rows moves M / 16384 times those bytes (x, h
-# and the per-row-group weight re-reads all grow in proportion to the rows)
-CFG5_TRAFFIC_16K: dict = {
-    ("tj_matmul_1", False): 1727.9e6,
-    ("tj_matmul_2", False): 2822.8e6,
-    ("tj_matmul_1", True): 1555.1e6,
-    ("tj_matmul_2", True): 3272.9e6,
-}
-
-
-def traffic_per_launch(config: str, ks):
-    if config == "cfg5":
-        per = CFG5_TRAFFIC_16K.get((ks.symbol, bool(ks.info.get("pair"))))
-        return per * ks.info["M"] / 16384 if per is not None and "M" in ks.info else None
-    return TRAFFIC.get((config, ks.symbol))
 
 
 def main():
@@ -407,13 +614,20 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="cfg5", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--soak-s", type=float, default=2.0,
+                    help="untimed steps for this many seconds before the timed steps (power-capped steady state)")
+    ap.add_argument("--side-configs", default=",".join(SIDE_CONFIGS),
+                    help="1-GPU runs: also measure these configs into the line's 'configs' record ('' = none)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gather", action="store_true")
     ap.add_argument("--rows", type=int, default=None,
                     help="cfg5 only: run a leading slice of this many rows (for small profiling captures)")
     a = ap.parse_args()
     if a.warmup < 3 and a.impl == "b200":
         a.warmup = 3
+    if a.config != "cfg5" and a.side_configs == ",".join(SIDE_CONFIGS):
+        a.side_configs = ""          # a single-config run measures that config only
     if a.impl == "reference":
         run_reference(a)
     else:

@@ -33,19 +33,27 @@ def test_cfg5_traffic_scales_with_rows_and_follows_the_tile_kind():
     full = _sources("cfg5_m131072")
     shard = _sources("cfg5_m16384")
     for sym in ("tj_matmul_1", "tj_matmul_2"):
-        k_full, k_shard = full[sym], shard[sym]
-        per = b.CFG5_TRAFFIC_16K[(sym, bool(k_full.info["pair"]))]
-        assert b.traffic_per_launch("cfg5", k_full) == pytest.approx(per * 8)
-        per_s = b.CFG5_TRAFFIC_16K[(sym, bool(k_shard.info["pair"]))]
-        assert b.traffic_per_launch("cfg5", k_shard) == pytest.approx(per_s)
-    assert b.traffic_per_launch("cfg5", full["tj_row_0"]) is None
+        for k, scale in ((full[sym], 8), (shard[sym], 1)):
+            per, rows = b.TRAFFIC[("cfg5", sym, b.tile_signature(k))]
+            traffic, src = b.traffic_per_launch("cfg5", k)
+            assert rows == 16384 and traffic == pytest.approx(per * scale) and "scaled" in src
+    assert b.traffic_per_launch("cfg5", full["tj_row_0"])[0] is None
+
+
+def test_traffic_is_withheld_for_a_tile_that_was_not_captured():
+    b = _bench()
+    k = _sources("cfg5_m131072")["tj_matmul_1"]
+    k.info = dict(k.info, BN=64)          # a different tile than the captured one
+    traffic, src = b.traffic_per_launch("cfg5", k)
+    assert traffic is None and "no ncu capture" in src
 
 
 def test_traffic_of_the_other_configs_names_their_dominant_kernels():
     b = _bench()
     for cfg, sym in (("cfg3", "tj_matmul_0"), ("cfg4", "tj_attention_2"), ("cfg2", "tj_row_0")):
         k = _sources(cfg)[sym]
-        assert b.traffic_per_launch(cfg, k) == b.TRAFFIC[(cfg, sym)] > 0
+        traffic, _ = b.traffic_per_launch(cfg, k)
+        assert traffic == b.TRAFFIC[(cfg, sym, b.tile_signature(k))][0] > 0
 
 
 def test_reference_arm_prints_the_contract_line():
@@ -61,3 +69,22 @@ def test_reference_arm_prints_the_contract_line():
     assert line["impl"] == "reference" and line["value"] > 0 and line["unit"] == "TFLOP/s"
     assert line["cpu_baseline"]["kind"] == "reference" and line["cpu_baseline"]["value"] == line["value"]
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+
+
+def test_reference_arm_uses_every_host_core_under_a_launcher():
+    """torchrun sets OMP_NUM_THREADS=1 in every rank; the reference arm still runs rank 0 on
+    every host core (and the other ranks exit without work)."""
+    import os
+
+    env = dict(os.environ, OMP_NUM_THREADS="1", RANK="0", WORLD_SIZE="2", LOCAL_RANK="0")
+    r = subprocess.run([sys.executable, "bench.py", "--config", "cfg1", "--impl", "reference", "--steps", "1",
+                        "--warmup", "1", "--gpus", "2"], cwd=ROOT, capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads([x for x in r.stdout.splitlines() if x.startswith("{")][-1])
+    if "unavailable" in line:
+        pytest.skip(line["unavailable"])
+    assert line["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0)) and line["n_gpus"] == 2
+    env["RANK"] = "1"
+    r = subprocess.run([sys.executable, "bench.py", "--config", "cfg1", "--impl", "reference", "--steps", "1",
+                        "--warmup", "1", "--gpus", "2"], cwd=ROOT, capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0 and not r.stdout.strip()
