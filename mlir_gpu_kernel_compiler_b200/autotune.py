@@ -40,6 +40,7 @@ class TileConfig:
     STAGES: int
     GROUP_M: int = 16
     PAIR: bool = False      # 2-SM cluster (cta_group::2), 256-row tiles
+    GROUP_N: int = 0        # column tiles per raster band (0 = all of N in one band)
 
     def as_dict(self) -> dict:
         return asdict(self)
@@ -254,7 +255,7 @@ def tiles_for_plan(plan) -> dict:
         if env:
             cfg = parse_tile(env)
             if cfg.PAIR and form.b_mn:
-                cfg = TileConfig(cfg.BN, cfg.STAGES, cfg.GROUP_M, False)
+                cfg = TileConfig(cfg.BN, cfg.STAGES, cfg.GROUP_M, False, cfg.GROUP_N)
         else:
             cfg = lookup_any(M, N, K, batch, a.dtype, form.b_mn) or pick(M, N, K, batch, form.b_mn)
         out[idx] = cfg.as_dict()
@@ -262,9 +263,10 @@ def tiles_for_plan(plan) -> dict:
 
 
 def parse_tile(s: str) -> TileConfig:
-    """``BN:STAGES[:GROUP_M[:PAIR]]`` (the ``TENSORJIT_B200_TILE`` syntax)."""
+    """``BN:STAGES[:GROUP_M[:PAIR[:GROUP_N]]]`` (the ``TENSORJIT_B200_TILE`` syntax)."""
     parts = [int(x) for x in s.split(":")]
-    return TileConfig(parts[0], parts[1], parts[2] if len(parts) > 2 else 16, bool(parts[3]) if len(parts) > 3 else False)
+    return TileConfig(parts[0], parts[1], parts[2] if len(parts) > 2 else 16, bool(parts[3]) if len(parts) > 3 else False,
+                      parts[4] if len(parts) > 4 else 0)
 
 
 def plain_gemm_plan(M: int, N: int, K: int, dtype: str = "bf16"):
@@ -307,7 +309,7 @@ def compare_with_library(M: int, N: int, K: int, tiles: list[TileConfig], rounds
     for cfg in tiles:
         prog = B200Program(plain_gemm_plan(M, N, K, dtype), device=device, use_graph=False,
                            tiles={0: cfg.as_dict()})
-        arms[f"{cfg.BN}:{cfg.STAGES}:{cfg.GROUP_M}:{int(cfg.PAIR)}"] = prog
+        arms[f"{cfg.BN}:{cfg.STAGES}:{cfg.GROUP_M}:{int(cfg.PAIR)}" + (f":{cfg.GROUP_N}" if cfg.GROUP_N else "")] = prog
 
     def run(name, iters):
         if name == "library":

@@ -14,23 +14,31 @@ from __future__ import annotations
 
 from ..plan import PProgram
 from .attention import gen_attention
-from .common import KernelSource
+from .common import KernelSource, checked_build
 from .ewise import gen_elementwise
 from .gemm import gen_gemm_multi, gen_matmul
 from .row import gen_row
 
 
-def generate(plan: PProgram, tiles: dict | None = None, prefix: str = "tj") -> list[KernelSource]:
+def generate(plan: PProgram, tiles: dict | None = None, prefix: str = "tj", checked: bool = False) -> list[KernelSource]:
+    """``checked``: emit the checked build (every global access bounds-checked against its
+    operand, TMA coordinates and TMEM columns checked in the templates; compile with
+    -DTJ_CHECKED, ``toolchain.CHECKED_FLAGS``)."""
+    with checked_build(checked):
+        return _generate(plan, tiles, prefix)
+
+
+def _generate(plan: PProgram, tiles: dict | None, prefix: str) -> list[KernelSource]:
     out: list[KernelSource] = []
     for idx, k in enumerate(plan.kernels):
         sym = f"{prefix}_{k.kind}_{idx}"
         if k.kind in ("elementwise", "copy"):
-            ks = gen_elementwise(k, sym)
+            ks = gen_elementwise(k, sym, idx)
         elif k.kind == "row":
-            ks = gen_row(k, k.stages, tuple(k.rows), int(k.n), sym)
+            ks = gen_row(k, k.stages, tuple(k.rows), int(k.n), sym, idx)
         elif k.kind == "reduce":
             x = k.anchor.inputs[0]
-            ks = gen_row(k, [k], tuple(x.shape[:-1]), int(x.shape[-1]) if x.shape else 1, sym)
+            ks = gen_row(k, [k], tuple(x.shape[:-1]), int(x.shape[-1]) if x.shape else 1, sym, idx)
         elif k.kind == "attention":
             ks = gen_attention(k, sym, idx)
         elif k.kind == "matmul_multi":

@@ -86,7 +86,7 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     L.append("struct Cfg {")
     L.append(f"  using T = {CTYPE[dt]};")
     L.append(f"  static constexpr int SQ = {sq}, SK = {sk}, D = {d}, DV = {dv}, STAGES = {STAGES};")
-    L.append(f"  static constexpr long BATCH = {bh_total}L;")
+    L.append(f"  static constexpr long BATCH = {bh_total}L, O_NUMEL = {out_node.numel}L;")
     L.append(f"  static constexpr bool BF16 = {'true' if dt == 'bf16' else 'false'};")
     L.append(f"  static constexpr int EMU = {kn['EMU']};")
     L.append(f"  static constexpr bool DESYNC = {'true' if kn['DESYNC'] else 'false'};")

@@ -10,11 +10,49 @@ and the DAG as compile-time constants.
 """
 from __future__ import annotations
 
+import contextlib
+import contextvars
 import math
 from dataclasses import dataclass, field
 from typing import Optional
 
 from ..plan import PKernel, PNode
+
+# Checked build (TENSORJIT_B200_CHECKED=1): generators declare global operands as bounded views
+# (``tj_view`` in tj_common.cuh, compiled with -DTJ_CHECKED) and give every kernel a status
+# argument, so an out-of-range element index is reported instead of touching memory.
+_CHECKED = contextvars.ContextVar("tj_checked", default=False)
+BOUNDS_SITE = 15          # status "where" = plan kernel index * 16 + BOUNDS_SITE
+
+
+def checked() -> bool:
+    return _CHECKED.get()
+
+
+@contextlib.contextmanager
+def checked_build(on: bool = True):
+    token = _CHECKED.set(bool(on))
+    try:
+        yield
+    finally:
+        _CHECKED.reset(token)
+
+
+def ptr_decl(name: str, ctype: str, idx: int, numel: int, const: bool, kernel_id: int = 0,
+             status: str = "tj_status") -> str:
+    """Declaration of kernel argument ``idx`` as ``name``: a restrict pointer, or in a checked
+    build a ``tj_view`` over its ``numel`` elements that reports (TJ_STATUS_BOUNDS,
+    kernel_id * 16 + 15, argument idx) through ``status``."""
+    t = f"const {ctype}" if const else ctype
+    if not checked():
+        return f"{t}* __restrict__ {name} = ({t}*)prm.p[{idx}];"
+    return (f"const tj_view<{t}> {name}{{({t}*)prm.p[{idx}], {numel}L, {status}, "
+            f"{kernel_id * 16 + BOUNDS_SITE}, {idx}}};")
+
+
+def status_decl(idx: int) -> str:
+    """``tj_status``: the program's status words (argument ``idx``), declared in checked builds."""
+    return f"int* const tj_status = (int*)prm.p[{idx}];" if checked() else ""
 
 CTYPE = {"f32": "float", "f16": "__half", "bf16": "__nv_bfloat16", "i32": "int"}
 ITEM = {"f32": 4, "f16": 2, "bf16": 2, "i32": 4}

@@ -14,14 +14,14 @@ the scalar path with compile-time index decomposition.
 from __future__ import annotations
 
 from ..plan import PKernel, access_strides, contiguous_strides, first_consumer
-from .common import (CTYPE, HEADER, NUM_SMS, KernelSource, coalesce, decompose_stmts, expr, fast_math_for,
-                     offset_expr, params_struct, pick_vec, prod)
+from .common import (CTYPE, HEADER, NUM_SMS, KernelSource, checked, coalesce, decompose_stmts, expr, fast_math_for,
+                     offset_expr, params_struct, pick_vec, prod, ptr_decl, status_decl)
 
 THREADS = 256
 UNROLL = 2
 
 
-def gen_elementwise(k: PKernel, symbol: str) -> KernelSource:
+def gen_elementwise(k: PKernel, symbol: str, kernel_id: int = 0) -> KernelSource:
     shape = tuple(k.iter_shape)
     numel = prod(shape)
     ins, outs = list(k.inputs), list(k.outputs)
@@ -40,12 +40,15 @@ def gen_elementwise(k: PKernel, symbol: str) -> KernelSource:
     if not vec_ok:
         VEC = 1
 
-    L = [HEADER, params_struct(len(ins) + len(outs), 0),
+    chk = checked()
+    L = [HEADER, params_struct(len(ins) + len(outs) + (1 if chk else 0), 0),
          f'extern "C" __global__ void __launch_bounds__({THREADS}) {symbol}(const __grid_constant__ Params prm) {{']
+    if chk:
+        L.append("  " + status_decl(len(ins) + len(outs)))
     for j, n in enumerate(ins):
-        L.append(f"  const {CTYPE[n.dtype]}* __restrict__ in{j} = (const {CTYPE[n.dtype]}*)prm.p[{j}];")
+        L.append("  " + ptr_decl(f"in{j}", CTYPE[n.dtype], j, n.numel, True, kernel_id))
     for j, o in enumerate(outs):
-        L.append(f"  {CTYPE[o.dtype]}* __restrict__ out{j} = ({CTYPE[o.dtype]}*)prm.p[{len(ins) + j}];")
+        L.append("  " + ptr_decl(f"out{j}", CTYPE[o.dtype], len(ins) + j, o.numel, False, kernel_id))
     names = {n.id: f"x{j}" for j, n in enumerate(ins)}
     fast = fast_math_for([o.dtype for o in outs])
     nvec = numel // VEC
@@ -100,7 +103,7 @@ def gen_elementwise(k: PKernel, symbol: str) -> KernelSource:
     L.append("}")
     grid = max(1, min((nvec + THREADS * UNROLL - 1) // (THREADS * UNROLL), NUM_SMS * 8)) if nvec else 0
     ks = KernelSource(symbol, "copy" if k.kind == "copy" else "ewise", "\n".join(L), (grid, 1, 1), (THREADS, 1, 1),
-                      [("node", n) for n in ins + outs],
+                      [("node", n) for n in ins + outs] + ([("status", None)] if chk else []),
                       info={"vec": VEC, "numel": numel, "shape": list(cshape),
                             "bytes": sum(n.nbytes for n in ins) + sum(o.nbytes for o in outs)})
     ks.finalize_params()

@@ -27,8 +27,8 @@ from __future__ import annotations
 import os
 
 from ..plan import PKernel, PNode, access_strides, contiguous_strides, first_consumer
-from .common import (CTYPE, HEADER, ITEM, NUM_SMS, TMAP_DTYPE, KernelSource, TMapSpec, decompose_stmts, expr,
-                     fast_math_for, offset_expr, params_struct, prod)
+from .common import (BOUNDS_SITE, CTYPE, HEADER, ITEM, NUM_SMS, TMAP_DTYPE, KernelSource, TMapSpec, checked,
+                     decompose_stmts, expr, fast_math_for, offset_expr, params_struct, prod, ptr_decl, status_decl)
 
 
 def _mm_dims(k: PKernel):
@@ -91,7 +91,7 @@ def x3_eligible(k: PKernel) -> bool:
     return gemm_form(k).mode == "x3"
 
 
-def gen_pack_operands(symbol: str, segments: list[dict]) -> KernelSource:
+def gen_pack_operands(symbol: str, segments: list[dict], kernel_id: int = 0) -> KernelSource:
     """Copy GEMM operands into K-major buffers with a 16-byte row pitch in the workspace, for
     the cases the tensor maps cannot read in place: a K that breaks the 16-byte row pitch, an
     N-major B whose N does, and every operand of a 3xTF32 GEMM that is not an f32 K-major
@@ -111,10 +111,21 @@ def gen_pack_operands(symbol: str, segments: list[dict]) -> KernelSource:
         rt = (sg["rows"] + 31) // 32
         tiles.append(sg["mats"] * rt * kt)
     total = sum(tiles)
-    nptr = 3 * len(segments)
+    chk = checked()
+    nptr = 3 * len(segments) + (1 if chk else 0)
     L = [HEADER, params_struct(nptr, 0),
-         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{',
-         "  __shared__ float tile[32][33];",
+         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{']
+    if chk:
+        L.append("  " + status_decl(3 * len(segments)))
+    for j, sg in enumerate(segments):
+        n_src = sg["mats"] * sg["rows"] * sg["K"]
+        n_dst = sg["mats"] * sg["rows"] * sg["pitch"]
+        dt = "float" if sg["split"] else CTYPE[sg["dst_dtype"]]
+        L.append("  " + ptr_decl(f"src{j}", CTYPE[sg["src_dtype"]], 3 * j, n_src, True, kernel_id))
+        L.append("  " + ptr_decl(f"hi{j}", dt, 3 * j + 1, n_dst, False, kernel_id))
+        if sg["split"]:
+            L.append("  " + ptr_decl(f"lo{j}", dt, 3 * j + 2, n_dst, False, kernel_id))
+    L += ["  __shared__ float tile[32][33];",
          "  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;",
          f"  for (long t = blockIdx.x; t < {total}L; t += gridDim.x) {{",
          "    long u = t;"]
@@ -128,14 +139,15 @@ def gen_pack_operands(symbol: str, segments: list[dict]) -> KernelSource:
         L.append(f"    {'if' if j == 0 else 'else if'} ({cond}) {{")
         L.append(f"      u -= {acc}L;")
         L.append(f"      const long kt = u % {kt}L, rt = (u / {kt}L) % {rt}L, mat = u / {kt * rt}L;")
-        L.append(f"      const {st}* __restrict__ src = (const {st}*)prm.p[{3 * j}] + mat * {R * K}L;")
         L.append("      for (int y = ty; y < 32; y += 8) {")
         if sg["k_major"]:
             L.append("        const long r = rt * 32 + y, kk = kt * 32 + tx;")
-            L.append(f"        tile[y][tx] = (r < {R}L && kk < {K}L) ? tj_f32(src[r * {K}L + kk]) : 0.0f;")
+            L.append(f"        tile[y][tx] = (r < {R}L && kk < {K}L) ? tj_f32(src{j}[mat * {R * K}L + r * {K}L + kk]) "
+                     ": 0.0f;")
         else:   # source [K, rows]: consecutive threads read consecutive rows
             L.append("        const long kk = kt * 32 + y, r = rt * 32 + tx;")
-            L.append(f"        tile[tx][y] = (r < {R}L && kk < {K}L) ? tj_f32(src[kk * {R}L + r]) : 0.0f;")
+            L.append(f"        tile[tx][y] = (r < {R}L && kk < {K}L) ? tj_f32(src{j}[mat * {R * K}L + kk * {R}L + r]) "
+                     ": 0.0f;")
         L.append("      }")
         L.append("      __syncthreads();")
         L.append("      for (int y = ty; y < 32; y += 8) {")
@@ -145,10 +157,10 @@ def gen_pack_operands(symbol: str, segments: list[dict]) -> KernelSource:
         L.append(f"          const long o = (mat * {R}L + r) * {P}L + kk;")
         if sg["split"]:
             L.append("          const float h = __uint_as_float(__float_as_uint(v) & 0xffffe000u);")
-            L.append(f"          ((float*)prm.p[{3 * j + 1}])[o] = h;")
-            L.append(f"          ((float*)prm.p[{3 * j + 2}])[o] = v - h;")
+            L.append(f"          hi{j}[o] = h;")
+            L.append(f"          lo{j}[o] = v - h;")
         else:
-            L.append(f"          (({dt}*)prm.p[{3 * j + 1}])[o] = tj_from<{dt}>(v);")
+            L.append(f"          hi{j}[o] = tj_from<{dt}>(v);")
         L.append("        }")
         L.append("      }")
         L.append("      __syncthreads();")
@@ -159,6 +171,9 @@ def gen_pack_operands(symbol: str, segments: list[dict]) -> KernelSource:
     nbytes = 0
     for sg in segments:
         args += [sg["src"], ("scratch", sg["hi"]), ("scratch", sg.get("lo", sg["hi"]))]
+    if chk:
+        args.append(("status", None))
+    for sg in segments:
         n_src = sg["mats"] * sg["rows"] * sg["K"]
         n_dst = sg["mats"] * sg["rows"] * sg["pitch"]
         nbytes += n_src * ITEM[sg["src_dtype"]] + n_dst * ITEM[sg["dst_dtype"]] * (2 if sg["split"] else 1)
@@ -169,16 +184,17 @@ def gen_pack_operands(symbol: str, segments: list[dict]) -> KernelSource:
     return ks
 
 
-def gen_epilogue_only(k: PKernel, symbol: str) -> KernelSource:
+def gen_epilogue_only(k: PKernel, symbol: str, kernel_id: int = 0) -> KernelSource:
     """A matmul whose every dot product is empty (K == 0), or which has no output element: the
     epilogue over a zero accumulator as one grid-stride launch (none when nothing is stored)."""
     mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
     ins, outs = list(k.inputs), list(k.outputs)
     in_index = {n.id: j for j, n in enumerate(ins)}
     out_index = {o.id: len(ins) + j for j, o in enumerate(outs)}
-    epi = Epilogue(k, in_index, out_index)
+    chk = checked()
+    epi = Epilogue(k, in_index, out_index, kernel_id, len(ins) + len(outs))
     total = prod(out_shape[:-2]) * M * N
-    L = [HEADER, params_struct(len(ins) + len(outs), 0),
+    L = [HEADER, params_struct(len(ins) + len(outs) + (1 if chk else 0), 0),
          f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{']
     L += ["  " + x for x in epi._ptr_lines()]
     L.append(f"  for (long e = (long)blockIdx.x * 256 + threadIdx.x; e < {total}L; e += (long)gridDim.x * 256) {{")
@@ -190,7 +206,7 @@ def gen_epilogue_only(k: PKernel, symbol: str) -> KernelSource:
     L += ["  }", "}"]
     grid = min((total + 255) // 256, NUM_SMS * 8) if total else 0
     ks = KernelSource(symbol, "ewise", "\n".join(L), (grid, 1, 1), (256, 1, 1),
-                      [("node", n) for n in ins] + [("node", o) for o in outs],
+                      [("node", n) for n in ins] + [("node", o) for o in outs] + ([("status", None)] if chk else []),
                       info={"bytes": sum(n.nbytes for n in k.inputs if n is not a and n is not b)
                             + sum(o.nbytes for o in outs), "numel": total, "flops": 0.0})
     ks.finalize_params()
@@ -208,7 +224,7 @@ def gen_matmul(k: PKernel, symbol: str, kernel_id: int, tile: dict | None) -> li
     finalize]; or the epilogue alone when there is nothing to multiply."""
     form = gemm_form(k)
     if form.mode == "empty":
-        return [gen_epilogue_only(k, symbol)]
+        return [gen_epilogue_only(k, symbol, kernel_id)]
     if form.mode == "x3":
         return gen_matmul_tc_x3(k, symbol, kernel_id, tile)
     if not (form.pack_a or form.pack_b):
@@ -223,7 +239,7 @@ def gen_matmul(k: PKernel, symbol: str, kernel_id: int, tile: dict | None) -> li
         segs.append(_operand_segment(a, M, K, P, True, False, a.dtype, a_off, a_off))
     if form.pack_b:
         segs.append(_operand_segment(b, N, K, P, tb, False, b.dtype, b_off, b_off))
-    pk = gen_pack_operands(f"{symbol}_pack", segs)
+    pk = gen_pack_operands(f"{symbol}_pack", segs, kernel_id)
     g = gen_gemm_tc(k, symbol, kernel_id, tile, packed={"a": a_off if form.pack_a else None,
                                                         "b": b_off if form.pack_b else None, "pitch": P})
     for ks in (pk, g):
@@ -231,7 +247,7 @@ def gen_matmul(k: PKernel, symbol: str, kernel_id: int, tile: dict | None) -> li
     return [pk, g]
 
 
-def gen_split_tf32(symbol: str, segments: list[tuple]) -> KernelSource:
+def gen_split_tf32(symbol: str, segments: list[tuple], kernel_id: int = 0) -> KernelSource:
     """x -> (hi, lo) with hi = x with its 13 low mantissa bits cleared (exactly a TF32 value)
     and lo = x - hi (exact in f32): the operand split of 3xTF32 (hi*hi + hi*lo + lo*hi keeps
     ~21 mantissa bits of every product).  ``segments`` = [(numel, src, hi_off, lo_off), ...]:
@@ -241,9 +257,12 @@ def gen_split_tf32(symbol: str, segments: list[tuple]) -> KernelSource:
         acc += numel // 4
         bounds.append(acc)
     nseg = len(segments)
-    L = [HEADER, params_struct(3 * nseg, 0),
-         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{',
-         f"  for (long g = (long)blockIdx.x * 256 + threadIdx.x; g < {acc}L; g += (long)gridDim.x * 256) {{",
+    chk = checked()
+    L = [HEADER, params_struct(3 * nseg + (1 if chk else 0), 0),
+         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{']
+    if chk:
+        L.append("  " + status_decl(3 * nseg))
+    L += [f"  for (long g = (long)blockIdx.x * 256 + threadIdx.x; g < {acc}L; g += (long)gridDim.x * 256) {{",
          "    int s = 0;",
          "    long i = g;"]
     for j in range(nseg - 1):
@@ -256,6 +275,12 @@ def gen_split_tf32(symbol: str, segments: list[tuple]) -> KernelSource:
             e = f"(s == {j} ? prm.p[{3 * j + slot}] : {e})"
         return e
 
+    if chk:   # the segment's index stays inside its operand (in float4 units)
+        n4 = f"{segments[-1][0] // 4}L"
+        for j in range(nseg - 2, -1, -1):
+            n4 = f"(s == {j} ? {segments[j][0] // 4}L : {n4})"
+        L.append(f"    if (!tj_check(i >= 0 && i < {n4}, tj_status, {kernel_id * 16 + BOUNDS_SITE}, 3 * s, i)) "
+                 "continue;")
     L += [f"    const float4* __restrict__ x = (const float4*){pick(0)};",
           f"    float4* __restrict__ hi = (float4*){pick(1)};",
           f"    float4* __restrict__ lo = (float4*){pick(2)};",
@@ -273,6 +298,8 @@ def gen_split_tf32(symbol: str, segments: list[tuple]) -> KernelSource:
     args = []
     for _numel, src, hi_off, lo_off in segments:
         args += [src, ("scratch", hi_off), ("scratch", lo_off)]
+    if chk:
+        args.append(("status", None))
     total = sum(sg[0] for sg in segments)
     ks = KernelSource(symbol, "split", "\n".join(L), (grid, 1, 1), (256, 1, 1), args,
                       info={"bytes": total * 12, "numel": total})
@@ -335,35 +362,36 @@ def gen_matmul_tc_x3(k: PKernel, symbol: str, kernel_id: int, tile: dict | None)
     if a.dtype == b.dtype == "f32" and tb and K % 4 == 0:
         # both operands already K-major f32 with a 16-byte pitch: the vectorised split
         sp = gen_split_tf32(f"{symbol}_split", [(a.numel, ("node", a), a_hi, a_lo),
-                                                (b.numel, ("node", b), b_hi, b_lo)])
+                                                (b.numel, ("node", b), b_hi, b_lo)], kernel_id)
     else:
         sp = gen_pack_operands(f"{symbol}_split", [_operand_segment(a, M, K, P, True, True, "f32", a_hi, a_lo),
-                                                   _operand_segment(b, N, K, P, tb, True, "f32", b_hi, b_lo)])
+                                                   _operand_segment(b, N, K, P, tb, True, "f32", b_hi, b_lo)],
+                               kernel_id)
     g = gen_gemm_tc(k, symbol, kernel_id, tile, x3_scratch=(a_hi, b_hi, a_lo, b_lo),
                     ksplit=ksplit, partial_scratch=part)
     parts = [sp, g]
     if ksplit > 1:
-        parts.append(gen_ksplit_finalize(k, f"{symbol}_finalize", g.args, ksplit))
+        parts.append(gen_ksplit_finalize(k, f"{symbol}_finalize", g.args, ksplit, kernel_id))
     for ks in parts:
         ks.info["scratch_bytes"] = ws
     return parts
 
 
-def gen_ksplit_finalize(k: PKernel, symbol: str, args: list, ksplit: int) -> KernelSource:
+def gen_ksplit_finalize(k: PKernel, symbol: str, args: list, ksplit: int, kernel_id: int = 0) -> KernelSource:
     """out = epilogue(sum over the K slices of the partial sums): the second half of a split-K
     GEMM.  Takes the GEMM launch's argument list, so operand indices are the same."""
     mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
     ins, outs = list(k.inputs), list(k.outputs)
     in_index = {n.id: j for j, n in enumerate(ins)}
     out_index = {o.id: len(ins) + j for j, o in enumerate(outs)}
-    epi = Epilogue(k, in_index, out_index)
+    epi = Epilogue(k, in_index, out_index, kernel_id, len(ins) + len(outs))   # the GEMM's status argument
     batch = prod(out_shape[:-2])
     total = batch * M * N
     part_idx = len(args) - 1
     L = [HEADER, params_struct(len(args), 0),
-         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{',
-         f"  const float* __restrict__ part = (const float*)prm.p[{part_idx}];"]
+         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{']
     L += ["  " + x for x in epi._ptr_lines()]
+    L.append("  " + ptr_decl("part", "float", part_idx, ksplit * total, True, kernel_id))
     L.append(f"  for (long e = (long)blockIdx.x * 256 + threadIdx.x; e < {total}L; e += (long)gridDim.x * 256) {{")
     L.append(f"    const long j = e % {N}L, row = e / {N}L, i = row % {M}L, b = row / {M}L;")
     L.append("    float acc = 0.0f;")
@@ -388,8 +416,10 @@ class Epilogue:
     """Emits the per-element epilogue of a matmul kernel: load epilogue inputs at
     (batch, i, j), evaluate the DAG, store every escaping node."""
 
-    def __init__(self, k: PKernel, in_index: dict[int, int], out_index: dict[int, int]):
+    def __init__(self, k: PKernel, in_index: dict[int, int], out_index: dict[int, int], kernel_id: int = 0,
+                 status_idx: int | None = None):
         self.k = k
+        self.kernel_id, self.status_idx = kernel_id, status_idx
         mm, a, b, tb, M, N, K, out_shape = _mm_dims(k)
         self.mm, self.M, self.N, self.out_shape = mm, M, N, out_shape
         self.batch_shape = out_shape[:-2]
@@ -508,9 +538,7 @@ class Epilogue:
              "    #pragma unroll",
              "    for (int c = 0; c < 32; ++c) out[c] = 0.0f;",
              f"    if (i >= {self.M}L) return;"]
-        for n in self.epi_inputs:
-            idx = self.in_index[n.id]
-            L.append(f"    const {CTYPE[n.dtype]}* __restrict__ in{idx} = (const {CTYPE[n.dtype]}*)prm.p[{idx}];")
+        L += ["    " + x for x in self._status_lines() + self._in_lines()]
         bl, bidx = self.batch_index_lines("b")
         L += ["    " + s for s in bl]
         L.append("    #pragma unroll")
@@ -542,14 +570,18 @@ class Epilogue:
         L.append("  }")
         return "\n".join(L)
 
+    def _status_lines(self) -> list[str]:
+        return [status_decl(self.status_idx)] if checked() else []
+
+    def _in_lines(self) -> list[str]:
+        return [ptr_decl(f"in{self.in_index[n.id]}", CTYPE[n.dtype], self.in_index[n.id], n.numel, True, self.kernel_id)
+                for n in self.epi_inputs]
+
     def _ptr_lines(self) -> list[str]:
-        L = []
-        for n in self.epi_inputs:
-            idx = self.in_index[n.id]
-            L.append(f"const {CTYPE[n.dtype]}* __restrict__ in{idx} = (const {CTYPE[n.dtype]}*)prm.p[{idx}];")
+        L = self._status_lines() + self._in_lines()
         for o in self.k.outputs:
             oi = self.out_index[o.id]
-            L.append(f"{CTYPE[o.dtype]}* __restrict__ out{oi} = ({CTYPE[o.dtype]}*)prm.p[{oi}];")
+            L.append(ptr_decl(f"out{oi}", CTYPE[o.dtype], oi, o.numel, False, self.kernel_id))
         return L
 
     def scalar_element_lines(self, bidx: list[str], ivar: str, jvar: str, acc: str) -> list[str]:
@@ -571,20 +603,23 @@ class Epilogue:
 # ---------------------------------------------------------------------------
 # tcgen05 kernel
 # ---------------------------------------------------------------------------
-def partial_store_function(M: int, N: int, part_idx: int) -> str:
+def partial_store_function(M: int, N: int, part_idx: int, numel: int = 0, kernel_id: int = 0,
+                           status_idx: int = 0) -> str:
     """``epilogue(prm, b, i, j0, acc[32])`` of a split-K GEMM: the raw f32 accumulator row
     into partial-sum slice ``b`` (= slice * batch + batch index) of the workspace."""
     vec = N % 4 == 0
     L = ["  template <class P>",
          "  static __device__ __forceinline__ void epilogue(const P& prm, long b, long i, long j0, const float (&acc)[32]) {",
          f"    if (i >= {M}L) return;",
-         f"    float* __restrict__ row = (float*)prm.p[{part_idx}] + (b * {M}L + i) * {N}L;",
+         *(["    " + status_decl(status_idx)] if checked() else []),
+         "    " + ptr_decl("part", "float", part_idx, numel, False, kernel_id),
+         f"    const auto row = part + (b * {M}L + i) * {N}L;",
          "    #pragma unroll",
          "    for (int c = 0; c < 32; c += 4) {",
          "      const long j = j0 + c;"]
     if vec:
         L += [f"      if (j >= {N}L) break;",
-              "      *reinterpret_cast<float4*>(row + j) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);"]
+              "      tj_store_vec(row + j, &acc[c]);"]
     else:
         L += ["      #pragma unroll",
               f"      for (int u = 0; u < 4; ++u) if (j + u < {N}L) row[j + u] = acc[c + u];"]
@@ -632,7 +667,7 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     # + status word (+ hi/lo operand copies) (+ packed operands) (+ the partial sums of a split-K GEMM)
     nptr = len(ins) + len(outs) + 1 + (4 if x3 else 0) + int(pk_a) + int(pk_b) + (1 if ksplit > 1 else 0)
     status_idx = len(ins) + len(outs)
-    epi = Epilogue(k, in_index, out_index)
+    epi = Epilogue(k, in_index, out_index, kernel_id, status_idx)
     # B is read N-major only in place from a plan matmul without trans_b; the workspace copies
     # (3xTF32 hi / lo, packed operands) are always K-major
     b_mn = not (tb or pk_b or x3)
@@ -654,14 +689,16 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     epi_warps = 8 if (BN % 64 == 0 or pair) else 4
     threads = 64 + 32 * epi_warps
     out_stage = epi_warps * 2 * 32 * 32 * 2 if tma_store else 0
+    GROUP_N = int((tile or {}).get("GROUP_N", 0))
     L.append(f"  static constexpr int BN = {BN}, STAGES = {STAGES}, M = {M}, N = {N}, K = {K}, GROUP_M = {GROUP_M};")
+    L.append(f"  static constexpr int GROUP_N = {GROUP_N};")
     L.append(f"  static constexpr int EPI_WARPS = {epi_warps}, KSPLIT = {ksplit}, NSEG = 1;")
     L.append("  static __device__ __forceinline__ int segment(int) { return 0; }")
     L.append("  static __device__ __forceinline__ int seg_tile0(int) { return 0; }")
     L.append(f"  static constexpr bool TF32X3 = {'true' if x3 else 'false'};")
     L.append(f"  static constexpr bool TMA_STORE = {'true' if tma_store else 'false'};")
     L.append(f"  using OutT = {CTYPE[outs[0].dtype] if tma_store else 'float'};")
-    L.append(f"  static constexpr long BATCH = {batch}L;")
+    L.append(f"  static constexpr long BATCH = {batch}L, A_MATS = {a_mats}L, B_MATS = {b_mats}L;")
     L.append(f"  static constexpr bool BF16 = {'true' if a.dtype == 'bf16' else 'false'}, B_MN_MAJOR = {'true' if b_mn else 'false'};")
     L.append("  static __device__ __forceinline__ void batch_map(long b, long& ab, long& bb_) {")
     L += ["    " + s for s in bl]
@@ -669,7 +706,7 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     L.append(f"    bb_ = {offset_expr(bidx, b_bs) if batch_shape else '0L'};")
     L.append("  }")
     if ksplit > 1:
-        L.append(partial_store_function(M, N, nptr - 1))
+        L.append(partial_store_function(M, N, nptr - 1, ksplit * batch * M * N, kernel_id, status_idx))
     else:
         L.append(epi.vals32_function() if tma_store else epi.chunk32_function())
     L.append("};")
@@ -762,10 +799,11 @@ def gen_gemm_multi(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = 
          params_struct(status_idx + 1, 1 + len(parts))]
     L.append("struct Cfg {")
     L.append(f"  static constexpr int BN = {BN}, STAGES = {STAGES}, M = {M}, N = {N}, K = {K}, GROUP_M = {GROUP_M};")
+    L.append(f"  static constexpr int GROUP_N = {int((tile or {}).get('GROUP_N', 0))};")
     L.append(f"  static constexpr int EPI_WARPS = 8, KSPLIT = 1, NSEG = {len(parts)};")
     L.append("  static constexpr bool TF32X3 = false, TMA_STORE = false;")
     L.append("  using OutT = float;")
-    L.append("  static constexpr long BATCH = 1L;")
+    L.append("  static constexpr long BATCH = 1L, A_MATS = 1L, B_MATS = 1L;")
     L.append(f"  static constexpr bool BF16 = {'true' if dt == 'bf16' else 'false'}, B_MN_MAJOR = false;")
     L.append("  static __device__ __forceinline__ void batch_map(long, long& ab, long& bb_) { ab = 0; bb_ = 0; }")
     seg = " : ".join(f"nt < {starts[g] + seg_tiles[g]} ? {g}" for g in range(len(parts) - 1)) + f" : {len(parts) - 1}"
@@ -780,8 +818,10 @@ def gen_gemm_multi(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = 
             L.append("    else {")
         else:
             L.append(f"    {'if' if g == 0 else 'else if'} (j0 < {col0[g] + ng}L) {{")
-        L.append(f"      {CTYPE[onode.dtype]}* __restrict__ dst = ({CTYPE[onode.dtype]}*)prm.p[{len(ins) + g}] + "
-                 f"i * {ng}L + (j0 - {col0[g]}L);")
+        if checked():
+            L.append("      " + status_decl(status_idx))
+        L.append("      " + ptr_decl("outg", CTYPE[onode.dtype], len(ins) + g, onode.numel, False, kernel_id))
+        L.append(f"      const auto dst = outg + (i * {ng}L + (j0 - {col0[g]}L));")
         L.append("      #pragma unroll")
         L.append("      for (int c = 0; c < 32; c += 8) tj_store_vec(dst + c, acc + c);")
         L.append("    }")

@@ -19,7 +19,8 @@ one CTA's registers, so no cluster is needed.
 from __future__ import annotations
 
 from ..plan import PKernel, PNode, broadcast_strides
-from .common import CTYPE, HEADER, KernelSource, expr, fast_math_for, literal, offset_expr, params_struct, pick_vec, prod
+from .common import (CTYPE, HEADER, KernelSource, checked, expr, fast_math_for, literal, offset_expr, params_struct,
+                     pick_vec, prod, ptr_decl, status_decl)
 
 CTA_THREADS = 256
 
@@ -38,7 +39,8 @@ def _geometry(N: int, VEC: int) -> tuple[int, int, int]:
     return tpr, vpt, rpc
 
 
-def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str) -> KernelSource:
+def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str,
+            kernel_id: int = 0) -> KernelSource:
     rows = tuple(rows)
     nrows = prod(rows)
     vec_shape = rows + (N,)
@@ -81,12 +83,16 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str)
     block = TPR * RPC
     grid = (nrows + RPC - 1) // RPC if nrows else 0
 
-    L = [HEADER, params_struct(len(ins) + len(outs), 0)]
+    chk = checked()
+    nargs = len(ins) + len(outs) + (1 if chk else 0)     # + the status words in a checked build
+    L = [HEADER, params_struct(nargs, 0)]
     entry_at = len(L)   # the entry line is added once the per-thread register arrays are known
+    if chk:
+        L.append("  " + status_decl(len(ins) + len(outs)))
     for j, n in enumerate(ins):
-        L.append(f"  const {CTYPE[n.dtype]}* __restrict__ in{j} = (const {CTYPE[n.dtype]}*)prm.p[{j}];")
+        L.append("  " + ptr_decl(f"in{j}", CTYPE[n.dtype], j, n.numel, True, kernel_id))
     for j, o in enumerate(outs):
-        L.append(f"  {CTYPE[o.dtype]}* __restrict__ out{j} = ({CTYPE[o.dtype]}*)prm.p[{len(ins) + j}];")
+        L.append("  " + ptr_decl(f"out{j}", CTYPE[o.dtype], len(ins) + j, o.numel, False, kernel_id))
     nred = sum(1 for st in stages if st.kind == "reduce")
     if TPR > 32 and nred:
         L.append(f"  __shared__ float red[{nred}][{RPC}][{NW}];")
@@ -393,7 +399,8 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str)
         L.append("  }")
     L.append("}")
     nbytes = sum(n.nbytes for n in ins) + sum(o.nbytes for o in outs)
-    ks = KernelSource(symbol, "row", "\n".join(L), (grid, 1, 1), (block, 1, 1), [("node", n) for n in ins + outs],
+    ks = KernelSource(symbol, "row", "\n".join(L), (grid, 1, 1), (block, 1, 1),
+                      [("node", n) for n in ins + outs] + ([("status", None)] if chk else []),
                       info={"vec": VEC, "tpr": TPR, "vpt": VPT, "rpc": RPC, "rows": nrows, "n": N, "bytes": nbytes})
     ks.finalize_params()
     return ks

@@ -325,6 +325,10 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
     if (lane == 0) {
       // ---------------- TMA producer ----------------
       int c[5];
+#ifdef TJ_CHECKED
+      // checked build: this CTA's (batch x head) and query rows lie inside the operands
+      if (!tj_check(bh >= 0 && bh < Cfg::BATCH && q0 < Cfg::SQ, status, kernel_id * 16 + 15, -1, bh)) *abort_flag = 1;
+#endif
       mbar_expect_tx(smem_u32(q_full), ntiles * Q_BYTES);
       for (int t = 0; t < ntiles; ++t) {
         Cfg::q_coords(bh, q0 + t * BM, c);
@@ -580,7 +584,14 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
           const float inv = 1.0f / l;
           float o[32];
           tmem_ld32(tO, o);
-          if (row < Cfg::SQ) {
+          bool store = row < Cfg::SQ;
+#ifdef TJ_CHECKED
+          // checked build: this thread's 32 output columns lie inside O
+          if (store)
+            store = tj_check(Cfg::out_offset(bh, row) >= 0 && Cfg::out_offset(bh, row) + h * 32 + 32 <= Cfg::O_NUMEL,
+                             status, kernel_id * 16 + 15, -3, row);
+#endif
+          if (store) {
             T* orow = out + Cfg::out_offset(bh, row) + h * 32;
 #pragma unroll
             for (int v = 0; v < 4; ++v) {

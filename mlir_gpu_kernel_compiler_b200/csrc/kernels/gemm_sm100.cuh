@@ -211,21 +211,32 @@ TJ_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // Grouped raster over (m, n) tiles inside one batch: GROUP_M m-tiles share the
 // same B columns while the whole group sweeps N, so concurrently running CTAs
 // reuse A and B tiles through L2.
-TJ_DEV void tile_coords(long t, int m_tiles, int n_tiles, int group_m, long& b, int& mt, int& nt) {
+// Tile order of the persistent kernels: batch by batch; inside a batch, bands of group_n column
+// tiles (0 = one band over all of N) are swept one after the other, and inside a band groups of
+// group_m row tiles, row tile fastest.  A band keeps its B panels in L2 for the whole sweep over
+// the rows, so with a wide K the weights are read from DRAM once per band instead of once per
+// wave of row tiles; each A panel is then read once per band.
+TJ_DEV void tile_coords(long t, int m_tiles, int n_tiles, int group_m, int group_n, long& b, int& mt, int& nt) {
   const long per_batch = static_cast<long>(m_tiles) * n_tiles;
   b = t / per_batch;
-  const long r = t - b * per_batch;
-  const long per_group = static_cast<long>(group_m) * n_tiles;
+  long r = t - b * per_batch;
+  const int gn = (group_n > 0 && group_n < n_tiles) ? group_n : n_tiles;
+  const long per_band = static_cast<long>(m_tiles) * gn;  // every band but the last is full
+  const int band = static_cast<int>(r / per_band);
+  const int n_first = band * gn;
+  const int bw = min(n_tiles - n_first, gn);
+  r -= static_cast<long>(band) * per_band;
+  const long per_group = static_cast<long>(group_m) * bw;
   const int g = static_cast<int>(r / per_group);
   const int first_m = g * group_m;
   const int gsize = min(m_tiles - first_m, group_m);
   const int in_g = static_cast<int>(r - static_cast<long>(g) * per_group);
   mt = first_m + in_g % gsize;
-  nt = in_g / gsize;
+  nt = n_first + in_g / gsize;
 }
 
 // Cfg provides:
-//   static constexpr int BN, STAGES, M, N, K, GROUP_M, EPI_WARPS, KSPLIT, NSEG; static constexpr long BATCH;
+//   static constexpr int BN, STAGES, M, N, K, GROUP_M, GROUP_N, EPI_WARPS, KSPLIT, NSEG; static constexpr long BATCH;
 //   (NSEG > 1: static __device__ int segment(int nt), seg_tile0(int g) map a column tile to its B operand)
 //   static constexpr bool BF16, B_MN_MAJOR, TMA_STORE;  using OutT = <output element type>;
 //   static __device__ void batch_map(long b, long& a_batch, long& b_batch);
@@ -335,7 +346,7 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
         const int kb0 = static_cast<int>(w % KSPLIT) * KPB, kb1 = min(kb0 + KPB, k_blocks);
         long b;
         int mt, nt;
-        tile_coords(t, m_tiles, n_tiles, Cfg::GROUP_M, b, mt, nt);
+        tile_coords(t, m_tiles, n_tiles, Cfg::GROUP_M, Cfg::GROUP_N, b, mt, nt);
         long ab, bb;
         Cfg::batch_map(b, ab, bb);
         const int a_row = static_cast<int>(ab * Cfg::M + static_cast<long>(mt) * BM);
@@ -361,6 +372,18 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
               phase ^= 1u;
             }
             continue;
+          }
+#endif
+#ifdef TJ_CHECKED
+          // checked build: the tile walk stays inside the operands (a TMA load outside them would
+          // only zero-fill, so a wrong walk would otherwise go unnoticed); on a violation the CTA
+          // aborts like on a timeout
+          if (!tj_check(kb * BK < Cfg::K && mt * BM < Cfg::M && ab >= 0 && ab < Cfg::A_MATS && bb >= 0 &&
+                            bb < Cfg::B_MATS && n0 >= 0 && n0 < Cfg::N,
+                        status, kernel_id * 16 + 15, -1, static_cast<long>(kb))) {
+            *abort_flag = 1;
+            ok = false;
+            break;
           }
 #endif
           const uint32_t fb = smem_u32(&full[stage]);
@@ -453,7 +476,7 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
       const long t = w / KSPLIT;
       long b;
       int mt, nt;
-      tile_coords(t, m_tiles, n_tiles, Cfg::GROUP_M, b, mt, nt);
+      tile_coords(t, m_tiles, n_tiles, Cfg::GROUP_M, Cfg::GROUP_N, b, mt, nt);
       b += (w % KSPLIT) * Cfg::BATCH;  // partial-sum slice (KSPLIT > 1)
       const int buf = it & 1;
       const bool ok = mbar_wait(smem_u32(&tfull[buf]), (it >> 1) & 1, abort_flag, status, kernel_id * 16 + 4);
@@ -464,6 +487,9 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN + col0);
 #pragma unroll 1
       for (int c = 0; c < EPI_COLS / 32; ++c) {
+        // checked build: the accumulator columns read lie inside this CTA's TMEM allocation
+        TJ_CHECKED_ONLY(if (!tj_check(buf * BN + col0 + c * 32 + 32 <= static_cast<int>(TMEM_COLS), status,
+                                      kernel_id * 16 + 15, -2, c)) break;)
         float acc[32];
         tmem_ld32(tbase + c * 32, acc);
         const long j0 = static_cast<long>(nt) * BN + col0 + c * 32;

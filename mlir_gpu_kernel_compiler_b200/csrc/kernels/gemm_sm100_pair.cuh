@@ -205,7 +205,7 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
       for (long t = cluster_id; t < num_tiles && ok; t += num_clusters) {
         long b;
         int mt, nt;
-        tile_coords(t, m_tiles, n_tiles, Cfg::GROUP_M, b, mt, nt);
+        tile_coords(t, m_tiles, n_tiles, Cfg::GROUP_M, Cfg::GROUP_N, b, mt, nt);
         long ab, bb;
         Cfg::batch_map(b, ab, bb);
         const int a_row = static_cast<int>(ab * Cfg::M + static_cast<long>(mt) * BM + rank * 128);
@@ -232,6 +232,17 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
               phase ^= 1u;
             }
             continue;
+          }
+#endif
+#ifdef TJ_CHECKED
+          // checked build: the tile walk stays inside the operands; a violation aborts both CTAs
+          if (!tj_check(kb * BK < Cfg::K && mt * BM < Cfg::M && ab >= 0 && ab < Cfg::A_MATS && bb >= 0 &&
+                            bb < Cfg::B_MATS && nt * BN < Cfg::N,
+                        status, kernel_id * 16 + 15, -1, static_cast<long>(kb))) {
+            *abort_flag = 1;
+            st_cluster_u32(peer_abort, 1u);
+            ok = false;
+            break;
           }
 #endif
           const uint32_t leader_full = mapa_shared(smem_u32(&full[stage]), 0);
@@ -302,7 +313,7 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
     for (long t = cluster_id; t < num_tiles; t += num_clusters, ++it) {
       long b;
       int mt, nt;
-      tile_coords(t, m_tiles, n_tiles, Cfg::GROUP_M, b, mt, nt);
+      tile_coords(t, m_tiles, n_tiles, Cfg::GROUP_M, Cfg::GROUP_N, b, mt, nt);
       const int buf = it & 1;
       const bool ok = mbar_wait_pair(smem_u32(&tfull[buf]), (it >> 1) & 1, abort_flag, peer_abort, status,
                                      kernel_id * 16 + 4);
@@ -314,6 +325,8 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN + col0);
 #pragma unroll 1
       for (int c = 0; c < EPI_COLS / 32; ++c) {
+        TJ_CHECKED_ONLY(if (!tj_check(buf * BN + col0 + c * 32 + 32 <= static_cast<int>(TMEM_COLS), status,
+                                      kernel_id * 16 + 15, -2, c)) break;)
         float acc[32];
         tmem_ld32(tbase + c * 32, acc);
         const long j0 = static_cast<long>(nt) * BN + col0 + c * 32;

@@ -141,3 +141,78 @@ TJ_DEV uint64_t tj_globaltimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+
+// ---------------------------------------------------------------------------
+// checked build (-DTJ_CHECKED, TENSORJIT_B200_CHECKED=1): the generated kernels declare their
+// global operands as bounded views instead of raw pointers, so every computed element index of
+// a load or store is compared with the operand's element count first.  A violation skips the
+// access (loads read 0) and records (TJ_STATUS_BOUNDS, kernel * 16 + 15) in the program's
+// status words, with the operand's argument index and the offending element offset in words 2
+// and 3.  The unchecked build never sees these types.
+// ---------------------------------------------------------------------------
+#ifdef TJ_CHECKED
+TJ_DEV void tj_report_bounds(int* status, int where, int arg, long off) {
+  if (status && atomicCAS(status, 0, TJ_STATUS_BOUNDS) == 0) {
+    status[1] = where;
+    status[2] = arg;
+    status[3] = static_cast<int>(off > 0x7fffffffL ? 0x7fffffffL : (off < -0x7fffffffL ? -0x7fffffffL : off));
+  }
+}
+// element reference through a view: reads give 0 and writes are dropped when out of bounds
+template <class T> struct tj_ref {
+  T* p;
+  bool ok;
+  TJ_DEV tj_ref& operator=(T v) {
+    if (ok) *p = v;
+    return *this;
+  }
+  TJ_DEV operator T() const { return ok ? *p : T(); }
+};
+// a view plus an element offset (what `view + off` yields; vector accesses check all 16 bytes)
+template <class T> struct tj_cptr {
+  T* p;
+  long n;
+  int* status;
+  int where, arg;
+  long off;
+  TJ_DEV tj_cptr operator+(long d) const { return tj_cptr{p, n, status, where, arg, off + d}; }
+  TJ_DEV bool check(long len) const {
+    const bool ok = off >= 0 && off + len <= n;
+    if (!ok) tj_report_bounds(status, where, arg, off);
+    return ok;
+  }
+  TJ_DEV tj_ref<T> operator[](long i) const { return (*this + i).deref(); }
+  TJ_DEV tj_ref<T> deref() const {
+    const bool ok = check(1);
+    return tj_ref<T>{p + (ok ? off : 0), ok};
+  }
+};
+template <class T> struct tj_view {
+  T* p;
+  long n;
+  int* status;
+  int where, arg;
+  TJ_DEV tj_cptr<T> operator+(long d) const { return tj_cptr<T>{p, n, status, where, arg, d}; }
+  TJ_DEV tj_ref<T> operator[](long i) const { return (*this + i).deref(); }
+};
+template <typename T> TJ_DEV void tj_load_vec(tj_cptr<const T> q, float* f) {
+  if (!q.check(TjVec<T>::N)) {
+#pragma unroll
+    for (int i = 0; i < TjVec<T>::N; ++i) f[i] = 0.0f;
+    return;
+  }
+  tj_load_vec(q.p + q.off, f);
+}
+template <typename T> TJ_DEV void tj_load_vec_stream(tj_cptr<const T> q, float* f) { tj_load_vec(q, f); }
+template <typename T> TJ_DEV void tj_store_vec(tj_cptr<T> q, const float* f) {
+  if (q.check(TjVec<T>::N)) tj_store_vec(q.p + q.off, f);
+}
+// a condition the generated code asserts (a TMA coordinate, a TMEM column): false = violation
+TJ_DEV bool tj_check(bool ok, int* status, int where, int arg, long what) {
+  if (!ok) tj_report_bounds(status, where, arg, what);
+  return ok;
+}
+#define TJ_CHECKED_ONLY(...) __VA_ARGS__
+#else
+#define TJ_CHECKED_ONLY(...)
+#endif

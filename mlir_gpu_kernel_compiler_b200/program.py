@@ -32,7 +32,7 @@ from .codegen import generate
 from .fuse import fuse
 from .memory import MemoryPlan, plan_memory
 from .plan import PNode, PProgram, as_plan
-from .toolchain import compile_cubins
+from .toolchain import CHECKED_FLAGS, compile_cubins
 
 TORCH_DTYPE = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16, "i32": torch.int32}
 FROM_TORCH = {v: k for k, v in TORCH_DTYPE.items()}
@@ -83,7 +83,8 @@ class B200Program:
     backend = "b200"
 
     def __init__(self, program, device: str | torch.device = "cuda", use_graph: Optional[bool] = None,
-                 tune: bool = True, tiles: dict | None = None, nvcc_flags: tuple = (), fuse_kernels: bool = True):
+                 tune: bool = True, tiles: dict | None = None, nvcc_flags: tuple = (), fuse_kernels: bool = True,
+                 checked: Optional[bool] = None):
         self.program = program
         self.pplan: PProgram = as_plan(program)
         self.device = torch.device(device)
@@ -98,10 +99,13 @@ class B200Program:
 
             tiles = tiles_for_plan(self.xplan)
         _trace("tiles", tiles)
-        self.kernel_sources = generate(self.xplan, tiles=tiles)
+        # checked build: every global access bounds-checked, violations reported as TJ_STATUS_BOUNDS
+        self.checked = (os.environ.get("TENSORJIT_B200_CHECKED") == "1") if checked is None else bool(checked)
+        self.kernel_sources = generate(self.xplan, tiles=tiles, checked=self.checked)
         _trace("generated")
         self.source = "\n\n".join(ks.source for ks in self.kernel_sources)
-        self.cubins = compile_cubins([(ks.symbol, ks.source) for ks in self.kernel_sources], tuple(nvcc_flags))
+        flags = tuple(nvcc_flags) + (CHECKED_FLAGS if self.checked else ())
+        self.cubins = compile_cubins([(ks.symbol, ks.source) for ks in self.kernel_sources], flags)
         _trace("compiled")
         self.use_graph = (os.environ.get("TENSORJIT_B200_GRAPH", "1") == "1") if use_graph is None else use_graph
         g = self.xplan
@@ -259,11 +263,13 @@ class B200Program:
         return [(tuple(o.shape), TORCH_DTYPE[o.dtype]) for o in self._out_nodes]
 
     def check(self) -> None:
-        """Synchronise and raise if any kernel of this program reported a failure."""
+        """Synchronise and raise if any kernel of this program reported a failure (a bounded wait
+        that ran out, or in a checked build an out-of-range access)."""
         code, where = self.native.check_status()
         if code:
+            what = {1: "wait timeout", 2: "out-of-bounds access"}.get(code, f"status {code}")
             raise rt.RuntimeError_(rt.TJ_ERR_DEVICE_STATUS,
-                                   f"kernel status {code} (kernel {where // 16}, site {where % 16})")
+                                   f"kernel {what} (kernel {where // 16}, site {where % 16})")
 
     def close(self) -> None:
         if self._native is not None:

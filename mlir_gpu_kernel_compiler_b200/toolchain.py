@@ -36,6 +36,9 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr", "-Xp
 # wait gives up after 20 ms, so the timeout reporting can be tested without a GPU fault
 STALL_TEST_FLAGS = ("-DTJ_TEST_STALL_FIRST_LOAD", "-DTJ_WAIT_NS=20000000ull")
 
+# the checked kernel build (every global access and TMA coordinate bounds-checked on the device)
+CHECKED_FLAGS = ("-DTJ_CHECKED",)
+
 _lock = threading.Lock()
 
 

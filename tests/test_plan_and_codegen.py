@@ -417,3 +417,33 @@ def test_compile_batch_with_repeated_source(tmp_path, monkeypatch):
     assert a == b and a[:4] == b"\x7fELF" and c != a
     suffixes = [p.suffix for p in tmp_path.iterdir()]
     assert suffixes.count(".cubin") == 2 and ".tmp" not in suffixes
+
+
+def test_checked_build_bounds_checks_every_kernel_family():
+    """TENSORJIT_B200_CHECKED: every generated kernel gets the status words and declares its
+    global operands as bounded views (element counts baked in); the GEMM and attention
+    templates receive the operand extents their coordinate checks use.  The normal build
+    contains none of it."""
+    from mlir_gpu_kernel_compiler_b200.fuse import fuse
+
+    seen = set()
+    for case in ("cuda_rows__f32", "ew_chain_8x33__bf16", "cfg1", "matmul_epi_7x13x5__bf16",
+                 "linear_splitk_ragged__f32", "attention_heads__bf16", "shared_a_projections__bf16",
+                 "matmul_epi_1x1x1__f32"):
+        plan = fuse(FX.load_plan(case))
+        plain = generate(plan)
+        chk = generate(plan, checked=True)
+        assert [k.symbol for k in plain] == [k.symbol for k in chk]
+        for k0, k1 in zip(plain, chk):
+            seen.add(k1.family)
+            assert "tj_view" not in k0.source and "tj_status" not in k0.source
+            assert ("status", None) in k1.args
+            if k1.family in ("ewise", "copy", "row", "split"):
+                assert "tj_view<" in k1.source or "tj_check(" in k1.source, (case, k1.symbol)
+            if k1.family == "gemm_tc":
+                assert "A_MATS" in k1.source
+            if k1.family == "attention":
+                assert "O_NUMEL" in k1.source
+            k1.finalize_params()
+            assert k1.param_bytes >= 8 * len(k1.args)
+    assert {"ewise", "row", "split", "gemm_tc", "attention"} <= seen
