@@ -18,6 +18,9 @@
 
 #include <cuda.h>
 #include <dlfcn.h>
+// NVTX ranges name every plan kernel on a profiler timeline (nsys / ncu --nvtx).  NVTX v3 is
+// header-only: without a tool attached the calls return at once.
+#include <nvtx3/nvToolsExt.h>
 
 #include <chrono>
 #include <cstdarg>
@@ -177,6 +180,7 @@ struct Program {
   CUgraph graph = nullptr;
   CUgraphExec exec = nullptr;
   uint64_t calls = 0, launches = 0, replays = 0, node_updates = 0, instantiations = 0;
+  std::string graph_label;  // NVTX range around a graph replay: "tj_b200 graph: <first> .. <last>"
   double host_us = 0.0;
   std::mutex mu;
 
@@ -269,7 +273,9 @@ int launch_direct(Program& p, KernelRec& k, CUstream s) {
   cfg.attrs = attr;
   cfg.numAttrs = nattr;
   void* kp[1] = {k.params.data()};
+  nvtxRangePushA(k.symbol.c_str());
   CUresult r = drv().cuLaunchKernelEx(&cfg, k.fn, kp, nullptr);
+  nvtxRangePop();
   if (r != CUDA_SUCCESS) return cu_fail(r, ("cuLaunchKernelEx " + k.symbol).c_str());
   p.launches++;
   return TJ_OK;
@@ -460,6 +466,9 @@ int tj_b200_program_create(const void* const* cubins, const size_t* cubin_sizes,
   }
   TJ_CU(d.cuMemAlloc_v2(&p->status, 16), "cuMemAlloc(status)");
   TJ_CU(d.cuMemsetD32_v2(p->status, 0, 4), "cuMemsetD32(status)");
+  if (!p->kernels.empty())
+    p->graph_label = "tj_b200 graph: " + p->kernels.front().symbol +
+                     (p->kernels.size() > 1 ? " .. " + p->kernels.back().symbol : std::string());
   *out_program = p.release();
   return TJ_OK;
 }
@@ -503,7 +512,10 @@ int tj_b200_run(void* program, const void* const* inputs, void* const* outputs, 
         p.node_updates++;
       }
     }
-    TJ_CU(drv().cuGraphLaunch(p.exec, s), "cuGraphLaunch");
+    nvtxRangePushA(p.graph_label.c_str());   // the graph's kernel nodes carry the plan kernels' names
+    const CUresult gr = drv().cuGraphLaunch(p.exec, s);
+    nvtxRangePop();
+    TJ_CU(gr, "cuGraphLaunch");
     p.replays++;
   }
   p.calls++;
