@@ -14,7 +14,9 @@ transpose that only feeds Q, K or V (or only consumes O) into that kernel's
 addressing, so the copy kernel disappears as well.
 
 ``fuse_shared_a_gemms`` merges consecutive bare GEMMs that read the same A operand (the
-q / k / v projections of a transformer block) into one ``matmul_multi`` kernel.
+q / k / v projections of a transformer block) into one ``matmul_multi`` kernel, and
+``absorb_elementwise_epilogues`` moves an elementwise kernel that only post-processes a GEMM's
+output (a residual add) into that GEMM's epilogue.
 
 The attention rewrite is semantic-preserving for the plan's outputs only: S and P must not
 escape (not graph outputs, no user outside the chain), otherwise the chain is left
@@ -271,9 +273,54 @@ def fuse_shared_a_gemms(plan: PProgram) -> PProgram:
                     aliases=plan.aliases, meta=dict(plan.meta, fused_shared_a=True))
 
 
+def absorb_elementwise_epilogues(plan: PProgram) -> PProgram:
+    """An elementwise kernel right after a matmul kernel joins that GEMM's epilogue when it
+    consumes the GEMM's only output, elementwise over exactly that output's shape, and nothing
+    else reads that output (it is no graph output either): e.g. the residual add after a
+    transformer MLP's down projection.  The GEMM then evaluates the added nodes on its f32
+    accumulator tile and stores only their outputs, so the intermediate never reaches HBM (and
+    is not rounded to the storage dtype in between).  The elementwise kernel's other inputs are
+    produced before the GEMM runs, since the plan is in execution order."""
+    from .codegen.common import EXPR
+    from .plan import access_strides, first_consumer
+
+    escaping = {plan.resolve(o).id for o in plan.outputs}
+    ks = plan.kernels
+    out: list[PKernel] = []
+    changed = 0
+    i = 0
+    while i < len(ks):
+        g = ks[i]
+        e = ks[i + 1] if i + 1 < len(ks) else None
+        if (e is not None and g.kind == "matmul" and e.kind == "elementwise" and len(g.outputs) == 1
+                and g.outputs[0] in e.inputs):
+            o = g.outputs[0]
+            shape = tuple(o.shape)
+            ok = (o.id not in escaping and tuple(e.iter_shape) == shape and _only_users(o, {n.id for n in e.nodes})
+                  and all(n.op in EXPR for n in e.nodes))
+            if ok:
+                c = first_consumer(o, e.nodes, e.nodes[0])
+                ok = tuple(access_strides(o, c, shape)) == contiguous_strides(shape)
+            if ok:
+                inputs = list(g.inputs) + [n for n in e.inputs if n is not o and n not in g.inputs]
+                fk = PKernel(kind="matmul", nodes=list(g.nodes) + list(e.nodes), anchor=g.anchor, inputs=inputs,
+                             outputs=list(e.outputs), iter_shape=tuple(g.iter_shape))
+                fk.attrs = dict(g.attrs)
+                out.append(fk)
+                changed += 1
+                i += 2
+                continue
+        out.append(g)
+        i += 1
+    if not changed:
+        return plan
+    return PProgram(name=plan.name, nodes=plan.nodes, inputs=plan.inputs, outputs=plan.outputs, kernels=out,
+                    aliases=plan.aliases, meta=dict(plan.meta, absorbed_epilogues=changed))
+
+
 def fuse(plan: PProgram) -> PProgram:
-    """All backend rewrites (``TENSORJIT_B200_FUSE=0`` disables them): attention chains, then
-    GEMMs that share their A operand."""
+    """All backend rewrites (``TENSORJIT_B200_FUSE=0`` disables them): attention chains, GEMMs
+    that share their A operand, then elementwise kernels absorbed into the GEMM before them."""
     if os.environ.get("TENSORJIT_B200_FUSE", "1") == "0":
         return plan
-    return fuse_shared_a_gemms(fuse_attention(plan))
+    return absorb_elementwise_epilogues(fuse_shared_a_gemms(fuse_attention(plan)))

@@ -150,6 +150,15 @@ def cases(tj):
         return tj.linear(tj.reshape(tj.permute(tj.matmul(s, v), 0, 2, 1, 3), (512, 256)), wo) * 0.0625
 
     add("attention_heads", mha, [(512, 128), (256, 128), (256, 128), (256, 128), (128, 256)], dtypes=(BF16,))
+
+    # a pre-norm block's tail: the residual add after the MLP is planned as its own elementwise
+    # kernel (x1 also feeds the LayerNorm), which the B200 backend folds into the GEMM epilogue
+    def block_tail(x, r, wo, g, w1, b1, w2, b2):
+        x1 = r + tj.linear(x, wo) * 0.0883883461
+        return x1 + tj.linear(tj.gelu(tj.linear(tj.layer_norm(x1, g), w1, b1) * 0.0883883461), w2, b2) * 0.0441941738
+
+    add("block_tail", block_tail, [(300, 128), (300, 128), (128, 128), (128,), (512, 128), (512,), (128, 512), (128,)],
+        dtypes=(F32, BF16))
     return C
 
 

@@ -361,10 +361,11 @@ def test_gemms_sharing_a_become_one_launch():
     assert all(t.box[1] == 128 for t in ks.tmaps[1:]) and "gemm_sm100_pair<Cfg>" in ks.source
     single = generate(p, tiles={0: {"BN": 256, "STAGES": 4, "GROUP_M": 16, "PAIR": False}})[0]
     assert not single.info["pair"] and single.cluster == (1, 1, 1) and single.tmaps[1].box[1] == 256
-    # cfg4: the q, k, v projections (same LayerNorm output) -> one launch; 16 plan kernels -> 8
+    # cfg4: the q, k, v projections (same LayerNorm output) -> one launch; with the attention chain
+    # and the residual add folded as well, 16 plan kernels -> 7
     p4 = fuse(FX.load_plan("cfg4"))
     assert [k.kind for k in p4.kernels] == ["row", "matmul_multi", "attention", "matmul", "row", "matmul",
-                                           "matmul", "elementwise"]
+                                           "matmul"]
     # a GEMM with an epilogue, or N not a multiple of the 256-column tile, is left alone
     p5 = fuse(FX.load_plan("attention_heads__bf16"))
     assert "matmul_multi" not in [k.kind for k in p5.kernels]
@@ -447,3 +448,21 @@ def test_checked_build_bounds_checks_every_kernel_family():
             k1.finalize_params()
             assert k1.param_bytes >= 8 * len(k1.args)
     assert {"ewise", "row", "split", "gemm_tc", "attention"} <= seen
+
+
+def test_residual_add_after_a_gemm_joins_its_epilogue():
+    """The elementwise kernel after the MLP's down projection (the residual add, planned on its
+    own because x1 also feeds the LayerNorm) is evaluated in that GEMM's epilogue; a kernel that
+    is not only post-processing the GEMM output is left alone."""
+    from mlir_gpu_kernel_compiler_b200.fuse import absorb_elementwise_epilogues, fuse
+
+    for case in ("block_tail__f32", "block_tail__bf16", "cfg4"):
+        p = FX.load_plan(case)
+        f = fuse(p)
+        assert f.meta.get("absorbed_epilogues") == 1
+        last = f.kernels[-1]
+        assert last.kind == "matmul" and [o.id for o in last.outputs] == [p.resolve(p.outputs[0]).id]
+        assert len(f.kernels) == len(p.kernels) - 1 - (len(p.kernels) - 8 if case == "cfg4" else 0)
+        assert generate(f)[-1].info["kind"] == "matmul"      # the GEMM (or its split-K finalize) is last
+    # the GEMM output also escapes as a graph output: nothing to absorb
+    assert absorb_elementwise_epilogues(FX.load_plan("cuda_mlp__bf16")).meta.get("absorbed_epilogues") is None
