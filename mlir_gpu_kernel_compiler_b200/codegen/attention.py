@@ -26,8 +26,11 @@ LOG2E = 1.4426950408889634
 # K/V ring; SPEC starts a block's exponentials with the current row max (speculation, redone
 # when the max moved past the rescale threshold); ALT makes the two query tiles take turns on the
 # MUFU (exponential phases alternate).
+# SPLIT selects the split-row kernel (``attention_split_sm100.cuh``: the two threads of a query
+# row keep separate softmax statistics and O accumulators, combined once at the end, instead of
+# exchanging row maxima every key block).
 # ``TENSORJIT_B200_ATTN="EMU=4,DESYNC=1"`` overrides.
-ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3, "SPEC": 0, "ALT": 1}
+ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3, "SPEC": 0, "ALT": 1, "SPLIT": 0}
 
 
 def attention_knobs() -> dict:
@@ -82,7 +85,11 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     kn = attention_knobs()
     STAGES = kn["STAGES"]
     bl, bidx = decompose_stmts("bh", batch, "b") if batch else ([], [])
-    L = [HEADER, '#include "attention_sm100.cuh"', params_struct(status_idx + 1, 3)]
+    split = bool(kn["SPLIT"])
+    if split and kn["SPEC"]:
+        raise ValueError("TENSORJIT_B200_ATTN: SPEC applies to the row-exchange kernel, not SPLIT")
+    L = [HEADER, f'#include "{"attention_split_sm100.cuh" if split else "attention_sm100.cuh"}"',
+         params_struct(status_idx + 1, 3)]
     L.append("struct Cfg {")
     L.append(f"  using T = {CTYPE[dt]};")
     L.append(f"  static constexpr int SQ = {sq}, SK = {sk}, D = {d}, DV = {dv}, STAGES = {STAGES};")
@@ -125,7 +132,8 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     L.append("  }")
     L.append("};")
     L.append(f'extern "C" __global__ void __launch_bounds__({THREADS}, 1) {symbol}(const __grid_constant__ Params prm) {{')
-    L.append(f"  tja::attention_sm100<Cfg>(prm, ({CTYPE[dt]}*)prm.p[{out_idx}], (int*)prm.p[{status_idx}], {kernel_id});")
+    fn = "attention_split_sm100" if split else "attention_sm100"
+    L.append(f"  tja::{fn}<Cfg>(prm, ({CTYPE[dt]}*)prm.p[{out_idx}], (int*)prm.p[{status_idx}], {kernel_id});")
     L.append("}")
     q_bytes, kv_bytes = BM * d * esz, BN * d * esz
     # + half-row maxima (2 parities x 2 tiles x 2 halves x 128 f32) and sums (2 x 2 x 128 f32)
