@@ -30,7 +30,8 @@ LOG2E = 1.4426950408889634
 # row keep separate softmax statistics and O accumulators, combined once at the end, instead of
 # exchanging row maxima every key block).
 # ``TENSORJIT_B200_ATTN="EMU=4,DESYNC=1"`` overrides.
-ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3, "SPEC": 0, "ALT": 1, "SPLIT": 0}
+# NAP: nanoseconds the producer and MMA warps sleep between barrier polls.
+ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3, "SPEC": 0, "ALT": 1, "SPLIT": 0, "NAP": 0}
 
 
 def attention_knobs() -> dict:
@@ -99,6 +100,7 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     L.append(f"  static constexpr bool DESYNC = {'true' if kn['DESYNC'] else 'false'};")
     L.append(f"  static constexpr bool SPEC = {'true' if kn['SPEC'] else 'false'};")
     L.append(f"  static constexpr bool ALT = {'true' if kn['ALT'] else 'false'};")
+    L.append(f"  static constexpr int NAP = {int(kn['NAP'])};")
     c = float(a["scale"]) * LOG2E
     L.append(f"  static constexpr float C = {c!r}f;")
     tmaps = []

@@ -95,6 +95,35 @@ TJ_DEV float fmax3(float a, float b, float c) {
   return d;
 }
 
+// Bounded wait that sleeps NAP_NS between polls: for the producer and MMA warps, which wait most
+// of the time on the softmax warps; their polls would otherwise take issue slots from the
+// softmax warps sharing their scheduler.  NAP_NS = 0 is the plain bounded wait.
+template <int NAP_NS>
+TJ_DEV bool mbar_wait_nap(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status, int where) {
+  if constexpr (NAP_NS == 0) {
+    return mbar_wait(bar, parity, abort_flag, status, where);
+  } else {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = tj_globaltimer();
+    for (uint32_t it = 1;; ++it) {
+      __nanosleep(NAP_NS);
+      if (mbar_try_wait(bar, parity)) return true;
+      if ((it & 7u) == 0) {
+        if (*abort_flag) return false;
+        if (tj_globaltimer() - t0 > TJ_WAIT_NS) {
+          *abort_flag = 1;
+          tj_report(status, TJ_STATUS_WAIT_TIMEOUT, where);
+          return false;
+        }
+      }
+    }
+  }
+}
+template <int NAP_NS>
+TJ_DEV bool mbar_wait_warp_nap(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status, int where) {
+  return __all_sync(0xffffffffu, mbar_wait_nap<NAP_NS>(bar, parity, abort_flag, status, where));
+}
+
 // 32 lanes x 32 consecutive f32 columns, no wait (the caller waits once for several loads).
 TJ_DEV void tmem_ld32_async(uint32_t taddr, uint32_t* r) {
   asm volatile(
@@ -230,6 +259,7 @@ TJ_DEV void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
 //   static constexpr int EMU (exponentials of every 16 column pairs computed by ex2_poly, 0..16);
 //   static constexpr bool DESYNC (tile 1 starts one key block behind tile 0);
 //   static constexpr bool ALT (the two tiles' exponential phases alternate, one mbarrier token each);
+//   static constexpr int NAP (ns the producer and MMA warps sleep between polls; 0 = none);
 //   static constexpr bool SPEC (exponentials with the current row max while the block's max is
 //   exchanged; recomputed when it moved by more than the rescale threshold);
 //   static constexpr long BATCH;  static constexpr bool BF16;  static constexpr float C (scale * log2 e, > 0);
@@ -338,7 +368,7 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
       for (int j = 0; j < NB; ++j) {
         const int s = j % STAGES;
         const uint32_t ph = (j / STAGES) & 1;
-        if (!mbar_wait(smem_u32(&kv_empty[s]), ph ^ 1u, abort_flag, status, kernel_id * 16 + 1)) break;
+        if (!mbar_wait_nap<Cfg::NAP>(smem_u32(&kv_empty[s]), ph ^ 1u, abort_flag, status, kernel_id * 16 + 1)) break;
 #ifdef TJ_TEST_STALL_FIRST_LOAD
         // Failure-path test build only: K_0 / V_0 are never loaded, so the MMA warps' bounded
         // wait on them must run out and report through the status words.
@@ -393,16 +423,18 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
       const int s = j % STAGES;
       if (j + 1 < NB) {
         const int s1 = (j + 1) % STAGES;
-        if (!mbar_wait_warp(smem_u32(&k_full[s1]), ((j + 1) / STAGES) & 1, abort_flag, status, kernel_id * 16 + 3) ||
-            !mbar_wait_warp(smem_u32(&s_free[t]), j & 1, abort_flag, status, kernel_id * 16 + 4)) {
+        if (!mbar_wait_warp_nap<Cfg::NAP>(smem_u32(&k_full[s1]), ((j + 1) / STAGES) & 1, abort_flag, status,
+                                          kernel_id * 16 + 3) ||
+            !mbar_wait_warp_nap<Cfg::NAP>(smem_u32(&s_free[t]), j & 1, abort_flag, status, kernel_id * 16 + 4)) {
           ok = false;
           break;
         }
         tc_fence_after();
         issue_s(s1);
       }
-      if (!mbar_wait_warp(smem_u32(&v_full[s]), (j / STAGES) & 1, abort_flag, status, kernel_id * 16 + 3) ||
-          !mbar_wait_warp(smem_u32(&p_ready[t]), j & 1, abort_flag, status, kernel_id * 16 + 5)) {
+      if (!mbar_wait_warp_nap<Cfg::NAP>(smem_u32(&v_full[s]), (j / STAGES) & 1, abort_flag, status,
+                                        kernel_id * 16 + 3) ||
+          !mbar_wait_warp_nap<Cfg::NAP>(smem_u32(&p_ready[t]), j & 1, abort_flag, status, kernel_id * 16 + 5)) {
         ok = false;
         break;
       }
