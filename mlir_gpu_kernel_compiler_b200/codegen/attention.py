@@ -30,8 +30,10 @@ LOG2E = 1.4426950408889634
 # row keep separate softmax statistics and O accumulators, combined once at the end, instead of
 # exchanging row maxima every key block).
 # ``TENSORJIT_B200_ATTN="EMU=4,DESYNC=1"`` overrides.
-# NAP: nanoseconds the producer and MMA warps sleep between barrier polls.
-ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3, "SPEC": 0, "ALT": 1, "SPLIT": 0, "NAP": 0}
+# NAP: nanoseconds the producer and MMA warps sleep between barrier polls.  ROW selects the
+# one-thread-per-row kernel (``attention_row_sm100.cuh``: 64-key blocks, S and P double-buffered
+# in TMEM, 384 threads; STAGES then counts 64-key K/V stages).
+ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3, "SPEC": 0, "ALT": 1, "SPLIT": 0, "NAP": 0, "ROW": 0}
 
 
 def attention_knobs() -> dict:
@@ -44,8 +46,8 @@ def attention_knobs() -> dict:
         k[name] = int(val)
     if not 0 <= k["EMU"] <= 16:
         raise ValueError("TENSORJIT_B200_ATTN: EMU must be in 0..16")
-    if not 2 <= k["STAGES"] <= 6:
-        raise ValueError("TENSORJIT_B200_ATTN: STAGES must be in 2..6")
+    if not 2 <= k["STAGES"] <= (10 if k["ROW"] else 6):
+        raise ValueError("TENSORJIT_B200_ATTN: STAGES must be in 2..6 (2..10 with ROW)")
     return k
 BM = 128
 BN = 128
@@ -87,9 +89,15 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     STAGES = kn["STAGES"]
     bl, bidx = decompose_stmts("bh", batch, "b") if batch else ([], [])
     split = bool(kn["SPLIT"])
+    row = bool(kn["ROW"])
+    if row and (split or kn["SPEC"]):
+        raise ValueError("TENSORJIT_B200_ATTN: ROW excludes SPLIT and SPEC")
+    kv_rows = 64 if row else BN
+    threads = 384 if row else THREADS
     if split and kn["SPEC"]:
         raise ValueError("TENSORJIT_B200_ATTN: SPEC applies to the row-exchange kernel, not SPLIT")
-    L = [HEADER, f'#include "{"attention_split_sm100.cuh" if split else "attention_sm100.cuh"}"',
+    header = "attention_row_sm100.cuh" if row else ("attention_split_sm100.cuh" if split else "attention_sm100.cuh")
+    L = [HEADER, f'#include "{header}"',
          params_struct(status_idx + 1, 3)]
     L.append("struct Cfg {")
     L.append(f"  using T = {CTYPE[dt]};")
@@ -123,7 +131,7 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
                 e = f"static_cast<int>({bidx[role]})"
             L.append(f"    c[{mi}] = {e};")
         L.append("  }")
-        box = [64] + [BM if role == "s" else 1 for _, role, _ in ordered[1:]]
+        box = [64] + [(BM if name == "q" else kv_rows) if role == "s" else 1 for _, role, _ in ordered[1:]]
         tmaps.append(TMapSpec(arg=in_index[src.id], dtype=dt, dims=dims,
                               strides=[s * esz for s, _, _ in ordered[1:]], box=box, swizzle=3))
     L.append("  static __device__ __forceinline__ long out_offset(long bh, long s) {")
@@ -133,8 +141,8 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     L.append(f"    return {' + '.join(terms)};")
     L.append("  }")
     L.append("};")
-    L.append(f'extern "C" __global__ void __launch_bounds__({THREADS}, 1) {symbol}(const __grid_constant__ Params prm) {{')
-    fn = "attention_split_sm100" if split else "attention_sm100"
+    L.append(f'extern "C" __global__ void __launch_bounds__({threads}, 1) {symbol}(const __grid_constant__ Params prm) {{')
+    fn = "attention_row_sm100" if row else ("attention_split_sm100" if split else "attention_sm100")
     L.append(f"  tja::{fn}<Cfg>(prm, ({CTYPE[dt]}*)prm.p[{out_idx}], (int*)prm.p[{status_idx}], {kernel_id});")
     L.append("}")
     q_bytes, kv_bytes = BM * d * esz, BN * d * esz
@@ -142,10 +150,12 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     # + mbarriers (q_full, k/v_full and kv_empty per stage, s_full/s_free/p_ready/o_done/drain
     # per tile, 8 half-row exchange barriers, 2 turn tokens) + TMEM slot and abort flag
     smem = 1024 + 2 * q_bytes + STAGES * 2 * kv_bytes + 4096 + 2048 + (21 + 3 * STAGES) * 8 + 8
+    if row:   # 64-key K / V stages; barriers (q_full, 3 per stage, 4 x 4 per tile buffer, 2 drain) + slot
+        smem = 1024 + 2 * q_bytes + STAGES * 2 * (kv_rows * d * esz) + (1 + 3 * STAGES + 18) * 8 + 16
     args = [("node", n) for n in ins] + [("node", out_node), ("status", None)]
     flops = 2.0 * bh_total * sq * sk * (d + dv)
     nbytes = sum(n.nbytes for n in ins) + out_node.nbytes
-    ks = KernelSource(symbol, "attention", "\n".join(L), (bh_total * qpairs, 1, 1), (THREADS, 1, 1), args,
+    ks = KernelSource(symbol, "attention", "\n".join(L), (bh_total * qpairs, 1, 1), (threads, 1, 1), args,
                       smem=smem, tmaps=tmaps,
                       info={"batch": bh_total, "sq": sq, "sk": sk, "d": d, "dv": dv, "flops": flops,
                             "bytes": nbytes, "exps": float(bh_total * sq * sk), "scale": a["scale"],
