@@ -305,6 +305,22 @@ def test_fused_attention_compiles_for_sm100a(name):
     assert all(img[:4] == b"\x7fELF" for img in imgs)
 
 
+@pytest.mark.parametrize("knobs,header,threads,kv_rows", [("SPLIT=1", "attention_split_sm100.cuh", 640, 128),
+                                                          ("ROW=1,STAGES=6", "attention_row_sm100.cuh", 384, 64)])
+def test_attention_kernel_variants_generate_and_compile(knobs, header, threads, kv_rows, monkeypatch):
+    """The split-row and one-thread-per-row attention kernels (``TENSORJIT_B200_ATTN``) build for
+    sm_100a with their own launch shape and K/V tensor-map boxes."""
+    from mlir_gpu_kernel_compiler_b200.toolchain import compile_cubins
+
+    monkeypatch.setenv("TENSORJIT_B200_ATTN", knobs)
+    _, f = _fused("attention_ragged__f16")
+    (k,) = [k for k in generate(f) if k.family == "attention"]
+    assert f'#include "{header}"' in k.source and k.block == (threads, 1, 1)
+    assert k.tmaps[0].box[-2 if len(k.tmaps[0].box) > 2 else 1] == 128
+    assert all(kv_rows in t.box for t in k.tmaps[1:])
+    assert compile_cubins([(k.symbol, k.source)])[0][:4] == b"\x7fELF"
+
+
 def _ex2_poly_f32(x):
     """numpy float32 restatement of ex2_poly (csrc/kernels/attention_sm100.cuh)."""
     x = np.maximum(np.asarray(x, np.float32), np.float32(-126.0))
