@@ -25,9 +25,11 @@ from .common import (CTYPE, HEADER, KernelSource, checked, expr, fast_math_for, 
 CTA_THREADS = 256
 
 
-def _geometry(N: int, VEC: int) -> tuple[int, int, int]:
+def _geometry(N: int, VEC: int, vpt_target: int = 4) -> tuple[int, int, int]:
+    """(threads per row, vectors per thread, rows per CTA): threads per row sized for about
+    ``vpt_target`` 16-byte vectors per thread."""
     nvec = (N + VEC - 1) // VEC
-    target = max(1, (nvec + 3) // 4)          # about four 16-byte vectors per thread
+    target = max(1, (nvec + vpt_target - 1) // vpt_target)
     tpr = 1
     while tpr < target:
         tpr *= 2
@@ -74,7 +76,9 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str,
     if not ok:
         VEC = 1
     fast = fast_math_for([o.dtype for o in outs])
-    TPR, VPT, RPC = _geometry(N, VEC)
+    # the row stays in registers across the stages: with more than two arrays read per element
+    # (e.g. x, r and the gain of RMSNorm(x + r)) two vectors per thread keep enough warps resident
+    TPR, VPT, RPC = _geometry(N, VEC, 4 if len(vec_reads) <= 2 else 2)
     NVEC = (N + VEC - 1) // VEC if N else 0
     if N == 0:
         VPT = 0
