@@ -33,7 +33,9 @@ LOG2E = 1.4426950408889634
 # NAP: nanoseconds the producer and MMA warps sleep between barrier polls.  ROW selects the
 # one-thread-per-row kernel (``attention_row_sm100.cuh``: 64-key blocks, S and P double-buffered
 # in TMEM, 384 threads; STAGES then counts 64-key K/V stages).
-ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3, "SPEC": 0, "ALT": 1, "SPLIT": 0, "NAP": 0, "ROW": 0}
+# QUAD selects the four-threads-per-row kernel (``attention_quad_sm100.cuh``: one query tile per CTA,
+# 256 TMEM columns, two CTAs per SM; STAGES is then at most 2).
+ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3, "SPEC": 0, "ALT": 1, "SPLIT": 0, "NAP": 0, "ROW": 0, "QUAD": 0}
 
 
 def attention_knobs() -> dict:
@@ -90,13 +92,17 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     bl, bidx = decompose_stmts("bh", batch, "b") if batch else ([], [])
     split = bool(kn["SPLIT"])
     row = bool(kn["ROW"])
-    if row and (split or kn["SPEC"]):
-        raise ValueError("TENSORJIT_B200_ATTN: ROW excludes SPLIT and SPEC")
+    quad = bool(kn["QUAD"])
+    if sum((split, row, quad)) > 1 or ((row or quad) and kn["SPEC"]):
+        raise ValueError("TENSORJIT_B200_ATTN: SPLIT, ROW and QUAD exclude each other (and SPEC)")
+    if quad:
+        STAGES = min(STAGES, 2)       # two CTAs per SM must fit in shared memory
     kv_rows = 64 if row else BN
-    threads = 384 if row else THREADS
+    threads = 384 if row else (576 if quad else THREADS)
     if split and kn["SPEC"]:
         raise ValueError("TENSORJIT_B200_ATTN: SPEC applies to the row-exchange kernel, not SPLIT")
-    header = "attention_row_sm100.cuh" if row else ("attention_split_sm100.cuh" if split else "attention_sm100.cuh")
+    header = ("attention_row_sm100.cuh" if row else "attention_quad_sm100.cuh" if quad
+              else "attention_split_sm100.cuh" if split else "attention_sm100.cuh")
     L = [HEADER, f'#include "{header}"',
          params_struct(status_idx + 1, 3)]
     L.append("struct Cfg {")
@@ -141,8 +147,10 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     L.append(f"    return {' + '.join(terms)};")
     L.append("  }")
     L.append("};")
-    L.append(f'extern "C" __global__ void __launch_bounds__({threads}, 1) {symbol}(const __grid_constant__ Params prm) {{')
-    fn = "attention_row_sm100" if row else ("attention_split_sm100" if split else "attention_sm100")
+    L.append(f'extern "C" __global__ void __launch_bounds__({threads}, {2 if quad else 1}) '
+             f'{symbol}(const __grid_constant__ Params prm) {{')
+    fn = ("attention_row_sm100" if row else "attention_quad_sm100" if quad
+          else "attention_split_sm100" if split else "attention_sm100")
     L.append(f"  tja::{fn}<Cfg>(prm, ({CTYPE[dt]}*)prm.p[{out_idx}], (int*)prm.p[{status_idx}], {kernel_id});")
     L.append("}")
     q_bytes, kv_bytes = BM * d * esz, BN * d * esz
@@ -152,10 +160,13 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     smem = 1024 + 2 * q_bytes + STAGES * 2 * kv_bytes + 4096 + 2048 + (21 + 3 * STAGES) * 8 + 8
     if row:   # 64-key K / V stages; barriers (q_full, 3 per stage, 4 x 4 per tile buffer, 2 drain) + slot
         smem = 1024 + 2 * q_bytes + STAGES * 2 * (kv_rows * d * esz) + (1 + 3 * STAGES + 18) * 8 + 16
+    if quad:  # one Q tile, the quarter-row exchange (2 x 4 x 128 f32), barriers + slot
+        smem = 1024 + q_bytes + STAGES * 2 * kv_bytes + 4096 + (1 + 3 * STAGES + 9) * 8 + 16
     args = [("node", n) for n in ins] + [("node", out_node), ("status", None)]
     flops = 2.0 * bh_total * sq * sk * (d + dv)
     nbytes = sum(n.nbytes for n in ins) + out_node.nbytes
-    ks = KernelSource(symbol, "attention", "\n".join(L), (bh_total * qpairs, 1, 1), (threads, 1, 1), args,
+    grid = bh_total * ((sq + BM - 1) // BM if quad else qpairs)
+    ks = KernelSource(symbol, "attention", "\n".join(L), (grid, 1, 1), (threads, 1, 1), args,
                       smem=smem, tmaps=tmaps,
                       info={"batch": bh_total, "sq": sq, "sk": sk, "d": d, "dv": dv, "flops": flops,
                             "bytes": nbytes, "exps": float(bh_total * sq * sk), "scale": a["scale"],
