@@ -242,6 +242,9 @@ def decompose_stmts(linear: str, shape: tuple, prefix: str) -> tuple[list[str], 
 
 
 HEADER = '#include "tj_common.cuh"\n'
+# first statements of every generated kernel without a template prologue: let the program's next
+# kernel launch early, then wait for the previous one (programmatic dependent launch)
+PDL = "  tj_pdl_launch_dependents();\n  tj_pdl_wait();"
 
 
 def node_var(n: PNode) -> str:

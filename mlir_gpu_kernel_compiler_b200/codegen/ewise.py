@@ -14,7 +14,7 @@ the scalar path with compile-time index decomposition.
 from __future__ import annotations
 
 from ..plan import PKernel, access_strides, contiguous_strides, first_consumer
-from .common import (CTYPE, HEADER, NUM_SMS, KernelSource, checked, coalesce, decompose_stmts, expr, fast_math_for,
+from .common import (PDL, CTYPE, HEADER, NUM_SMS, KernelSource, checked, coalesce, decompose_stmts, expr, fast_math_for,
                      offset_expr, params_struct, pick_vec, prod, ptr_decl, status_decl)
 
 THREADS = 256
@@ -42,7 +42,7 @@ def gen_elementwise(k: PKernel, symbol: str, kernel_id: int = 0) -> KernelSource
 
     chk = checked()
     L = [HEADER, params_struct(len(ins) + len(outs) + (1 if chk else 0), 0),
-         f'extern "C" __global__ void __launch_bounds__({THREADS}) {symbol}(const __grid_constant__ Params prm) {{']
+         f'extern "C" __global__ void __launch_bounds__({THREADS}) {symbol}(const __grid_constant__ Params prm) {{', PDL]
     if chk:
         L.append("  " + status_decl(len(ins) + len(outs)))
     for j, n in enumerate(ins):

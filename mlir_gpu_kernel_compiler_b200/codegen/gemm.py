@@ -27,7 +27,7 @@ from __future__ import annotations
 import os
 
 from ..plan import PKernel, PNode, access_strides, contiguous_strides, first_consumer
-from .common import (BOUNDS_SITE, CTYPE, HEADER, ITEM, NUM_SMS, TMAP_DTYPE, KernelSource, TMapSpec, checked,
+from .common import (PDL, BOUNDS_SITE, CTYPE, HEADER, ITEM, NUM_SMS, TMAP_DTYPE, KernelSource, TMapSpec, checked,
                      decompose_stmts, expr, fast_math_for, offset_expr, params_struct, prod, ptr_decl, status_decl)
 
 
@@ -114,7 +114,7 @@ def gen_pack_operands(symbol: str, segments: list[dict], kernel_id: int = 0) -> 
     chk = checked()
     nptr = 3 * len(segments) + (1 if chk else 0)
     L = [HEADER, params_struct(nptr, 0),
-         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{']
+         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{', PDL]
     if chk:
         L.append("  " + status_decl(3 * len(segments)))
     for j, sg in enumerate(segments):
@@ -195,7 +195,7 @@ def gen_epilogue_only(k: PKernel, symbol: str, kernel_id: int = 0) -> KernelSour
     epi = Epilogue(k, in_index, out_index, kernel_id, len(ins) + len(outs))
     total = prod(out_shape[:-2]) * M * N
     L = [HEADER, params_struct(len(ins) + len(outs) + (1 if chk else 0), 0),
-         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{']
+         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{', PDL]
     L += ["  " + x for x in epi._ptr_lines()]
     L.append(f"  for (long e = (long)blockIdx.x * 256 + threadIdx.x; e < {total}L; e += (long)gridDim.x * 256) {{")
     L.append(f"    const long j = e % {max(N, 1)}L, row = e / {max(N, 1)}L, i = row % {max(M, 1)}L, "
@@ -259,7 +259,7 @@ def gen_split_tf32(symbol: str, segments: list[tuple], kernel_id: int = 0) -> Ke
     nseg = len(segments)
     chk = checked()
     L = [HEADER, params_struct(3 * nseg + (1 if chk else 0), 0),
-         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{']
+         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{', PDL]
     if chk:
         L.append("  " + status_decl(3 * nseg))
     L += [f"  for (long g = (long)blockIdx.x * 256 + threadIdx.x; g < {acc}L; g += (long)gridDim.x * 256) {{",
@@ -389,7 +389,7 @@ def gen_ksplit_finalize(k: PKernel, symbol: str, args: list, ksplit: int, kernel
     total = batch * M * N
     part_idx = len(args) - 1
     L = [HEADER, params_struct(len(args), 0),
-         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{']
+         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{', PDL]
     L += ["  " + x for x in epi._ptr_lines()]
     L.append("  " + ptr_decl("part", "float", part_idx, ksplit * total, True, kernel_id))
     L.append(f"  for (long e = (long)blockIdx.x * 256 + threadIdx.x; e < {total}L; e += (long)gridDim.x * 256) {{")

@@ -19,7 +19,7 @@ one CTA's registers, so no cluster is needed.
 from __future__ import annotations
 
 from ..plan import PKernel, PNode, broadcast_strides
-from .common import (CTYPE, HEADER, KernelSource, checked, expr, fast_math_for, literal, offset_expr, params_struct,
+from .common import (PDL, CTYPE, HEADER, KernelSource, checked, expr, fast_math_for, literal, offset_expr, params_struct,
                      pick_vec, prod, ptr_decl, status_decl)
 
 CTA_THREADS = 256
@@ -232,6 +232,7 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str,
     min_ctas = min(6, 65536 // (block * (live + 16))) if block and TPR <= 32 else 1
     bounds = f"{block}, {min_ctas}" if min_ctas >= 2 else f"{block}"
     L.insert(entry_at, f'extern "C" __global__ void __launch_bounds__({bounds}) {symbol}(const __grid_constant__ Params prm) {{')
+    L.insert(entry_at + 1, PDL)
 
     def elem_name(nid: int) -> str:
         kind, nm = per_elem[nid]

@@ -94,6 +94,8 @@ __device__ __forceinline__ void attention_quad_sm100(const P& prm, typename Cfg:
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  tj_pdl_launch_dependents();
+  tj_pdl_wait();  // the previous kernel of the program is complete and its writes are visible
 
   bool q_pending = false;
   uint32_t pending = 0, issued_phase = 0;

@@ -346,6 +346,8 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  tj_pdl_launch_dependents();
+  tj_pdl_wait();  // the previous kernel of the program is complete and its writes are visible
 
   // producer bookkeeping for the abort drain: stages with copies possibly in flight
   bool q_pending = false;

@@ -322,6 +322,8 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  tj_pdl_launch_dependents();
+  tj_pdl_wait();  // the previous kernel of the program is complete and its writes are visible
 
   // stages the producer filled (and the phase it filled them in): on an abort, the
   // copies still in flight are waited for before shared memory is released

@@ -190,6 +190,8 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
   cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any remote access
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  tj_pdl_launch_dependents();
+  tj_pdl_wait();  // the previous kernel of the program is complete and its writes are visible
 
   if (warp == 0) {
     if (lane == 0) {

@@ -136,6 +136,13 @@ enum : int { TJ_STATUS_WAIT_TIMEOUT = 1, TJ_STATUS_BOUNDS = 2 };
 TJ_DEV void tj_report(int* status, int code, int where) {
   if (status && atomicCAS(status, 0, code) == 0) status[1] = where;
 }
+// Programmatic dependent launch: the runtime lets a program's next kernel start while this one
+// finishes.  Every kernel lets its dependents launch as soon as it starts (its own blocks are all
+// resident or done by then), and waits for the previous kernel's completion and memory before
+// its first global access; only set-up (barriers, TMEM allocation, descriptor prefetch) overlaps.
+// Both are no-ops for a kernel launched without the attribute.
+TJ_DEV void tj_pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+TJ_DEV void tj_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 TJ_DEV uint64_t tj_globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

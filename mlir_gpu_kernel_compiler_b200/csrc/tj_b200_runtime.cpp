@@ -74,6 +74,7 @@ struct Driver {
   TJ_FN(cuTensorMapEncodeTiled);
   TJ_FN(cuGraphCreate);
   TJ_FN(cuGraphAddKernelNode_v2);
+  TJ_FN(cuGraphAddDependencies_v2);
   TJ_FN(cuGraphKernelNodeSetAttribute);
   TJ_FN(cuGraphInstantiateWithFlags);
   TJ_FN(cuGraphLaunch);
@@ -106,7 +107,7 @@ struct Driver {
     TJ_SYM(cuCtxSynchronize) TJ_SYM(cuModuleLoadData) TJ_SYM(cuModuleUnload) TJ_SYM(cuModuleGetFunction)
     TJ_SYM(cuFuncSetAttribute) TJ_SYM_OPT(cuFuncGetParamInfo) TJ_SYM(cuMemAlloc_v2) TJ_SYM(cuMemFree_v2)
     TJ_SYM(cuMemsetD32_v2) TJ_SYM(cuMemcpyDtoH_v2) TJ_SYM(cuLaunchKernelEx) TJ_SYM(cuTensorMapEncodeTiled)
-    TJ_SYM(cuGraphCreate) TJ_SYM(cuGraphAddKernelNode_v2) TJ_SYM(cuGraphKernelNodeSetAttribute)
+    TJ_SYM(cuGraphCreate) TJ_SYM(cuGraphAddKernelNode_v2) TJ_SYM_OPT(cuGraphAddDependencies_v2) TJ_SYM(cuGraphKernelNodeSetAttribute)
     TJ_SYM(cuGraphInstantiateWithFlags) TJ_SYM(cuGraphLaunch) TJ_SYM(cuGraphExecKernelNodeSetParams_v2)
     TJ_SYM(cuGraphExecDestroy) TJ_SYM(cuGraphDestroy) TJ_SYM(cuGetErrorString) TJ_SYM(cuEventCreate)
     TJ_SYM(cuEventDestroy_v2) TJ_SYM(cuEventRecord) TJ_SYM(cuEventSynchronize) TJ_SYM(cuEventElapsedTime)
@@ -177,6 +178,9 @@ struct Program {
   CUdeviceptr status = 0;  // int32[4]: code, where, spare, spare
   int32_t num_inputs = 0, num_outputs = 0;
   bool graph_enabled = false;
+  // programmatic dependent launch between the program's kernels: each kernel may start (set-up
+  // only; it waits in griddepcontrol.wait) while the previous one finishes
+  bool pdl = true;
   CUgraph graph = nullptr;
   CUgraphExec exec = nullptr;
   uint64_t calls = 0, launches = 0, replays = 0, node_updates = 0, instantiations = 0;
@@ -250,7 +254,7 @@ int build_params(const Program& p, KernelRec& k, const void* const* in, void* co
   return TJ_OK;
 }
 
-int launch_direct(Program& p, KernelRec& k, CUstream s) {
+int launch_direct(Program& p, KernelRec& k, CUstream s, bool pdl = false) {
   CUlaunchConfig cfg{};
   cfg.gridDimX = k.launch.grid[0];
   cfg.gridDimY = k.launch.grid[1];
@@ -260,15 +264,20 @@ int launch_direct(Program& p, KernelRec& k, CUstream s) {
   cfg.blockDimZ = k.launch.block[2];
   cfg.sharedMemBytes = k.launch.smem_bytes;
   cfg.hStream = s;
-  CUlaunchAttribute attr[1];
+  CUlaunchAttribute attr[2];
   unsigned nattr = 0;
   const uint32_t* c = k.launch.cluster;
   if (c[0] * c[1] * c[2] > 1) {
-    attr[0].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
-    attr[0].value.clusterDim.x = c[0] ? c[0] : 1;
-    attr[0].value.clusterDim.y = c[1] ? c[1] : 1;
-    attr[0].value.clusterDim.z = c[2] ? c[2] : 1;
-    nattr = 1;
+    attr[nattr].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+    attr[nattr].value.clusterDim.x = c[0] ? c[0] : 1;
+    attr[nattr].value.clusterDim.y = c[1] ? c[1] : 1;
+    attr[nattr].value.clusterDim.z = c[2] ? c[2] : 1;
+    ++nattr;
+  }
+  if (pdl) {
+    attr[nattr].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+    attr[nattr].value.programmaticStreamSerializationAllowed = 1;
+    ++nattr;
   }
   cfg.attrs = attr;
   cfg.numAttrs = nattr;
@@ -299,12 +308,24 @@ CUDA_KERNEL_NODE_PARAMS node_params(KernelRec& k, void** kp) {
 int build_graph(Program& p) {
   TJ_CU(drv().cuGraphCreate(&p.graph, 0), "cuGraphCreate");
   CUgraphNode prev = nullptr;
+  // consecutive kernels are joined by programmatic edges (the successor may start once every
+  // block of the predecessor has triggered launch_dependents, and waits in griddepcontrol.wait
+  // for its completion); plain edges when that is off or the driver lacks the call
+  const bool pdl = p.pdl && drv().cuGraphAddDependencies_v2 != nullptr;
   for (KernelRec& k : p.kernels) {
     if (k.skip) continue;
     void* kp[1] = {k.params.data()};
     CUDA_KERNEL_NODE_PARAMS np = node_params(k, kp);
-    TJ_CU(drv().cuGraphAddKernelNode_v2(&k.node, p.graph, prev ? &prev : nullptr, prev ? 1 : 0, &np),
+    const bool plain = prev && !pdl;
+    TJ_CU(drv().cuGraphAddKernelNode_v2(&k.node, p.graph, plain ? &prev : nullptr, plain ? 1 : 0, &np),
           "cuGraphAddKernelNode");
+    if (prev && pdl) {
+      CUgraphEdgeData e{};
+      e.from_port = CU_GRAPH_KERNEL_NODE_PORT_PROGRAMMATIC;
+      e.to_port = 0;
+      e.type = CU_GRAPH_DEPENDENCY_TYPE_PROGRAMMATIC;
+      TJ_CU(drv().cuGraphAddDependencies_v2(p.graph, &prev, &k.node, &e, 1), "cuGraphAddDependencies");
+    }
     const uint32_t* c = k.launch.cluster;
     if (c[0] * c[1] * c[2] > 1) {
       CUkernelNodeAttrValue v{};
@@ -466,6 +487,10 @@ int tj_b200_program_create(const void* const* cubins, const size_t* cubin_sizes,
   }
   TJ_CU(d.cuMemAlloc_v2(&p->status, 16), "cuMemAlloc(status)");
   TJ_CU(d.cuMemsetD32_v2(p->status, 0, 4), "cuMemsetD32(status)");
+  {
+    const char* e = std::getenv("TENSORJIT_B200_PDL");  // "0": kernels strictly one after the other
+    p->pdl = !(e && e[0] == '0');
+  }
   if (!p->kernels.empty())
     p->graph_label = "tj_b200 graph: " + p->kernels.front().symbol +
                      (p->kernels.size() > 1 ? " .. " + p->kernels.back().symbol : std::string());
@@ -483,11 +508,13 @@ int tj_b200_run(void* program, const void* const* inputs, void* const* outputs, 
   CUstream s = reinterpret_cast<CUstream>(stream);
   int rc = TJ_OK;
   if (!p.graph_enabled) {
+    bool first = true;
     for (KernelRec& k : p.kernels) {
       if (k.skip) continue;
       bool changed = false;
       if ((rc = build_params(p, k, inputs, outputs, &changed)) != TJ_OK) return rc;
-      if ((rc = launch_direct(p, k, s)) != TJ_OK) return rc;
+      if ((rc = launch_direct(p, k, s, p.pdl && !first)) != TJ_OK) return rc;
+      first = false;
     }
   } else {
     bool any_changed = false;
