@@ -482,3 +482,24 @@ def test_residual_add_after_a_gemm_joins_its_epilogue():
         assert generate(f)[-1].info["kind"] == "matmul"      # the GEMM (or its split-K finalize) is last
     # the GEMM output also escapes as a graph output: nothing to absorb
     assert absorb_elementwise_epilogues(FX.load_plan("cuda_mlp__bf16")).meta.get("absorbed_epilogues") is None
+
+
+def test_every_kernel_waits_for_its_predecessor_before_touching_memory():
+    """Programmatic dependent launch: a kernel may start while the previous one of the program
+    finishes, so each one must wait (griddepcontrol.wait) before its first global access.  The
+    generated kernels do it first thing; the GEMM and attention templates right after their
+    set-up (barrier init, TMEM allocation), before their roles start."""
+    from mlir_gpu_kernel_compiler_b200.fuse import fuse
+    from mlir_gpu_kernel_compiler_b200.toolchain import KDIR
+
+    for case in FX.cases("case") + FX.cases("config"):
+        for k in generate(fuse(FX.load_plan(case))):
+            if k.family in ("gemm_tc", "attention"):
+                continue
+            body = k.source.split("Params prm) {", 1)[1]
+            assert body.lstrip().startswith("tj_pdl_launch_dependents();\n  tj_pdl_wait();"), (case, k.symbol)
+    for hdr in ("gemm_sm100.cuh", "gemm_sm100_pair.cuh", "attention_sm100.cuh", "attention_split_sm100.cuh",
+                "attention_row_sm100.cuh", "attention_quad_sm100.cuh"):
+        src = (KDIR / hdr).read_text()
+        setup_end = src.index("const uint32_t tmem_base = *tmem_slot;")
+        assert src.index("tj_pdl_wait();", setup_end) < src.index("if (warp == 0)", setup_end), hdr
