@@ -432,6 +432,63 @@ def measure_side_config(cfg: str, a, dev) -> dict:
     return rec
 
 
+def rows_on_root_step(plan, ins, y_local, total_rows: int, steps: int, dev, barrier) -> dict:
+    """The step with its output gathered on rank 0 without a collective: every rank's program
+    (built with plain-store epilogues) is launched with its rows of rank 0's full-size y as the
+    output, a CUDA IPC mapping on the other ranks, so the down projection's epilogue stores its
+    tiles into rank 0's HBM over NVLink while the GEMM runs.  Timed like the step (events,
+    barrier + synchronize on both sides, max over ranks); then rank 0 checks that every rank's
+    rows equal, bit for bit, what that rank's ordinary program wrote locally."""
+    import torch
+    import torch.distributed as dist
+
+    from mlir_gpu_kernel_compiler_b200 import B200Program
+    from mlir_gpu_kernel_compiler_b200.distributed import RowsOnRoot
+
+    world, rank = dist.get_world_size(), dist.get_rank()
+    prog = B200Program(plan, device=dev, use_graph=True, peer_outputs=True)
+    target = RowsOnRoot((total_rows,) + tuple(y_local.shape[1:]), y_local.dtype, dev)
+    try:
+        for _ in range(3):
+            prog.run_into(ins, [target.dest])
+        torch.cuda.synchronize(dev)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            prog.run_into(ins, [target.dest])
+        e1.record()
+        torch.cuda.synchronize(dev)
+        barrier()
+        prog.check()
+        ms = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        # each rank's local rows, as its ordinary program stored them, against rank 0's copy
+        sums = torch.zeros(world, 2, dtype=torch.float64, device=dev)
+        sums[rank, 0] = y_local.double().sum()
+        sums[rank, 1] = y_local.double().abs().sum()
+        dist.all_reduce(sums)
+        same = torch.zeros(1, device=dev)
+        if rank == 0:
+            ok = True
+            for r in range(world):
+                part = target.full.chunk(world, dim=0)[r]
+                ok &= bool(part.double().sum() == sums[r, 0]) and bool(part.double().abs().sum() == sums[r, 1])
+            ok &= bool(torch.equal(target.full.chunk(world, dim=0)[0], y_local))
+            same[0] = float(ok)
+        dist.broadcast(same, src=0)
+        ms = float(ms.item())
+        nbytes = total_rows * y_local[0].numel() * y_local.element_size()
+        return {"ms_per_step": ms, "bytes_to_rank0": nbytes * (world - 1) // world,
+                "rows_identical": bool(same.item()),
+                "how": "step whose last GEMM stores its rows into rank 0's y over NVLink (CUDA IPC mapping, "
+                       f"plain-store epilogue), {steps} steps, max over ranks; rows_identical: every rank's "
+                       "rows on rank 0 have the checksums of its locally stored y (rank 0's: bit for bit)"}
+    finally:
+        target.close()
+        prog.close()
+
+
 def run_b200(a) -> None:
     import torch
     import torch.distributed as dist
@@ -514,6 +571,8 @@ def run_b200(a) -> None:
                   "how": "NCCL all_gather_into_tensor of every rank's y rows (bf16) to every rank, mean of "
                          f"{reps}, max over ranks; busbw = bytes x (N-1)/N / time, the bytes each GPU receives"}
         del full
+        gather["rows_on_root"] = rows_on_root_step(plan, ins, outs[0], total_rows, a.steps, dev, barrier)
+        gather["rows_on_root"]["step_then_nccl_gather_ms"] = ms_max + gms
 
     # end to end through the C ABI with host data every step: HostPipeline streams the row
     # inputs in from pinned host memory and the result out, overlapping both copy directions

@@ -167,6 +167,29 @@ TJ_API int tj_b200_linear_f32_noalloc(const float* A, const float* B, float* C, 
  * nothing.  No counterpart in the reference (its kernels have no bounded waits). */
 TJ_API int tj_b200_linear_f32_noalloc_status(int32_t* code, int32_t* where, void* stream);
 
+/* Peer memory between the processes of one node (one process per GPU), for row-sharded
+ * programs whose output rows go straight into one rank's buffer over NVLink: the owner exports
+ * the device allocation that holds `dptr`, every other rank opens it and passes the returned
+ * address (plus its row offset) to tj_b200_run as an output pointer, so the program's last
+ * kernel stores its rows into the owner's memory with no separate gather.
+ * No counterpart in the reference (it runs on one device; its only output path is a copy,
+ * `cuda_backend.py:535`).  A handle is the driver's 64-byte CUipcMemHandle; `offset` is
+ * `dptr` minus the base of its allocation.  Allocations made through the virtual-memory API
+ * (e.g. a caching allocator with expandable segments) cannot be exported: TJ_ERR_CUDA. */
+typedef struct tj_ipc_handle {
+  unsigned char bytes[64];
+} tj_ipc_handle;
+
+TJ_API int tj_b200_ipc_export(const void* dptr, int32_t device, tj_ipc_handle* handle, uint64_t* offset);
+
+/* Map a handle exported by another process into this process on `device` (peer access is
+ * enabled as needed); *dptr = mapped base + offset.  Release with tj_b200_ipc_close. */
+TJ_API int tj_b200_ipc_open(const tj_ipc_handle* handle, uint64_t offset, int32_t device, void** dptr);
+
+/* Unmap an address returned by tj_b200_ipc_open (same offset and device).  The caller must
+ * have synchronised every stream that still writes through it. */
+TJ_API int tj_b200_ipc_close(void* dptr, uint64_t offset, int32_t device);
+
 /* Message of the last failure on this thread ("" if none). */
 TJ_API const char* tj_b200_last_error(void);
 

@@ -14,17 +14,19 @@ from __future__ import annotations
 
 from ..plan import PProgram
 from .attention import gen_attention
-from .common import KernelSource, checked_build
+from .common import KernelSource, checked_build, store_mode
 from .ewise import gen_elementwise
 from .gemm import gen_gemm_multi, gen_matmul
 from .row import gen_row
 
 
-def generate(plan: PProgram, tiles: dict | None = None, prefix: str = "tj", checked: bool = False) -> list[KernelSource]:
+def generate(plan: PProgram, tiles: dict | None = None, prefix: str = "tj", checked: bool = False,
+             tma_store: bool = True) -> list[KernelSource]:
     """``checked``: emit the checked build (every global access bounds-checked against its
     operand, TMA coordinates and TMEM columns checked in the templates; compile with
-    -DTJ_CHECKED, ``toolchain.CHECKED_FLAGS``)."""
-    with checked_build(checked):
+    -DTJ_CHECKED, ``toolchain.CHECKED_FLAGS``).  ``tma_store=False``: GEMM epilogues store
+    with plain 16-byte stores (for outputs that may be a peer GPU's memory)."""
+    with checked_build(checked), store_mode(tma_store):
         return _generate(plan, tiles, prefix)
 
 

@@ -38,6 +38,24 @@ def checked_build(on: bool = True):
         _CHECKED.reset(token)
 
 
+# Programs whose outputs may live in another GPU's memory (rows stored over NVLink into a peer's
+# buffer) keep every epilogue on plain 16-byte stores instead of TMA stores.
+_TMA_STORE = contextvars.ContextVar("tj_tma_store", default=True)
+
+
+def tma_store_allowed() -> bool:
+    return _TMA_STORE.get()
+
+
+@contextlib.contextmanager
+def store_mode(tma_store: bool = True):
+    token = _TMA_STORE.set(bool(tma_store))
+    try:
+        yield
+    finally:
+        _TMA_STORE.reset(token)
+
+
 def ptr_decl(name: str, ctype: str, idx: int, numel: int, const: bool, kernel_id: int = 0,
              status: str = "tj_status") -> str:
     """Declaration of kernel argument ``idx`` as ``name``: a restrict pointer, or in a checked

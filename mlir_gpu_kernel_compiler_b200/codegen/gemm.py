@@ -28,7 +28,8 @@ import os
 
 from ..plan import PKernel, PNode, access_strides, contiguous_strides, first_consumer
 from .common import (PDL, BOUNDS_SITE, CTYPE, HEADER, ITEM, NUM_SMS, TMAP_DTYPE, KernelSource, TMapSpec, checked,
-                     decompose_stmts, expr, fast_math_for, offset_expr, params_struct, prod, ptr_decl, status_decl)
+                     decompose_stmts, expr, fast_math_for, offset_expr, params_struct, prod, ptr_decl, status_decl,
+                     tma_store_allowed)
 
 
 def _mm_dims(k: PKernel):
@@ -526,7 +527,7 @@ class Epilogue:
         pitch (N % 8 == 0) and the vectorised operand path."""
         outs = self.k.outputs
         return (len(outs) == 1 and outs[0].dtype in ("bf16", "f16") and self.N % 8 == 0 and self.vec_ok()
-                and os.environ.get("TENSORJIT_B200_NO_TMA_STORE") != "1")
+                and os.environ.get("TENSORJIT_B200_NO_TMA_STORE") != "1" and tma_store_allowed())
 
     def vals32_function(self) -> str:
         """``epilogue_vals(prm, b, i, j0, acc[32], out[32])``: the output values of one row's 32

@@ -88,6 +88,10 @@ struct Driver {
   TJ_FN(cuEventSynchronize);
   TJ_FN(cuEventElapsedTime);
   TJ_FN(cuOccupancyMaxActiveClusters);
+  TJ_FN(cuMemGetAddressRange_v2);
+  TJ_FN(cuIpcGetMemHandle);
+  TJ_FN(cuIpcOpenMemHandle_v2);
+  TJ_FN(cuIpcCloseMemHandle);
 #undef TJ_FN
 
   void load() {
@@ -111,7 +115,8 @@ struct Driver {
     TJ_SYM(cuGraphInstantiateWithFlags) TJ_SYM(cuGraphLaunch) TJ_SYM(cuGraphExecKernelNodeSetParams_v2)
     TJ_SYM(cuGraphExecDestroy) TJ_SYM(cuGraphDestroy) TJ_SYM(cuGetErrorString) TJ_SYM(cuEventCreate)
     TJ_SYM(cuEventDestroy_v2) TJ_SYM(cuEventRecord) TJ_SYM(cuEventSynchronize) TJ_SYM(cuEventElapsedTime)
-    TJ_SYM_OPT(cuOccupancyMaxActiveClusters)
+    TJ_SYM_OPT(cuOccupancyMaxActiveClusters) TJ_SYM_OPT(cuMemGetAddressRange_v2) TJ_SYM_OPT(cuIpcGetMemHandle)
+    TJ_SYM_OPT(cuIpcOpenMemHandle_v2) TJ_SYM_OPT(cuIpcCloseMemHandle)
 #undef TJ_SYM
 #undef TJ_SYM_OPT
     if (!all) return;
@@ -641,6 +646,93 @@ int tj_b200_program_info(void* program, tj_program_info* info) {
 int tj_b200_destroy(void* program) {
   if (!program) return TJ_OK;
   delete static_cast<Program*>(program);
+  return TJ_OK;
+}
+
+// -- peer memory between the processes of a node ------------------------------
+// The primary context of `device` stays retained while one of its IPC mappings is open, so the
+// mapping outlives a caller that drops its own reference to the context first.
+static int ipc_driver(Driver** out) {
+  Driver& d = drv();
+  if (!d.ok) return fail(TJ_ERR_NO_DRIVER, "%s", d.why.c_str());
+  if (!d.cuMemGetAddressRange_v2 || !d.cuIpcGetMemHandle || !d.cuIpcOpenMemHandle_v2 || !d.cuIpcCloseMemHandle)
+    return fail(TJ_ERR_NOT_SUPPORTED, "this driver exports no CUDA IPC entry points");
+  *out = &d;
+  return TJ_OK;
+}
+
+int tj_b200_ipc_export(const void* dptr, int32_t device, tj_ipc_handle* handle, uint64_t* offset) {
+  if (!dptr || !handle || !offset) return fail(TJ_ERR_INVALID, "NULL argument to tj_b200_ipc_export");
+  Driver* d = nullptr;
+  int rc = ipc_driver(&d);
+  if (rc != TJ_OK) return rc;
+  CUdevice dev;
+  CUcontext ctx;
+  TJ_CU(d->cuDeviceGet(&dev, device), "cuDeviceGet");
+  TJ_CU(d->cuDevicePrimaryCtxRetain(&ctx, dev), "cuDevicePrimaryCtxRetain");
+  {
+    CtxGuard guard(ctx);
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    CUresult r = d->cuMemGetAddressRange_v2(&base, &size, reinterpret_cast<CUdeviceptr>(dptr));
+    if (r == CUDA_SUCCESS) {
+      CUipcMemHandle h;
+      r = d->cuIpcGetMemHandle(&h, base);
+      if (r == CUDA_SUCCESS) {
+        static_assert(sizeof(h) == sizeof(handle->bytes), "CUipcMemHandle is 64 bytes");
+        std::memcpy(handle->bytes, &h, sizeof(h));
+        *offset = static_cast<uint64_t>(reinterpret_cast<CUdeviceptr>(dptr) - base);
+      }
+    }
+    if (r != CUDA_SUCCESS) rc = cu_fail(r, "cuIpcGetMemHandle");
+  }
+  d->cuDevicePrimaryCtxRelease_v2(dev);
+  return rc;
+}
+
+int tj_b200_ipc_open(const tj_ipc_handle* handle, uint64_t offset, int32_t device, void** dptr) {
+  if (!handle || !dptr) return fail(TJ_ERR_INVALID, "NULL argument to tj_b200_ipc_open");
+  *dptr = nullptr;
+  Driver* d = nullptr;
+  int rc = ipc_driver(&d);
+  if (rc != TJ_OK) return rc;
+  CUdevice dev;
+  CUcontext ctx;
+  TJ_CU(d->cuDeviceGet(&dev, device), "cuDeviceGet");
+  TJ_CU(d->cuDevicePrimaryCtxRetain(&ctx, dev), "cuDevicePrimaryCtxRetain");
+  CUresult r;
+  CUdeviceptr base = 0;
+  {
+    CtxGuard guard(ctx);
+    CUipcMemHandle h;
+    std::memcpy(&h, handle->bytes, sizeof(h));
+    r = d->cuIpcOpenMemHandle_v2(&base, h, CU_IPC_MEM_LAZY_ENABLE_PEER_ACCESS);
+  }
+  if (r != CUDA_SUCCESS) {
+    d->cuDevicePrimaryCtxRelease_v2(dev);
+    return cu_fail(r, "cuIpcOpenMemHandle");
+  }
+  *dptr = reinterpret_cast<void*>(base + offset);   // the context stays retained until close
+  return TJ_OK;
+}
+
+int tj_b200_ipc_close(void* dptr, uint64_t offset, int32_t device) {
+  if (!dptr) return fail(TJ_ERR_INVALID, "NULL address to tj_b200_ipc_close");
+  Driver* d = nullptr;
+  int rc = ipc_driver(&d);
+  if (rc != TJ_OK) return rc;
+  CUdevice dev;
+  CUcontext ctx;
+  TJ_CU(d->cuDeviceGet(&dev, device), "cuDeviceGet");
+  TJ_CU(d->cuDevicePrimaryCtxRetain(&ctx, dev), "cuDevicePrimaryCtxRetain");
+  CUresult r;
+  {
+    CtxGuard guard(ctx);
+    r = d->cuIpcCloseMemHandle(reinterpret_cast<CUdeviceptr>(dptr) - offset);
+  }
+  d->cuDevicePrimaryCtxRelease_v2(dev);       // this call's retain
+  if (r != CUDA_SUCCESS) return cu_fail(r, "cuIpcCloseMemHandle");
+  d->cuDevicePrimaryCtxRelease_v2(dev);       // the one taken by tj_b200_ipc_open
   return TJ_OK;
 }
 

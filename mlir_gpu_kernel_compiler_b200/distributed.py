@@ -4,12 +4,22 @@ The large-batch programs are row-independent: every output row depends only on
 the same input row and on the (replicated) weights.  So the multi-GPU strategy
 is plain data parallelism over rows: one process per GPU, rank ``p`` of ``N``
 owns rows ``[p*R/N, (p+1)*R/N)``, compiles the same program for ``M = R/N`` rows
-and runs it with no cross-GPU traffic in the step.  Only when the caller wants
-the whole result on one device does a collective run: ``gather_rows`` is an
-NCCL all-gather of the row shards over NVLink (``all_gather_into_tensor``), or
-``all_gather`` on backends without it (gloo, used by the CPU tests).
+and runs it with no cross-GPU traffic in the step.  When the caller wants the
+whole result on one device there are two ways:
+
+* ``gather_rows``: after the step, an NCCL all-gather of the row shards over NVLink
+  (``all_gather_into_tensor``), or ``all_gather`` on backends without it (gloo, used
+  by the CPU tests);
+* ``RowsOnRoot``: no collective at all.  The root rank exports its full-size output
+  buffer (CUDA IPC through the runtime's C ABI), every other rank maps it, and each
+  rank's program is launched with its own rows of that buffer as the output, so the
+  last kernel's epilogue stores its tiles straight into the root's HBM over NVLink
+  while the rest of the GEMM is still running.  The only host-visible ordering
+  needed is the usual one: a rank's rows are complete when its stream is.
 """
 from __future__ import annotations
+
+from typing import Optional
 
 import torch
 import torch.distributed as dist
@@ -48,3 +58,56 @@ def max_over_ranks(value: float, device=None, group=None) -> float:
     t = torch.tensor([value], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return float(t.item())
+
+
+class RowsOnRoot:
+    """A ``[total, ...]`` tensor on the root rank whose row shards every rank writes directly.
+
+    Collective: every rank of ``group`` constructs it together (root allocates and exports
+    its buffer, the others map it).  ``dest`` is what a rank passes as its program's output:
+    the root's own tensor slice on the root, a raw peer address elsewhere (programs built
+    with ``peer_outputs=True``).  ``full`` is the whole tensor on the root (None elsewhere);
+    it holds every rank's rows once all ranks' streams have finished the step (synchronise,
+    then ``dist.barrier``).  ``close`` is collective as well: peers unmap first, and the root
+    keeps its buffer until they have.
+    """
+
+    def __init__(self, shape: tuple, dtype: torch.dtype, device: torch.device, root: int = 0, group=None):
+        from . import runtime as rt
+
+        self.group, self.root = group, root
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.device = torch.device(device)
+        self.shape, self.dtype = tuple(shape), dtype
+        self.lo, self.hi = shard_bounds(self.shape[0], self.world, self.rank)
+        row_bytes = torch.empty((), dtype=dtype).element_size()
+        for d in self.shape[1:]:
+            row_bytes *= d
+        self.full: Optional[torch.Tensor] = None
+        self._mapped: Optional[tuple[int, int]] = None
+        dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        self._dev = dev_index
+        msg: list = [None]
+        if self.rank == root:
+            self.full = torch.empty(self.shape, dtype=dtype, device=self.device)
+            torch.cuda.synchronize(self.device)
+            msg[0] = rt.ipc_export(self.full.data_ptr(), dev_index)
+        dist.broadcast_object_list(msg, src=dist.get_global_rank(group, root) if group else root, group=group)
+        if self.rank == root:
+            self.dest = self.full[self.lo:self.hi]
+        else:
+            handle, offset = msg[0]
+            base = rt.ipc_open(handle, offset, dev_index)
+            self._mapped = (base, offset)
+            self.dest = base + self.lo * row_bytes
+
+    def close(self) -> None:
+        from . import runtime as rt
+
+        torch.cuda.synchronize(self.device)
+        if self._mapped is not None:
+            base, offset = self._mapped
+            rt.ipc_close(base, offset, self._dev)
+            self._mapped = None
+        dist.barrier(group=self.group)       # the root frees its buffer only after every peer unmapped it
+        self.full = None

@@ -84,7 +84,7 @@ class B200Program:
 
     def __init__(self, program, device: str | torch.device = "cuda", use_graph: Optional[bool] = None,
                  tune: bool = True, tiles: dict | None = None, nvcc_flags: tuple = (), fuse_kernels: bool = True,
-                 checked: Optional[bool] = None):
+                 checked: Optional[bool] = None, peer_outputs: bool = False):
         self.program = program
         self.pplan: PProgram = as_plan(program)
         self.device = torch.device(device)
@@ -101,7 +101,11 @@ class B200Program:
         _trace("tiles", tiles)
         # checked build: every global access bounds-checked, violations reported as TJ_STATUS_BOUNDS
         self.checked = (os.environ.get("TENSORJIT_B200_CHECKED") == "1") if checked is None else bool(checked)
-        self.kernel_sources = generate(self.xplan, tiles=tiles, checked=self.checked)
+        # peer_outputs: the caller may bind outputs to another GPU's memory (rows stored over
+        # NVLink into a peer's buffer, ``distributed.RowsOnRoot``), so epilogues use plain stores
+        self.peer_outputs = bool(peer_outputs)
+        self.kernel_sources = generate(self.xplan, tiles=tiles, checked=self.checked,
+                                       tma_store=not self.peer_outputs)
         _trace("generated")
         self.source = "\n\n".join(ks.source for ks in self.kernel_sources)
         flags = tuple(nvcc_flags) + (CHECKED_FLAGS if self.checked else ())
@@ -222,11 +226,21 @@ class B200Program:
             ins.append(t)
         return ins
 
-    def run_into(self, ins: list[torch.Tensor], outs: list[torch.Tensor], stream: Optional[int] = None) -> None:
-        """Launch the whole program with caller-provided output buffers (no allocation)."""
+    def run_into(self, ins: list[torch.Tensor], outs: list, stream: Optional[int] = None) -> None:
+        """Launch the whole program with caller-provided output buffers (no allocation).  An
+        output may also be a raw device address (an int), e.g. a peer GPU's memory mapped by
+        ``runtime.ipc_open``; the program must then have been built with ``peer_outputs``."""
+        out_ptrs = []
+        for t in outs:
+            if isinstance(t, int):
+                if not self.peer_outputs:
+                    raise ValueError("raw output addresses need a program built with peer_outputs=True")
+                out_ptrs.append(t)
+            else:
+                out_ptrs.append(t.data_ptr())
         if stream is None:
             stream = torch.cuda.current_stream(self.device).cuda_stream
-        self.native.run([t.data_ptr() for t in ins], [t.data_ptr() for t in outs], stream)
+        self.native.run([t.data_ptr() for t in ins], out_ptrs, stream)
 
     def time_kernels(self, ins: list[torch.Tensor], outs: list[torch.Tensor], iters: int = 10,
                      stream: Optional[int] = None) -> list[float]:

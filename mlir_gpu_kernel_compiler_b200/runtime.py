@@ -16,6 +16,7 @@ TJ_ERR_INVALID = -1
 TJ_ERR_CUDA = -2
 TJ_ERR_NO_DRIVER = -3
 TJ_ERR_DEVICE_STATUS = -4
+TJ_ERR_NOT_SUPPORTED = -5
 
 ARG_INPUT, ARG_ARENA, ARG_OUTPUT, ARG_STATUS = 0, 1, 2, 3
 
@@ -23,7 +24,7 @@ EXPORTS = (
     "tj_b200_program_create", "tj_b200_run", "tj_b200_set_graph", "tj_b200_check_status",
     "tj_b200_program_info", "tj_b200_destroy", "tj_b200_last_error", "tj_b200_abi_version",
     "tj_b200_driver_available", "tj_b200_time_kernels", "tj_b200_linear_f32_noalloc",
-    "tj_b200_linear_f32_noalloc_status",
+    "tj_b200_linear_f32_noalloc_status", "tj_b200_ipc_export", "tj_b200_ipc_open", "tj_b200_ipc_close",
 )
 
 
@@ -47,6 +48,10 @@ class TjLaunch(ctypes.Structure):
         ("first_arg", ctypes.c_int32), ("num_args", ctypes.c_int32),
         ("first_tmap", ctypes.c_int32), ("num_tmaps", ctypes.c_int32),
     ]
+
+
+class TjIpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
 
 
 class TjProgramInfo(ctypes.Structure):
@@ -95,6 +100,12 @@ def library(path: str | Path | None = None) -> ctypes.CDLL:
         lib.tj_b200_linear_f32_noalloc.restype = ctypes.c_int
         lib.tj_b200_linear_f32_noalloc_status.argtypes = [ctypes.POINTER(i32), ctypes.POINTER(i32), vp]
         lib.tj_b200_linear_f32_noalloc_status.restype = ctypes.c_int
+        lib.tj_b200_ipc_export.argtypes = [vp, i32, ctypes.POINTER(TjIpcHandle), ctypes.POINTER(u64)]
+        lib.tj_b200_ipc_export.restype = ctypes.c_int
+        lib.tj_b200_ipc_open.argtypes = [ctypes.POINTER(TjIpcHandle), u64, i32, ctypes.POINTER(vp)]
+        lib.tj_b200_ipc_open.restype = ctypes.c_int
+        lib.tj_b200_ipc_close.argtypes = [vp, u64, i32]
+        lib.tj_b200_ipc_close.restype = ctypes.c_int
         lib.tj_b200_set_graph.argtypes = [vp, i32]
         lib.tj_b200_set_graph.restype = ctypes.c_int
         lib.tj_b200_check_status.argtypes = [vp, ctypes.POINTER(i32), ctypes.POINTER(i32)]
@@ -116,6 +127,30 @@ def check(rc: int, what: str = "") -> None:
     if rc != TJ_OK:
         msg = library().tj_b200_last_error().decode(errors="replace")
         raise RuntimeError_(rc, f"{what}: {msg}" if what else msg)
+
+
+def ipc_export(ptr: int, device: int) -> tuple[bytes, int]:
+    """(64-byte handle, offset) that lets another process of this node map the device
+    allocation holding ``ptr``."""
+    h, off = TjIpcHandle(), ctypes.c_uint64()
+    check(library().tj_b200_ipc_export(ctypes.c_void_p(ptr), device, ctypes.byref(h), ctypes.byref(off)),
+          "tj_b200_ipc_export")
+    return bytes(h.bytes), off.value
+
+
+def ipc_open(handle: bytes, offset: int, device: int) -> int:
+    """Device address, valid on ``device``, of the exported allocation plus ``offset``."""
+    if len(handle) != 64:
+        raise ValueError(f"an IPC handle has 64 bytes, got {len(handle)}")
+    h = TjIpcHandle()
+    ctypes.memmove(h.bytes, handle, 64)
+    out = ctypes.c_void_p()
+    check(library().tj_b200_ipc_open(ctypes.byref(h), offset, device, ctypes.byref(out)), "tj_b200_ipc_open")
+    return int(out.value)
+
+
+def ipc_close(ptr: int, offset: int, device: int) -> None:
+    check(library().tj_b200_ipc_close(ctypes.c_void_p(ptr), offset, device), "tj_b200_ipc_close")
 
 
 class NativeProgram:

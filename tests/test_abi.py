@@ -37,14 +37,15 @@ def test_library_exports_every_declared_symbol():
 def test_struct_layouts_match_header(tmp_path):
     src = tmp_path / "sz.c"
     src.write_text(f'#include "{HEADER}"\n#include <stdio.h>\n#include <stddef.h>\n'
-                   "int main(){printf(\"%zu %zu %zu %zu %zu %zu\\n\", sizeof(tj_argref), sizeof(tj_tmap), "
+                   "int main(){printf(\"%zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(tj_argref), sizeof(tj_tmap), "
                    "sizeof(tj_launch), sizeof(tj_program_info), offsetof(tj_launch, first_arg), "
-                   "offsetof(tj_tmap, param_offset)); return 0;}\n")
+                   "offsetof(tj_tmap, param_offset), sizeof(tj_ipc_handle)); return 0;}\n")
     exe = tmp_path / "sz"
     subprocess.run(["gcc", str(src), "-o", str(exe)], check=True)
     vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
     assert vals == [ctypes.sizeof(rt.TjArgRef), ctypes.sizeof(rt.TjTMap), ctypes.sizeof(rt.TjLaunch),
-                    ctypes.sizeof(rt.TjProgramInfo), rt.TjLaunch.first_arg.offset, rt.TjTMap.param_offset.offset]
+                    ctypes.sizeof(rt.TjProgramInfo), rt.TjLaunch.first_arg.offset, rt.TjTMap.param_offset.offset,
+                    ctypes.sizeof(rt.TjIpcHandle)]
 
 
 def test_abi_version_and_errors_without_gpu():
@@ -85,6 +86,14 @@ def test_abi_version_and_errors_without_gpu():
         assert rc == rt.TJ_ERR_NO_DRIVER
     assert lib.tj_b200_run(None, None, None, None) == rt.TJ_ERR_INVALID
     assert lib.tj_b200_destroy(None) == rt.TJ_OK
+    # peer-memory entry points: NULL arguments are rejected before the driver is used
+    h, off, p = rt.TjIpcHandle(), ctypes.c_uint64(), ctypes.c_void_p()
+    assert lib.tj_b200_ipc_export(None, 0, ctypes.byref(h), ctypes.byref(off)) == rt.TJ_ERR_INVALID
+    assert lib.tj_b200_ipc_open(None, 0, 0, ctypes.byref(p)) == rt.TJ_ERR_INVALID
+    assert lib.tj_b200_ipc_close(None, 0, 0) == rt.TJ_ERR_INVALID
+    if not lib.tj_b200_driver_available():
+        assert lib.tj_b200_ipc_export(ctypes.c_void_p(1 << 20), 0, ctypes.byref(h), ctypes.byref(off)) in (
+            rt.TJ_ERR_NO_DRIVER, rt.TJ_ERR_NOT_SUPPORTED)
 
 
 def test_tmap_validation():

@@ -4,7 +4,8 @@ Each of two ranks (one process per GPU) runs the cfg5 program on its own 1024 ro
 cfg5 inputs (rows [1024 r, 1024 r + 1024)), with the weights replicated and no collective in the
 step; ``distributed.gather_rows`` then all-gathers the row shards over NVLink.  Both ranks must
 hold the same gathered tensor, rank 0's rows must match the reference ``c`` backend's golden
-rows, and rank 1's rows the oracle.
+rows, and rank 1's rows the oracle.  A second test gathers without a collective: each rank's
+program stores its rows straight into rank 0's buffer (``distributed.RowsOnRoot``).
 """
 import os
 import socket
@@ -61,17 +62,85 @@ def _rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_rank_shards_and_nccl_gather():
-    world, port = 2, _free_port()
+def _rank_rows_on_root(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from mlir_gpu_kernel_compiler_b200 import B200Program
+    from mlir_gpu_kernel_compiler_b200 import workloads as W
+    from mlir_gpu_kernel_compiler_b200.distributed import RowsOnRoot
+    from oracle import fixtures as FX
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        w = W.WORKLOADS["cfg5"]
+        ins = W.make_inputs(w, device=dev, rows=(1024 * rank, 1024 * (rank + 1)))
+        plan = FX.load_plan("cfg5_m1024")
+        ref = B200Program(plan, device=dev)
+        y = ref(*ins)[0]                       # this rank's rows, stored locally as usual
+        prog = B200Program(plan, device=dev, peer_outputs=True)
+        target = RowsOnRoot((2048, 4096), torch.bfloat16, dev)
+        results = []
+        for graph in (True, False):            # graph replay (3 replays), then direct launches
+            if rank == 0:
+                target.full.zero_()
+            torch.cuda.synchronize(dev)
+            dist.barrier(device_ids=[rank])
+            prog.native.set_graph(graph)
+            for _ in range(3 if graph else 1):
+                prog.run_into(ins, [target.dest])
+            torch.cuda.synchronize(dev)
+            dist.barrier(device_ids=[rank])
+            prog.check()
+            if rank == 0:
+                other = torch.empty_like(y)
+                dist.recv(other, src=1)
+                ok = bool(torch.equal(target.full[:1024], y)) and bool(torch.equal(target.full[1024:], other))
+                err = FX.check_against_golden(target.full[:1024], FX.case_expected("cfg5_m1024")[0], 2e-2)
+                results.append((ok, float(err)))
+            else:
+                dist.send(y, dst=0)
+                results.append((True, 0.0))
+        peer_mode = isinstance(target.dest, int)
+        target.close()
+        prog.close()
+        ref.close()
+        q.put((rank, peer_mode, results))
+    finally:
+        dist.destroy_process_group()
+
+
+def _spawn(fn, world: int = 2) -> list:
+    port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=fn, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted(q.get(timeout=600) for _ in range(world))
     for p in procs:
         p.join(timeout=120)
+    return res
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_store_rows_on_root_over_nvlink():
+    """Gather without a collective: rank 1's program stores its output rows into rank 0's
+    buffer through a CUDA IPC mapping (plain-store epilogue over NVLink), rank 0's into its own.
+    Rank 0's full buffer must equal, bit for bit, what each rank's ordinary program stores
+    locally, under graph replay and under direct launches."""
+    res = _spawn(_rank_rows_on_root)
+    assert [r[1] for r in res] == [False, True]          # rank 1 wrote through a peer address
+    for ok, err in res[0][2]:
+        assert ok and err <= 2e-2, (ok, err)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_shards_and_nccl_gather():
+    res = _spawn(_rank)
     for rank, same, ok_rows, shape, err in res:
         assert same and ok_rows and shape == (2048, 4096), (rank, same, ok_rows, shape)
         assert err <= 2e-2, (rank, err)

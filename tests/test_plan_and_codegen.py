@@ -503,3 +503,20 @@ def test_every_kernel_waits_for_its_predecessor_before_touching_memory():
         src = (KDIR / hdr).read_text()
         setup_end = src.index("const uint32_t tmem_base = *tmem_slot;")
         assert src.index("tj_pdl_wait();", setup_end) < src.index("if (warp == 0)", setup_end), hdr
+
+
+def test_peer_output_programs_store_without_tma():
+    """A program whose output rows may be a peer GPU's memory (``peer_outputs``) keeps every GEMM
+    epilogue on plain 16-byte stores: no output tensor map, same kernels otherwise."""
+    from mlir_gpu_kernel_compiler_b200 import B200Program
+
+    plan = FX.load_plan("cfg5_m1024")
+    normal = [k for k in generate(plan) if k.family == "gemm_tc"]
+    peer = [k for k in generate(plan, tma_store=False) if k.family == "gemm_tc"]
+    assert any(k.info["tma_store"] for k in normal)
+    assert not any(k.info["tma_store"] for k in peer)
+    assert [len(k.tmaps) for k in peer] == [len(k.tmaps) - int(k.info["tma_store"]) for k in normal]
+    assert "TMA_STORE = false" in peer[-1].source
+    prog = B200Program(plan, device="cuda", peer_outputs=False)
+    with pytest.raises(ValueError, match="peer_outputs"):
+        prog.run_into([], [1 << 40])
