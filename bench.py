@@ -24,7 +24,10 @@ that at every N the GPUs are timed in the same power-capped steady state.
               against MEASURED_PEAKS.json.
 ``cpu_baseline`` the reference's own ``c`` backend (its generated C/OpenMP kernels, built for
               this host by oracle/ref_runner.py) on a bounded row sample, every host core.
-``gather``    (N > 1) the optional NCCL all-gather of y to every rank, timed on its own.
+``gather``    (N > 1) the optional NCCL all-gather of y to every rank, timed on its own, and
+              ``gather.rows_on_root``: the step whose down projection stores its rows straight
+              into rank 0's y over NVLink (no collective), timed in alternation with the
+              ordinary step.
 ``configs``   (N = 1) cfg1-cfg4 measured the same way in the same run: program latency (graph
               replay), the dominant kernel's roofline, the reference baseline and clocks.
 
@@ -432,13 +435,14 @@ def measure_side_config(cfg: str, a, dev) -> dict:
     return rec
 
 
-def rows_on_root_step(plan, ins, y_local, total_rows: int, steps: int, dev, barrier) -> dict:
+def rows_on_root_step(plan, prog, ins, outs, total_rows: int, steps: int, dev, barrier) -> dict:
     """The step with its output gathered on rank 0 without a collective: every rank's program
     (built with plain-store epilogues) is launched with its rows of rank 0's full-size y as the
     output, a CUDA IPC mapping on the other ranks, so the down projection's epilogue stores its
-    tiles into rank 0's HBM over NVLink while the GEMM runs.  Timed like the step (events,
-    barrier + synchronize on both sides, max over ranks); then rank 0 checks that every rank's
-    rows equal, bit for bit, what that rank's ordinary program wrote locally."""
+    tiles into rank 0's HBM over NVLink while the GEMM runs.  Timed in alternation with the
+    ordinary step (local y), three rounds each (events, barrier + synchronize on both sides,
+    max over ranks, median round); then rank 0 checks that every rank's rows equal what that
+    rank's ordinary program stored locally."""
     import torch
     import torch.distributed as dist
 
@@ -446,23 +450,32 @@ def rows_on_root_step(plan, ins, y_local, total_rows: int, steps: int, dev, barr
     from mlir_gpu_kernel_compiler_b200.distributed import RowsOnRoot
 
     world, rank = dist.get_world_size(), dist.get_rank()
-    prog = B200Program(plan, device=dev, use_graph=True, peer_outputs=True)
+    y_local = outs[0]
+    peer = B200Program(plan, device=dev, use_graph=True, peer_outputs=True)
     target = RowsOnRoot((total_rows,) + tuple(y_local.shape[1:]), y_local.dtype, dev)
-    try:
-        for _ in range(3):
-            prog.run_into(ins, [target.dest])
+
+    def timed(fn) -> float:
         torch.cuda.synchronize(dev)
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
-            prog.run_into(ins, [target.dest])
+            fn()
         e1.record()
         torch.cuda.synchronize(dev)
         barrier()
-        prog.check()
         ms = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms.item())
+
+    try:
+        for _ in range(3):
+            peer.run_into(ins, [target.dest])
+        local_ms, peer_ms = [], []
+        for _ in range(3):
+            local_ms.append(timed(lambda: prog.run_into(ins, outs)))
+            peer_ms.append(timed(lambda: peer.run_into(ins, [target.dest])))
+        peer.check()
         # each rank's local rows, as its ordinary program stored them, against rank 0's copy
         sums = torch.zeros(world, 2, dtype=torch.float64, device=dev)
         sums[rank, 0] = y_local.double().sum()
@@ -470,23 +483,23 @@ def rows_on_root_step(plan, ins, y_local, total_rows: int, steps: int, dev, barr
         dist.all_reduce(sums)
         same = torch.zeros(1, device=dev)
         if rank == 0:
-            ok = True
+            parts = target.full.chunk(world, dim=0)
+            ok = bool(torch.equal(parts[0], y_local))
             for r in range(world):
-                part = target.full.chunk(world, dim=0)[r]
-                ok &= bool(part.double().sum() == sums[r, 0]) and bool(part.double().abs().sum() == sums[r, 1])
-            ok &= bool(torch.equal(target.full.chunk(world, dim=0)[0], y_local))
+                ok &= bool(parts[r].double().sum() == sums[r, 0]) and bool(parts[r].double().abs().sum() == sums[r, 1])
             same[0] = float(ok)
         dist.broadcast(same, src=0)
-        ms = float(ms.item())
         nbytes = total_rows * y_local[0].numel() * y_local.element_size()
-        return {"ms_per_step": ms, "bytes_to_rank0": nbytes * (world - 1) // world,
-                "rows_identical": bool(same.item()),
+        return {"ms_per_step": sorted(peer_ms)[1], "local_step_ms": sorted(local_ms)[1],
+                "rounds_ms": {"local": local_ms, "rows_on_root": peer_ms},
+                "bytes_to_rank0": nbytes * (world - 1) // world, "rows_identical": bool(same.item()),
                 "how": "step whose last GEMM stores its rows into rank 0's y over NVLink (CUDA IPC mapping, "
-                       f"plain-store epilogue), {steps} steps, max over ranks; rows_identical: every rank's "
-                       "rows on rank 0 have the checksums of its locally stored y (rank 0's: bit for bit)"}
+                       f"plain-store epilogue), alternating with the ordinary step, 3 rounds x {steps} steps, "
+                       "max over ranks, median round; rows_identical: rank 0's copy of every rank's rows has "
+                       "the checksums of that rank's locally stored y (rank 0's: bit for bit)"}
     finally:
         target.close()
-        prog.close()
+        peer.close()
 
 
 def run_b200(a) -> None:
@@ -571,8 +584,9 @@ def run_b200(a) -> None:
                   "how": "NCCL all_gather_into_tensor of every rank's y rows (bf16) to every rank, mean of "
                          f"{reps}, max over ranks; busbw = bytes x (N-1)/N / time, the bytes each GPU receives"}
         del full
-        gather["rows_on_root"] = rows_on_root_step(plan, ins, outs[0], total_rows, a.steps, dev, barrier)
-        gather["rows_on_root"]["step_then_nccl_gather_ms"] = ms_max + gms
+        ror = rows_on_root_step(plan, prog, ins, outs, total_rows, a.steps, dev, barrier)
+        ror["local_step_then_nccl_gather_ms"] = ror["local_step_ms"] + gms
+        gather["rows_on_root"] = ror
 
     # end to end through the C ABI with host data every step: HostPipeline streams the row
     # inputs in from pinned host memory and the result out, overlapping both copy directions

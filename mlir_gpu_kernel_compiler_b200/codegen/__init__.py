@@ -31,7 +31,12 @@ def generate(plan: PProgram, tiles: dict | None = None, prefix: str = "tj", chec
 
 
 def _generate(plan: PProgram, tiles: dict | None, prefix: str) -> list[KernelSource]:
+    """Each matmul with a pre-pass gets a workspace region of its own (``info["scratch_base"]``,
+    offsets relative to the program's workspace): its pre-pass may split or pack the program
+    inputs among its operands before waiting for the kernels ahead of it (programmatic
+    dependent launch), which is only safe when no earlier matmul still reads that region."""
     out: list[KernelSource] = []
+    ws_base = 0
     for idx, k in enumerate(plan.kernels):
         sym = f"{prefix}_{k.kind}_{idx}"
         if k.kind in ("elementwise", "copy"):
@@ -47,9 +52,15 @@ def _generate(plan: PProgram, tiles: dict | None, prefix: str) -> list[KernelSou
             ks = gen_gemm_multi(k, sym, idx, (tiles or {}).get(idx))
         elif k.kind == "matmul":
             parts = gen_matmul(k, sym, idx, (tiles or {}).get(idx))
+            ws = max(ks.info.get("scratch_bytes", 0) for ks in parts)
             for ks in parts:
                 ks.info["kind"] = k.kind
                 ks.info["index"] = idx
+                if ws:      # this matmul's own workspace region
+                    ks.args = [("scratch", a[1] + ws_base) if a[0] == "scratch" else a for a in ks.args]
+                    ks.info["scratch_base"] = ws_base
+                    ks.info["scratch_bytes"] = ws_base + ws
+            ws_base += (ws + 255) // 256 * 256
             out += parts
             continue
         else:

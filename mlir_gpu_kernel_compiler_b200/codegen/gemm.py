@@ -114,8 +114,12 @@ def gen_pack_operands(symbol: str, segments: list[dict], kernel_id: int = 0) -> 
     total = sum(tiles)
     chk = checked()
     nptr = 3 * len(segments) + (1 if chk else 0)
+    # program inputs (weights) are packed before the launch waits for the previous kernel
+    early, late = _early_late([sg["src"] for sg in segments])
+    prologue, loops, epilogue = _wait_split(early, late)
     L = [HEADER, params_struct(nptr, 0),
-         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{', PDL]
+         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{',
+         prologue]
     if chk:
         L.append("  " + status_decl(3 * len(segments)))
     for j, sg in enumerate(segments):
@@ -127,17 +131,46 @@ def gen_pack_operands(symbol: str, segments: list[dict], kernel_id: int = 0) -> 
         if sg["split"]:
             L.append("  " + ptr_decl(f"lo{j}", dt, 3 * j + 2, n_dst, False, kernel_id))
     L += ["  __shared__ float tile[32][33];",
-         "  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;",
-         f"  for (long t = blockIdx.x; t < {total}L; t += gridDim.x) {{",
+          "  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;"]
+    for idx, pre in loops:
+        if pre:
+            L.append(pre)
+        L += _pack_loop(segments, tiles, idx)
+    if epilogue:
+        L.append(epilogue)
+    L.append("}")
+    args = []
+    nbytes = 0
+    for sg in segments:
+        args += [sg["src"], ("scratch", sg["hi"]), ("scratch", sg.get("lo", sg["hi"]))]
+    if chk:
+        args.append(("status", None))
+    for sg in segments:
+        n_src = sg["mats"] * sg["rows"] * sg["K"]
+        n_dst = sg["mats"] * sg["rows"] * sg["pitch"]
+        nbytes += n_src * ITEM[sg["src_dtype"]] + n_dst * ITEM[sg["dst_dtype"]] * (2 if sg["split"] else 1)
+    grid = max(1, min(total, NUM_SMS * 8))
+    ks = KernelSource(symbol, "split", "\n".join(L), (grid, 1, 1), (256, 1, 1), args,
+                      info={"bytes": nbytes, "numel": sum(sg["mats"] * sg["rows"] * sg["K"] for sg in segments),
+                            "early_segments": len(early)})
+    ks.finalize_params()
+    return ks
+
+
+def _pack_loop(segments: list[dict], tiles: list[int], idx: list[int]) -> list[str]:
+    """Tile loop (one 32 x 32 tile per CTA iteration) over the segments ``idx``."""
+    total = sum(tiles[j] for j in idx)
+    L = [f"  for (long t = blockIdx.x; t < {total}L; t += gridDim.x) {{",
          "    long u = t;"]
     acc = 0
-    for j, (sg, nt) in enumerate(zip(segments, tiles)):
+    for q, j in enumerate(idx):
+        sg, nt = segments[j], tiles[j]
         R, K, P = sg["rows"], sg["K"], sg["pitch"]
         kt = (P + 31) // 32
         rt = (R + 31) // 32
-        st, dt = CTYPE[sg["src_dtype"]], CTYPE[sg["dst_dtype"]]
-        cond = f"u < {acc + nt}L" if j < len(segments) - 1 else "true"
-        L.append(f"    {'if' if j == 0 else 'else if'} ({cond}) {{")
+        dt = CTYPE[sg["dst_dtype"]]
+        cond = f"u < {acc + nt}L" if q < len(idx) - 1 else "true"
+        L.append(f"    {'if' if q == 0 else 'else if'} ({cond}) {{")
         L.append(f"      u -= {acc}L;")
         L.append(f"      const long kt = u % {kt}L, rt = (u / {kt}L) % {rt}L, mat = u / {kt * rt}L;")
         L.append("      for (int y = ty; y < 32; y += 8) {")
@@ -167,22 +200,8 @@ def gen_pack_operands(symbol: str, segments: list[dict], kernel_id: int = 0) -> 
         L.append("      __syncthreads();")
         L.append("    }")
         acc += nt
-    L += ["  }", "}"]
-    args = []
-    nbytes = 0
-    for sg in segments:
-        args += [sg["src"], ("scratch", sg["hi"]), ("scratch", sg.get("lo", sg["hi"]))]
-    if chk:
-        args.append(("status", None))
-    for sg in segments:
-        n_src = sg["mats"] * sg["rows"] * sg["K"]
-        n_dst = sg["mats"] * sg["rows"] * sg["pitch"]
-        nbytes += n_src * ITEM[sg["src_dtype"]] + n_dst * ITEM[sg["dst_dtype"]] * (2 if sg["split"] else 1)
-    grid = max(1, min(total, NUM_SMS * 8))
-    ks = KernelSource(symbol, "split", "\n".join(L), (grid, 1, 1), (256, 1, 1), args,
-                      info={"bytes": nbytes, "numel": sum(sg["mats"] * sg["rows"] * sg["K"] for sg in segments)})
-    ks.finalize_params()
-    return ks
+    L.append("  }")
+    return L
 
 
 def gen_epilogue_only(k: PKernel, symbol: str, kernel_id: int = 0) -> KernelSource:
@@ -248,39 +267,89 @@ def gen_matmul(k: PKernel, symbol: str, kernel_id: int, tile: dict | None) -> li
     return [pk, g]
 
 
+def _is_program_input(ref) -> bool:
+    """An argument that is a program input: no kernel of the program writes it, so a launch may
+    read it before waiting for the previous kernel (programmatic dependent launch)."""
+    return ref[0] == "node" and ref[1].op == "input"
+
+
+def _early_late(srcs: list) -> tuple[list[int], list[int]]:
+    """Segment indices split into (program inputs, the rest)."""
+    early = [j for j, src in enumerate(srcs) if _is_program_input(src)]
+    return early, [j for j in range(len(srcs)) if j not in early]
+
+
+def _wait_split(early: list, late: list) -> tuple[str, list, str]:
+    """(prologue, [(segments, preamble)], ...) of a pre-pass whose program-input segments run
+    before ``tj_pdl_wait()``: those read only caller inputs and write this matmul's own
+    workspace region, which nothing before it touches."""
+    if early and late:
+        return "  tj_pdl_launch_dependents();", [(early, ""), (late, "  tj_pdl_wait();")], ""
+    if early:
+        return "  tj_pdl_launch_dependents();", [(early, "")], "  tj_pdl_wait();"
+    return PDL, [(late, "")], ""
+
+
 def gen_split_tf32(symbol: str, segments: list[tuple], kernel_id: int = 0) -> KernelSource:
     """x -> (hi, lo) with hi = x with its 13 low mantissa bits cleared (exactly a TF32 value)
     and lo = x - hi (exact in f32): the operand split of 3xTF32 (hi*hi + hi*lo + lo*hi keeps
     ~21 mantissa bits of every product).  ``segments`` = [(numel, src, hi_off, lo_off), ...]:
-    the operands of one GEMM are split by one grid-stride launch."""
-    bounds, acc = [], 0
-    for numel, _src, _hi, _lo in segments:
-        acc += numel // 4
-        bounds.append(acc)
+    the operands of one GEMM are split by one grid-stride launch.  Segments that are program
+    inputs (weights) are split first, before the launch waits for the previous kernel, so with
+    programmatic dependent launch that part overlaps the kernels before it."""
     nseg = len(segments)
     chk = checked()
+    early, late = _early_late([sg[1] for sg in segments])
+    prologue, loops, epilogue = _wait_split(early, late)
     L = [HEADER, params_struct(3 * nseg + (1 if chk else 0), 0),
-         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{', PDL]
+         f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{',
+         prologue]
     if chk:
         L.append("  " + status_decl(3 * nseg))
-    L += [f"  for (long g = (long)blockIdx.x * 256 + threadIdx.x; g < {acc}L; g += (long)gridDim.x * 256) {{",
+    for segs, pre in loops:
+        if pre:
+            L.append(pre)
+        L += _split_loop(segments, segs, kernel_id, chk)
+    if epilogue:
+        L.append(epilogue)
+    L.append("}")
+    total4 = sum(sg[0] // 4 for sg in segments)
+    grid = max(1, min((total4 + 255) // 256, NUM_SMS * 8))
+    args = []
+    for _numel, src, hi_off, lo_off in segments:
+        args += [src, ("scratch", hi_off), ("scratch", lo_off)]
+    if chk:
+        args.append(("status", None))
+    total = sum(sg[0] for sg in segments)
+    ks = KernelSource(symbol, "split", "\n".join(L), (grid, 1, 1), (256, 1, 1), args,
+                      info={"bytes": total * 12, "numel": total, "early_segments": len(early)})
+    ks.finalize_params()
+    return ks
+
+
+def _split_loop(segments: list[tuple], idx: list[int], kernel_id: int, chk: bool) -> list[str]:
+    """Grid-stride loop splitting the float4s of segments ``idx`` (argument slots 3j..3j+2)."""
+    n4 = [segments[j][0] // 4 for j in idx]
+    acc = sum(n4)
+    L = [f"  for (long g = (long)blockIdx.x * 256 + threadIdx.x; g < {acc}L; g += (long)gridDim.x * 256) {{",
          "    int s = 0;",
          "    long i = g;"]
-    for j in range(nseg - 1):
-        n = bounds[j] - (bounds[j - 1] if j else 0)
-        L.append(f"    if (s == {j} && i >= {n}L) {{ i -= {n}L; s = {j + 1}; }}")
+    for q in range(len(idx) - 1):
+        L.append(f"    if (s == {q} && i >= {n4[q]}L) {{ i -= {n4[q]}L; s = {q + 1}; }}")
 
     def pick(slot: int) -> str:   # select the segment's pointer without indexing the params at run time
-        e = f"prm.p[{3 * (nseg - 1) + slot}]"
-        for j in range(nseg - 2, -1, -1):
-            e = f"(s == {j} ? prm.p[{3 * j + slot}] : {e})"
+        e = f"prm.p[{3 * idx[-1] + slot}]"
+        for q in range(len(idx) - 2, -1, -1):
+            e = f"(s == {q} ? prm.p[{3 * idx[q] + slot}] : {e})"
         return e
 
     if chk:   # the segment's index stays inside its operand (in float4 units)
-        n4 = f"{segments[-1][0] // 4}L"
-        for j in range(nseg - 2, -1, -1):
-            n4 = f"(s == {j} ? {segments[j][0] // 4}L : {n4})"
-        L.append(f"    if (!tj_check(i >= 0 && i < {n4}, tj_status, {kernel_id * 16 + BOUNDS_SITE}, 3 * s, i)) "
+        lim = f"{n4[-1]}L"
+        for q in range(len(idx) - 2, -1, -1):
+            lim = f"(s == {q} ? {n4[q]}L : {lim})"
+        arg = f"3 * {idx[0]}" if len(idx) == 1 else "3 * (" + "".join(
+            f"s == {q} ? {idx[q]} : " for q in range(len(idx) - 1)) + f"{idx[-1]})"
+        L.append(f"    if (!tj_check(i >= 0 && i < {lim}, tj_status, {kernel_id * 16 + BOUNDS_SITE}, {arg}, i)) "
                  "continue;")
     L += [f"    const float4* __restrict__ x = (const float4*){pick(0)};",
           f"    float4* __restrict__ hi = (float4*){pick(1)};",
@@ -293,19 +362,8 @@ def gen_split_tf32(symbol: str, segments: list[tuple], kernel_id: int = 0) -> Ke
           "    h.w = __uint_as_float(__float_as_uint(v.w) & 0xffffe000u);",
           "    hi[i] = h;",
           "    lo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);",
-          "  }",
-          "}"]
-    grid = max(1, min((acc + 255) // 256, NUM_SMS * 8))
-    args = []
-    for _numel, src, hi_off, lo_off in segments:
-        args += [src, ("scratch", hi_off), ("scratch", lo_off)]
-    if chk:
-        args.append(("status", None))
-    total = sum(sg[0] for sg in segments)
-    ks = KernelSource(symbol, "split", "\n".join(L), (grid, 1, 1), (256, 1, 1), args,
-                      info={"bytes": total * 12, "numel": total})
-    ks.finalize_params()
-    return ks
+          "  }"]
+    return L
 
 
 def _align(x: int, a: int = 256) -> int:
