@@ -35,7 +35,10 @@ LOG2E = 1.4426950408889634
 # in TMEM, 384 threads; STAGES then counts 64-key K/V stages).
 # QUAD selects the four-threads-per-row kernel (``attention_quad_sm100.cuh``: one query tile per CTA,
 # 256 TMEM columns, two CTAs per SM; STAGES is then at most 2).
-ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3, "SPEC": 0, "ALT": 1, "SPLIT": 0, "NAP": 0, "ROW": 0, "QUAD": 0}
+# F2: the softmax's scale-and-shift FMAs and running sums as packed f32x2 instructions (sm_100),
+# bit-identical to the scalar form with half the instructions.
+ATTN_DEFAULTS = {"EMU": 0, "DESYNC": 1, "STAGES": 3, "SPEC": 0, "ALT": 1, "SPLIT": 0, "NAP": 0, "ROW": 0, "QUAD": 0,
+                 "F2": 0}
 
 
 def attention_knobs() -> dict:
@@ -115,6 +118,7 @@ def gen_attention(k: PKernel, symbol: str, kernel_id: int) -> KernelSource:
     L.append(f"  static constexpr bool SPEC = {'true' if kn['SPEC'] else 'false'};")
     L.append(f"  static constexpr bool ALT = {'true' if kn['ALT'] else 'false'};")
     L.append(f"  static constexpr int NAP = {int(kn['NAP'])};")
+    L.append(f"  static constexpr bool F2 = {'true' if kn['F2'] else 'false'};")
     c = float(a["scale"]) * LOG2E
     L.append(f"  static constexpr float C = {c!r}f;")
     tmaps = []

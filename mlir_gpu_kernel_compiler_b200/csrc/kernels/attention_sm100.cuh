@@ -189,15 +189,52 @@ TJ_DEV void umma_f16_ts_elect(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, 
 }
 
 
+// Two f32 values in one 64-bit register pair, for the packed f32x2 FMA / add of sm_100 (each
+// lane rounds exactly like fmaf / a plain round-to-nearest add, so results are bit-identical).
+TJ_DEV uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+TJ_DEV void f2_unpack(uint64_t v, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
+TJ_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+TJ_DEV uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 template <class T> TJ_DEV uint32_t pack2(float lo, float hi);
 template <> TJ_DEV uint32_t pack2<__nv_bfloat16>(float lo, float hi) { return tj_pack_bf16x2(lo, hi); }
 template <> TJ_DEV uint32_t pack2<__half>(float lo, float hi) { return tj_pack_f16x2(lo, hi); }
 
 // p = 2^(x*c - m) for the column pairs [I0, I0 + 16) of a 64-column half row, packed two per
 // word to the element type; l0 / l1 accumulate the sum of the even / odd columns.  EMU of
-// every 16 pairs use ex2_poly (FMA pipe), the rest ex2.approx (MUFU).
-template <int I0, class T, int EMU>
+// every 16 pairs use ex2_poly (FMA pipe), the rest ex2.approx (MUFU).  F2: the scale-and-shift
+// and the running sums as packed f32x2 operations (half the FMA / add instructions, same bits).
+template <int I0, class T, int EMU, bool F2 = false>
 TJ_DEV void exp_pairs(const float (&x)[64], float c, float m, uint32_t (&pk)[16], float& l0, float& l1) {
+  if constexpr (F2) {
+    const uint64_t cc = f2_pack(c, c), nm = f2_pack(-m, -m);
+    uint64_t ll = f2_pack(l0, l1);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int i = I0 + k;
+      float a0, a1;
+      f2_unpack(f2_fma(f2_pack(x[2 * i], x[2 * i + 1]), cc, nm), a0, a1);
+      const bool emu = (i & 15) < EMU;
+      const float p0 = emu ? ex2_poly(a0) : ex2_approx(a0);
+      const float p1 = emu ? ex2_poly(a1) : ex2_approx(a1);
+      ll = f2_add(ll, f2_pack(p0, p1));
+      pk[k] = pack2<T>(p0, p1);
+    }
+    f2_unpack(ll, l0, l1);
+    return;
+  }
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
     const int i = I0 + k;
@@ -547,7 +584,7 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
               break;
             }
           }
-          exp_pairs<0, T, Cfg::EMU>(x, Cfg::C, m, pk, l0, l1);
+          exp_pairs<0, T, Cfg::EMU, Cfg::F2>(x, Cfg::C, m, pk, l0, l1);
           if (!wait_prev_pv()) {
             ok = false;
             break;
@@ -557,7 +594,7 @@ __device__ __forceinline__ void attention_sm100(const P& prm, typename Cfg::T* _
           // second half still keeps the unit busy
           if (alt) mbar_arrive(smem_u32(&turn[t ^ 1]));
           uint32_t pk2[16];
-          exp_pairs<16, T, Cfg::EMU>(x, Cfg::C, m, pk2, l0, l1);
+          exp_pairs<16, T, Cfg::EMU, Cfg::F2>(x, Cfg::C, m, pk2, l0, l1);
           tmem_st16(tP + 16, pk2);
           tmem_wait_st();
         } else {

@@ -135,3 +135,33 @@ def test_graph_replay_with_new_inputs_and_large_scores():
     ref2 = evaluate(plan, [t.cpu() for t in ins2])[0]
     assert normwise_error(y2, ref2) <= normwise_error(plain(*ins2)[0], ref2)
     assert prog.stats["graph_replays"] == 2
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_packed_f32x2_softmax_is_bit_identical(monkeypatch, dtype):
+    """The softmax's scale-and-shift FMAs and running sums as packed f32x2 instructions (knob
+    F2) round each lane exactly like the scalar code, in the same order: the output must be
+    the same bits, here on the long sequence whose row maximum moves on every key block and
+    on the head-split fixture."""
+    from mlir_gpu_kernel_compiler_b200 import B200Program
+
+    b, sq, sk = 2, 300, 2050
+    dt = {"bf16": torch.bfloat16, "f16": torch.float16}[dtype]
+    g = torch.Generator(device="cuda").manual_seed(12)
+    q = (torch.rand((b, sq, 64), generator=g, device="cuda") * 0.2 + 0.9).to(dt)
+    ramp = torch.linspace(0.0, 12.0, sk, device="cuda").view(1, sk, 1)
+    k = ((torch.rand((b, sk, 64), generator=g, device="cuda") * 0.2 + 0.9) * ramp).to(dt)
+    v = torch.randn((b, sk, 64), generator=g, device="cuda").to(dt)
+    heads = [t.cuda() for t in FX.case_inputs("attention_heads__bf16")]
+    outs = {}
+    for f2 in ("0", "1"):
+        monkeypatch.setenv("TENSORJIT_B200_ATTN", f"F2={f2}")
+        p1 = B200Program(_resized_attention_plan(b, sq, sk, dtype), device="cuda")
+        assert ("F2 = true" in p1.source) == (f2 == "1")
+        outs[f2] = [p1(q, k, v)[0]]
+        if dtype == "bf16":
+            outs[f2].append(_prog("attention_heads__bf16")(*heads)[0])
+        torch.cuda.synchronize()
+        p1.check()
+    for a, c in zip(outs["0"], outs["1"]):
+        assert torch.equal(a, c)

@@ -306,7 +306,8 @@ def test_fused_attention_compiles_for_sm100a(name):
 
 
 @pytest.mark.parametrize("knobs,header,threads,kv_rows", [("SPLIT=1", "attention_split_sm100.cuh", 640, 128),
-                                                          ("ROW=1,STAGES=6", "attention_row_sm100.cuh", 384, 64)])
+                                                          ("ROW=1,STAGES=6", "attention_row_sm100.cuh", 384, 64),
+                                                          ("F2=1", "attention_sm100.cuh", 640, 128)])
 def test_attention_kernel_variants_generate_and_compile(knobs, header, threads, kv_rows, monkeypatch):
     """The split-row and one-thread-per-row attention kernels (``TENSORJIT_B200_ATTN``) build for
     sm_100a with their own launch shape and K/V tensor-map boxes."""
