@@ -452,7 +452,11 @@ def rows_on_root_step(plan, prog, ins, outs, total_rows: int, steps: int, dev, b
     world, rank = dist.get_world_size(), dist.get_rank()
     y_local = outs[0]
     peer = B200Program(plan, device=dev, use_graph=True, peer_outputs=True)
-    target = RowsOnRoot((total_rows,) + tuple(y_local.shape[1:]), y_local.dtype, dev)
+    try:
+        target = RowsOnRoot((total_rows,) + tuple(y_local.shape[1:]), y_local.dtype, dev)
+    except RuntimeError:
+        peer.close()
+        raise
 
     def timed(fn) -> float:
         torch.cuda.synchronize(dev)
@@ -584,8 +588,11 @@ def run_b200(a) -> None:
                   "how": "NCCL all_gather_into_tensor of every rank's y rows (bf16) to every rank, mean of "
                          f"{reps}, max over ranks; busbw = bytes x (N-1)/N / time, the bytes each GPU receives"}
         del full
-        ror = rows_on_root_step(plan, prog, ins, outs, total_rows, a.steps, dev, barrier)
-        ror["local_step_then_nccl_gather_ms"] = ror["local_step_ms"] + gms
+        try:
+            ror = rows_on_root_step(plan, prog, ins, outs, total_rows, a.steps, dev, barrier)
+            ror["local_step_then_nccl_gather_ms"] = ror["local_step_ms"] + gms
+        except RuntimeError as ex:   # raised on every rank together (RowsOnRoot set-up)
+            ror = {"error": str(ex)[:300]}
         gather["rows_on_root"] = ror
 
     # end to end through the C ABI with host data every step: HostPipeline streams the row

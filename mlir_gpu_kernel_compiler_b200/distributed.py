@@ -85,26 +85,46 @@ class RowsOnRoot:
             row_bytes *= d
         self.full: Optional[torch.Tensor] = None
         self._mapped: Optional[tuple[int, int]] = None
-        dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        cuda = self.device.type == "cuda"
+        dev_index = self.device.index if self.device.index is not None else (torch.cuda.current_device() if cuda else 0)
         self._dev = dev_index
+        # Failures are collective: every rank learns of one and raises at the same point, so
+        # no rank is left waiting in a later collective.
         msg: list = [None]
         if self.rank == root:
             self.full = torch.empty(self.shape, dtype=dtype, device=self.device)
-            torch.cuda.synchronize(self.device)
-            msg[0] = rt.ipc_export(self.full.data_ptr(), dev_index)
+            if cuda:
+                torch.cuda.synchronize(self.device)
+            try:
+                msg[0] = ("ok",) + rt.ipc_export(self.full.data_ptr(), dev_index)
+            except Exception as ex:  # noqa: BLE001 - reported to every rank below
+                msg[0] = ("error", f"rank {root} could not export its buffer: {ex}")
         dist.broadcast_object_list(msg, src=dist.get_global_rank(group, root) if group else root, group=group)
+        err = msg[0][1] if msg[0][0] == "error" else ""
         if self.rank == root:
             self.dest = self.full[self.lo:self.hi]
-        else:
-            handle, offset = msg[0]
-            base = rt.ipc_open(handle, offset, dev_index)
-            self._mapped = (base, offset)
-            self.dest = base + self.lo * row_bytes
+        elif not err:
+            _, handle, offset = msg[0]
+            try:
+                base = rt.ipc_open(handle, offset, dev_index)
+                self._mapped = (base, offset)
+                self.dest = base + self.lo * row_bytes
+            except Exception as ex:  # noqa: BLE001
+                err = f"rank {self.rank} could not map rank {root}'s buffer: {ex}"
+        ok = torch.tensor([0 if err else 1], dtype=torch.int32, device=self.device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if not int(ok.item()):
+            if self._mapped is not None:
+                rt.ipc_close(self._mapped[0], self._mapped[1], dev_index)
+                self._mapped = None
+            self.full = None
+            raise RuntimeError(err or "another rank could not set up the shared output buffer")
 
     def close(self) -> None:
         from . import runtime as rt
 
-        torch.cuda.synchronize(self.device)
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
         if self._mapped is not None:
             base, offset = self._mapped
             rt.ipc_close(base, offset, self._dev)
