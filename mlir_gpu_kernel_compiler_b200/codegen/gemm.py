@@ -587,6 +587,28 @@ class Epilogue:
         return (len(outs) == 1 and outs[0].dtype in ("bf16", "f16") and self.N % 8 == 0 and self.vec_ok()
                 and os.environ.get("TENSORJIT_B200_NO_TMA_STORE") != "1" and tma_store_allowed())
 
+    def staged_store_ok(self) -> bool:
+        """The staged plain-store path (outputs that may be a peer GPU's memory): the same
+        output forms as the TMA-store path."""
+        outs = self.k.outputs
+        return len(outs) == 1 and outs[0].dtype in ("bf16", "f16") and self.N % 8 == 0 and self.vec_ok()
+
+    def store16_function(self) -> str:
+        """``store16(prm, b, i, j, v)``: 8 packed output elements at (batch b, row i, column j),
+        nothing outside the output (the staged store path)."""
+        o = self.k.outputs[0]
+        oi = self.out_index[o.id]
+        L = ["  template <class P>",
+             "  static __device__ __forceinline__ void store16(const P& prm, long b, long i, long j, const uint4& v) {",
+             f"    if (i >= {self.M}L || j >= {self.N}L) return;"]
+        L += ["    " + x for x in self._status_lines()]
+        L.append("    " + ptr_decl(f"out{oi}", CTYPE[o.dtype], oi, o.numel, False, self.kernel_id))
+        bl, bidx = self.batch_index_lines("b")
+        L += ["    " + x for x in bl]
+        L.append(f"    tj_st16(out{oi} + ({self.out_offset(bidx, 'i', 'j')}), v);")
+        L.append("  }")
+        return "\n".join(L)
+
     def vals32_function(self) -> str:
         """``epilogue_vals(prm, b, i, j0, acc[32], out[32])``: the output values of one row's 32
         columns (rows >= M and columns >= N are left at 0; the TMA store clips them)."""
@@ -742,12 +764,15 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     b_mats = prod(b.shape[:-2])
     bl, bidx = decompose_stmts("b", batch_shape, "bb") if batch_shape else ([], [])
     tma_store = epi.tma_store_ok() and not x3 and ksplit == 1
+    # outputs that may be a peer GPU's memory: staged in shared memory like the TMA-store path,
+    # then written with plain coalesced 16-byte stores (whole row segments per instruction)
+    staged = not tma_store and not tma_store_allowed() and epi.staged_store_ok() and not x3 and ksplit == 1
     L = [HEADER, '#include "gemm_sm100_pair.cuh"' if pair else '#include "gemm_sm100.cuh"',
          params_struct(nptr, 4 if x3 else (3 if tma_store else 2))]
     L.append("struct Cfg {")
     epi_warps = 8 if (BN % 64 == 0 or pair) else 4
     threads = 64 + 32 * epi_warps
-    out_stage = epi_warps * 2 * 32 * 32 * 2 if tma_store else 0
+    out_stage = epi_warps * 2 * 32 * 32 * 2 if (tma_store or staged) else 0
     GROUP_N = int((tile or {}).get("GROUP_N", 0))
     L.append(f"  static constexpr int BN = {BN}, STAGES = {STAGES}, M = {M}, N = {N}, K = {K}, GROUP_M = {GROUP_M};")
     L.append(f"  static constexpr int GROUP_N = {GROUP_N};")
@@ -756,7 +781,8 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     L.append("  static __device__ __forceinline__ int seg_tile0(int) { return 0; }")
     L.append(f"  static constexpr bool TF32X3 = {'true' if x3 else 'false'};")
     L.append(f"  static constexpr bool TMA_STORE = {'true' if tma_store else 'false'};")
-    L.append(f"  using OutT = {CTYPE[outs[0].dtype] if tma_store else 'float'};")
+    L.append(f"  static constexpr bool STAGED_STORE = {'true' if staged else 'false'};")
+    L.append(f"  using OutT = {CTYPE[outs[0].dtype] if (tma_store or staged) else 'float'};")
     L.append(f"  static constexpr long BATCH = {batch}L, A_MATS = {a_mats}L, B_MATS = {b_mats}L;")
     L.append(f"  static constexpr bool BF16 = {'true' if a.dtype == 'bf16' else 'false'}, B_MN_MAJOR = {'true' if b_mn else 'false'};")
     L.append("  static __device__ __forceinline__ void batch_map(long b, long& ab, long& bb_) {")
@@ -766,6 +792,9 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     L.append("  }")
     if ksplit > 1:
         L.append(partial_store_function(M, N, nptr - 1, ksplit * batch * M * N, kernel_id, status_idx))
+    elif staged:
+        L.append(epi.vals32_function())
+        L.append(epi.store16_function())
     else:
         L.append(epi.vals32_function() if tma_store else epi.chunk32_function())
     L.append("};")
@@ -822,7 +851,8 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     ks = KernelSource(symbol, "gemm_tc", "\n".join(L), (grid, 1, 1), (threads, 1, 1), args, smem=smem,
                       tmaps=tmaps, cluster=(2, 1, 1) if pair else (1, 1, 1),
                       info={"M": M, "N": N, "K": K, "batch": batch, "BN": BN, "stages": STAGES,
-                            "tma_store": tma_store, "epi_warps": epi_warps, "pair": pair, "tf32x3": x3,
+                            "tma_store": tma_store, "staged_store": staged, "epi_warps": epi_warps, "pair": pair,
+                            "tf32x3": x3,
                             "ksplit": ksplit, "packed": [x for x, f in (("a", pk_a), ("b", pk_b)) if f],
                             "flops": 2.0 * batch * M * N * K, "tiles": num_tiles,
                             "bytes": sum(n.nbytes for n in ins) + sum(o.nbytes for o in outs)})
@@ -860,7 +890,7 @@ def gen_gemm_multi(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = 
     L.append(f"  static constexpr int BN = {BN}, STAGES = {STAGES}, M = {M}, N = {N}, K = {K}, GROUP_M = {GROUP_M};")
     L.append(f"  static constexpr int GROUP_N = {int((tile or {}).get('GROUP_N', 0))};")
     L.append(f"  static constexpr int EPI_WARPS = 8, KSPLIT = 1, NSEG = {len(parts)};")
-    L.append("  static constexpr bool TF32X3 = false, TMA_STORE = false;")
+    L.append("  static constexpr bool TF32X3 = false, TMA_STORE = false, STAGED_STORE = false;")
     L.append("  using OutT = float;")
     L.append("  static constexpr long BATCH = 1L, A_MATS = 1L, B_MATS = 1L;")
     L.append(f"  static constexpr bool BF16 = {'true' if dt == 'bf16' else 'false'}, B_MN_MAJOR = false;")

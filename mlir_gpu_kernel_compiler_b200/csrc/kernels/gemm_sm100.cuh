@@ -235,16 +235,47 @@ TJ_DEV void tile_coords(long t, int m_tiles, int n_tiles, int group_m, int group
   nt = n_first + in_g / gsize;
 }
 
+// Plain coalesced stores of one epilogue warp's staged block: 32 rows x (32 * nch) columns of
+// 16-bit outputs, chunk c of the block in stage buffer c (32 rows x 64 bytes each, 16-byte
+// pieces swizzled as the TMA-store path writes them: piece ^= (row >> 1) & 3).  With two chunks
+// a row is one 128-byte segment (8 lanes, 4 rows per instruction); with one, 64 bytes (4 lanes,
+// 8 rows).  Used instead of TMA stores for outputs that may be another GPU's memory, where
+// whole-line writes matter most.  Cfg::store16(prm, b, i, j, v) stores 8 elements at (i, j)
+// (nothing for rows >= M or columns >= N).
+template <class Cfg, class P>
+TJ_DEV void staged_store_rows(const P& prm, const uint8_t* stage, uint32_t out_stage, int nch, long b, long row_base,
+                              long j0, int lane) {
+  if (nch == 2) {
+    const int piece = lane & 7;
+    const uint8_t* buf = stage + (piece >> 2) * out_stage;
+#pragma unroll
+    for (int rr = 0; rr < 8; ++rr) {
+      const int row = rr * 4 + (lane >> 3);
+      const uint4 v = *reinterpret_cast<const uint4*>(buf + row * 64 + (((piece & 3) ^ ((row >> 1) & 3)) << 4));
+      Cfg::store16(prm, b, row_base + row, j0 + piece * 8, v);
+    }
+  } else {
+    const int piece = lane & 3;
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      const int row = rr * 8 + (lane >> 2);
+      const uint4 v = *reinterpret_cast<const uint4*>(stage + row * 64 + ((piece ^ ((row >> 1) & 3)) << 4));
+      Cfg::store16(prm, b, row_base + row, j0 + piece * 8, v);
+    }
+  }
+}
+
 // Cfg provides:
 //   static constexpr int BN, STAGES, M, N, K, GROUP_M, GROUP_N, EPI_WARPS, KSPLIT, NSEG; static constexpr long BATCH;
 //   (NSEG > 1: static __device__ int segment(int nt), seg_tile0(int g) map a column tile to its B operand)
-//   static constexpr bool BF16, B_MN_MAJOR, TMA_STORE;  using OutT = <output element type>;
+//   static constexpr bool BF16, B_MN_MAJOR, TMA_STORE, STAGED_STORE;  using OutT = <output element type>;
 //   static __device__ void batch_map(long b, long& a_batch, long& b_batch);
 //   template <class P> static __device__ void epilogue(const P& prm, long b, long i, long j0, const float (&acc)[32]);
 //     (direct 16-byte stores), or with TMA_STORE:
 //   template <class P> static __device__ void epilogue_vals(const P& prm, long b, long i, long j0,
 //                                                           const float (&acc)[32], float (&out)[32]);
-//     (values only; the kernel stages them in shared memory and stores 32 x 32 tiles with TMA)
+//     (values only; the kernel stages them in shared memory and stores 32 x 32 tiles with TMA),
+//   or with STAGED_STORE: epilogue_vals and store16 (staged, then plain coalesced stores)
 template <class Cfg, class P>
 __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel_id) {
   // 3xTF32 mode (f32 operands): the stage holds hi and lo copies of A and B (written by the
@@ -283,7 +314,9 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
   uint8_t* sB = smem + STAGES * OPC * A_BYTES;     // stage s: [B (hi)][B lo]
   // TMA-store staging: per epilogue warp two 32 x 32 output tiles (64-byte rows, 64B swizzle)
   uint8_t* sOut = sB + STAGES * OPC * B_BYTES;
-  constexpr uint32_t OUT_STAGE = Cfg::TMA_STORE ? 32 * 32 * 2 : 0;
+  constexpr bool STAGED = Cfg::STAGED_STORE;
+  static_assert(!(STAGED && (Cfg::TMA_STORE || X3)), "one store path");
+  constexpr uint32_t OUT_STAGE = (Cfg::TMA_STORE || STAGED) ? 32 * 32 * 2 : 0;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + EPI_WARPS * 2 * OUT_STAGE);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
@@ -495,7 +528,23 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
         float acc[32];
         tmem_ld32(tbase + c * 32, acc);
         const long j0 = static_cast<long>(nt) * BN + col0 + c * 32;
-        if constexpr (!Cfg::TMA_STORE) {
+        if constexpr (STAGED) {
+          float vals[32];
+          Cfg::epilogue_vals(prm, b, i, j0, acc, vals);
+          if ((c & 1) == 0) __syncwarp();  // the previous block's stage reads are done
+          uint8_t* dst = stage_out + (c & 1) * OUT_STAGE + lane * 64;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const uint4 v = tj_pack(vals + 8 * cc, static_cast<const typename Cfg::OutT*>(nullptr));
+            *reinterpret_cast<uint4*>(dst + ((cc ^ ((lane >> 1) & 3)) << 4)) = v;
+          }
+          if ((c & 1) || c == EPI_COLS / 32 - 1) {
+            __syncwarp();
+            const int nch = (c & 1) + 1;
+            staged_store_rows<Cfg>(prm, stage_out, OUT_STAGE, nch, b, static_cast<long>(mt) * BM + q * 32,
+                                   j0 - 32 * (nch - 1), lane);
+          }
+        } else if constexpr (!Cfg::TMA_STORE) {
           Cfg::epilogue(prm, b, i, j0, acc);
         } else {
           float vals[32];

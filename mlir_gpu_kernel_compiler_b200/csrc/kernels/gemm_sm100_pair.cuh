@@ -147,7 +147,9 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sOut = sB + STAGES * B_BYTES;
-  constexpr uint32_t OUT_STAGE = Cfg::TMA_STORE ? 32 * 32 * 2 : 0;
+  constexpr bool STAGED = Cfg::STAGED_STORE;   // plain coalesced stores through the stage
+  static_assert(!(STAGED && Cfg::TMA_STORE), "one store path");
+  constexpr uint32_t OUT_STAGE = (Cfg::TMA_STORE || STAGED) ? 32 * 32 * 2 : 0;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + EPI_WARPS * 2 * OUT_STAGE);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
@@ -332,7 +334,22 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
         float acc[32];
         tmem_ld32(tbase + c * 32, acc);
         const long j0 = static_cast<long>(nt) * BN + col0 + c * 32;
-        if constexpr (!Cfg::TMA_STORE) {
+        if constexpr (STAGED) {
+          float vals[32];
+          Cfg::epilogue_vals(prm, b, i, j0, acc, vals);
+          if ((c & 1) == 0) __syncwarp();  // the previous block's stage reads are done
+          uint8_t* dst = stage_out + (c & 1) * OUT_STAGE + lane * 64;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const uint4 v = tj_pack(vals + 8 * cc, static_cast<const typename Cfg::OutT*>(nullptr));
+            *reinterpret_cast<uint4*>(dst + ((cc ^ ((lane >> 1) & 3)) << 4)) = v;
+          }
+          if ((c & 1) || c == EPI_COLS / 32 - 1) {
+            __syncwarp();
+            const int nch = (c & 1) + 1;
+            staged_store_rows<Cfg>(prm, stage_out, OUT_STAGE, nch, b, row0, j0 - 32 * (nch - 1), lane);
+          }
+        } else if constexpr (!Cfg::TMA_STORE) {
           Cfg::epilogue(prm, b, i, j0, acc);
         } else {
           float vals[32];

@@ -214,6 +214,9 @@ template <typename T> TJ_DEV void tj_load_vec_stream(tj_cptr<const T> q, float* 
 template <typename T> TJ_DEV void tj_store_vec(tj_cptr<T> q, const float* f) {
   if (q.check(TjVec<T>::N)) tj_store_vec(q.p + q.off, f);
 }
+template <typename T> TJ_DEV void tj_st16(tj_cptr<T> q, uint4 v) {
+  if (q.check(static_cast<int>(16 / sizeof(T)))) tj_st16(q.p + q.off, v);
+}
 // a condition the generated code asserts (a TMA coordinate, a TMEM column): false = violation
 TJ_DEV bool tj_check(bool ok, int* status, int where, int arg, long what) {
   if (!ok) tj_report_bounds(status, where, arg, what);

@@ -534,6 +534,7 @@ def test_peer_output_programs_store_without_tma():
     assert not any(k.info["tma_store"] for k in peer)
     assert [len(k.tmaps) for k in peer] == [len(k.tmaps) - int(k.info["tma_store"]) for k in normal]
     assert "TMA_STORE = false" in peer[-1].source
+    assert all(k.info["staged_store"] for k in peer) and not any(k.info["staged_store"] for k in normal)
     prog = B200Program(plan, device="cuda", peer_outputs=False)
     with pytest.raises(ValueError, match="peer_outputs"):
         prog.run_into([], [1 << 40])
