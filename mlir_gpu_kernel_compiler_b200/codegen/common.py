@@ -56,6 +56,51 @@ def store_mode(tma_store: bool = True):
         _TMA_STORE.reset(token)
 
 
+# 3xTF32 operand forwarding: an f32 intermediate whose only reader is a 3xTF32 GEMM is written by
+# its producer directly as that GEMM's TF32 hi / lo copies in the workspace, so the GEMM's split
+# launch keeps only the operands that are program inputs.  ``split_out``: node id -> elements from
+# the hi copy to the lo copy; ``split_skip``: plan kernel index -> operands ("a" / "b") whose
+# split its producer already wrote.
+_SPLIT_OUT = contextvars.ContextVar("tj_split_out", default=None)
+_SPLIT_SKIP = contextvars.ContextVar("tj_split_skip", default=None)
+
+
+def split_out() -> dict:
+    return _SPLIT_OUT.get() or {}
+
+
+def split_skip(kernel_id: int) -> set:
+    return (_SPLIT_SKIP.get() or {}).get(kernel_id, set())
+
+
+@contextlib.contextmanager
+def split_forwarding(out: dict, skip: dict):
+    t1, t2 = _SPLIT_OUT.set(dict(out)), _SPLIT_SKIP.set(dict(skip))
+    try:
+        yield
+    finally:
+        _SPLIT_SKIP.reset(t2)
+        _SPLIT_OUT.reset(t1)
+
+
+def split_store_lines(ptr: str, off: str, src: str, n: int, delta: int) -> list[str]:
+    """Store the ``n`` f32 values ``src[0..n)`` at ``ptr + off`` as their TF32 split: hi (13 low
+    mantissa bits cleared, as the split launch computes it) there, lo = value - hi ``delta``
+    elements further on; 16-byte stores for n a multiple of 4, else scalar."""
+    L = [f"{{ float sh[{n}], sl[{n}];",
+         "  #pragma unroll",
+         f"  for (int q = 0; q < {n}; ++q) {{ sh[q] = tj_tf32_hi({src}[q]); sl[q] = {src}[q] - sh[q]; }}"]
+    if n % 4 == 0:
+        for c in range(0, n, 4):
+            L.append(f"  tj_store_vec({ptr} + ({off}) + {c}, sh + {c}); "
+                     f"tj_store_vec({ptr} + ({off}) + {delta + c}L, sl + {c});")
+    else:
+        for c in range(n):
+            L.append(f"  {ptr}[({off}) + {c}] = sh[{c}]; {ptr}[({off}) + {delta + c}L] = sl[{c}];")
+    L.append("}")
+    return L
+
+
 def ptr_decl(name: str, ctype: str, idx: int, numel: int, const: bool, kernel_id: int = 0,
              status: str = "tj_status") -> str:
     """Declaration of kernel argument ``idx`` as ``name``: a restrict pointer, or in a checked

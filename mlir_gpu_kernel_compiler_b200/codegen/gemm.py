@@ -28,8 +28,8 @@ import os
 
 from ..plan import PKernel, PNode, access_strides, contiguous_strides, first_consumer
 from .common import (PDL, BOUNDS_SITE, CTYPE, HEADER, ITEM, NUM_SMS, TMAP_DTYPE, KernelSource, TMapSpec, checked,
-                     decompose_stmts, expr, fast_math_for, offset_expr, params_struct, prod, ptr_decl, status_decl,
-                     tma_store_allowed)
+                     decompose_stmts, expr, fast_math_for, offset_expr, params_struct, prod, ptr_decl, split_out,
+                     split_skip, split_store_lines, status_decl, tma_store_allowed)
 
 
 def _mm_dims(k: PKernel):
@@ -418,17 +418,25 @@ def gen_matmul_tc_x3(k: PKernel, symbol: str, kernel_id: int, tile: dict | None)
     BN, ksplit = x3_tile(M, N, K, batch, tile)
     tile = dict(tile or {"STAGES": 4, "GROUP_M": 16}, BN=BN)
     ws = part + (_align(ksplit * batch * M * N * 4) if ksplit > 1 else 0)
-    if a.dtype == b.dtype == "f32" and tb and K % 4 == 0:
-        # both operands already K-major f32 with a 16-byte pitch: the vectorised split
-        sp = gen_split_tf32(f"{symbol}_split", [(a.numel, ("node", a), a_hi, a_lo),
-                                                (b.numel, ("node", b), b_hi, b_lo)], kernel_id)
+    vec_split = a.dtype == b.dtype == "f32" and tb and K % 4 == 0
+    skip = split_skip(kernel_id) if vec_split else set()
+    if vec_split:
+        # both operands already K-major f32 with a 16-byte pitch: the vectorised split, minus the
+        # operands whose producer writes the hi / lo copies itself (3xTF32 operand forwarding)
+        segs = [seg for role, seg in (("a", (a.numel, ("node", a), a_hi, a_lo)),
+                                      ("b", (b.numel, ("node", b), b_hi, b_lo))) if role not in skip]
+        sp = gen_split_tf32(f"{symbol}_split", segs, kernel_id) if segs else None
     else:
         sp = gen_pack_operands(f"{symbol}_split", [_operand_segment(a, M, K, P, True, True, "f32", a_hi, a_lo),
                                                    _operand_segment(b, N, K, P, tb, True, "f32", b_hi, b_lo)],
                                kernel_id)
     g = gen_gemm_tc(k, symbol, kernel_id, tile, x3_scratch=(a_hi, b_hi, a_lo, b_lo),
                     ksplit=ksplit, partial_scratch=part)
-    parts = [sp, g]
+    if vec_split:
+        # where each operand's hi / lo copies are (workspace offsets), for operand forwarding
+        g.info["x3_vec"] = {"a": (a.id, a_hi, a_lo), "b": (b.id, b_hi, b_lo)}
+        g.info["x3_forwarded"] = sorted(skip)
+    parts = [sp, g] if sp is not None else [g]
     if ksplit > 1:
         parts.append(gen_ksplit_finalize(k, f"{symbol}_finalize", g.args, ksplit, kernel_id))
     for ks in parts:
@@ -491,6 +499,7 @@ class Epilogue:
             self.strides[n.id] = access_strides(n, c, out_shape)
         self.dtype_out = {o.id: o.dtype for o in k.outputs}
         self.fast = fast_math_for(self.dtype_out.values())
+        self.fwd = {o.id: split_out()[o.id] for o in k.outputs if o.id in split_out()}   # hi -> lo distance
 
     def vec_ok(self) -> bool:
         """8-column vector path: every epilogue operand unit-stride or broadcast along j,
@@ -565,7 +574,9 @@ class Epilogue:
             off = self.out_offset(bidx, "i", "j")
             for j, o in enumerate(outs):
                 oi = self.out_index[o.id]
-                if o.dtype == "f32":
+                if o.id in self.fwd:
+                    L += ["      " + x for x in split_store_lines(f"out{oi}", off, f"o{j}", 8, self.fwd[o.id])]
+                elif o.dtype == "f32":
                     L.append(f"      tj_store_vec(out{oi} + ({off}), o{j}); tj_store_vec(out{oi} + ({off}) + 4, o{j} + 4);")
                 else:
                     L.append(f"      tj_store_vec(out{oi} + ({off}), o{j});")
@@ -662,7 +673,8 @@ class Epilogue:
         L = self._status_lines() + self._in_lines()
         for o in self.k.outputs:
             oi = self.out_index[o.id]
-            L.append(ptr_decl(f"out{oi}", CTYPE[o.dtype], oi, o.numel, False, self.kernel_id))
+            L.append(ptr_decl(f"out{oi}", CTYPE[o.dtype], oi, o.numel + self.fwd.get(o.id, 0), False,
+                              self.kernel_id))
         return L
 
     def scalar_element_lines(self, bidx: list[str], ivar: str, jvar: str, acc: str) -> list[str]:
@@ -677,7 +689,11 @@ class Epilogue:
         off = self.out_offset(bidx, ivar, jvar)
         for o in self.k.outputs:
             oi = self.out_index[o.id]
-            L.append(f"out{oi}[{off}] = tj_from<{CTYPE[o.dtype]}>({m[o.id]});")
+            if o.id in self.fwd:
+                L.append(f"const float so{o.id}[1] = {{{m[o.id]}}};")
+                L += split_store_lines(f"out{oi}", off, f"so{o.id}", 1, self.fwd[o.id])
+            else:
+                L.append(f"out{oi}[{off}] = tj_from<{CTYPE[o.dtype]}>({m[o.id]});")
         return L
 
 

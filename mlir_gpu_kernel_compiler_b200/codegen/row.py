@@ -20,7 +20,7 @@ from __future__ import annotations
 
 from ..plan import PKernel, PNode, broadcast_strides
 from .common import (PDL, CTYPE, HEADER, KernelSource, checked, expr, fast_math_for, literal, offset_expr, params_struct,
-                     pick_vec, prod, ptr_decl, status_decl)
+                     pick_vec, prod, ptr_decl, split_out, split_store_lines, status_decl)
 
 CTA_THREADS = 256
 
@@ -95,8 +95,10 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str,
         L.append("  " + status_decl(len(ins) + len(outs)))
     for j, n in enumerate(ins):
         L.append("  " + ptr_decl(f"in{j}", CTYPE[n.dtype], j, n.numel, True, kernel_id))
+    fwd = split_out()       # outputs written as a 3xTF32 GEMM's hi / lo operand copies
     for j, o in enumerate(outs):
-        L.append("  " + ptr_decl(f"out{j}", CTYPE[o.dtype], len(ins) + j, o.numel, False, kernel_id))
+        L.append("  " + ptr_decl(f"out{j}", CTYPE[o.dtype], len(ins) + j, o.numel + fwd.get(o.id, 0), False,
+                                 kernel_id))
     nred = sum(1 for st in stages if st.kind == "reduce")
     if TPR > 32 and nred:
         L.append(f"  __shared__ float red[{nred}][{RPC}][{NW}];")
@@ -329,7 +331,11 @@ def gen_row(k: PKernel, stages: list[PKernel], rows: tuple, N: int, symbol: str,
             j = escaping[n.id]
             o = outs[j]
             cond = "valid" if all_valid else f"valid && vv < {NVEC}L"
-            if VEC > 1:
+            if n.id in fwd:
+                out.append(f"  if ({cond})")
+                out += ["  " + x for x in split_store_lines(f"out{j}", f"r * {N}L + vv * {VEC}L", f"ob{n.id}", VEC,
+                                                             fwd[n.id])]
+            elif VEC > 1:
                 out.append(f"  if ({cond}) tj_store_vec(out{j} + r * {N}L + vv * {VEC}L, ob{n.id});")
             else:
                 out.append(f"  if ({cond}) out{j}[r * {N}L + vv] = tj_from<{CTYPE[o.dtype]}>(ob{n.id}[0]);")

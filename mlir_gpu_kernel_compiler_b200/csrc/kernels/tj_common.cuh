@@ -39,6 +39,10 @@ TJ_DEV uint4 tj_ld16_stream(const void* p) {
 }
 TJ_DEV void tj_st16(void* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
 
+// hi part of the TF32 split of 3xTF32 operands: v with its 13 low mantissa bits cleared (the
+// lo part v - hi is exact in f32)
+TJ_DEV float tj_tf32_hi(float v) { return __uint_as_float(__float_as_uint(v) & 0xffffe000u); }
+
 TJ_DEV void tj_unpack(uint4 v, float* f, const float*) {
   f[0] = __uint_as_float(v.x); f[1] = __uint_as_float(v.y);
   f[2] = __uint_as_float(v.z); f[3] = __uint_as_float(v.w);

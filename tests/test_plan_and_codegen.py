@@ -538,3 +538,35 @@ def test_peer_output_programs_store_without_tma():
     prog = B200Program(plan, device="cuda", peer_outputs=False)
     with pytest.raises(ValueError, match="peer_outputs"):
         prog.run_into([], [1 << 40])
+
+
+def test_3xtf32_operand_forwarding():
+    """cfg1: the LayerNorm writes its output as the first GEMM's TF32 hi / lo A operand, and the
+    first GEMM's GELU epilogue writes h as the second GEMM's; the split launches keep only the
+    weights (program inputs, split before the wait).  Forwarding stops where the operand has
+    another reader or is a program output."""
+    plan = FX.load_plan("cfg1")
+    ks = generate(plan)
+    row, sp1, g1, sp2, g2 = ks[:5]
+    assert [k.family for k in ks] == ["row", "split", "gemm_tc", "split", "gemm_tc", "ewise"]
+    assert row.info["forwarded_outputs"] and g1.info["forwarded_outputs"]
+    assert g1.info["x3_forwarded"] == ["a"] and g2.info["x3_forwarded"] == ["a"]
+    for sp in (sp1, sp2):       # one segment each, the weight, handled before the wait
+        assert len(sp.args) == 3 and sp.args[0][1].op == "input" and sp.info["early_segments"] == 1
+    # the row kernel's output argument is the first GEMM's A hi copy, the GEMM's h argument the second's
+    assert ("scratch", g1.info["scratch_base"] + g1.info["x3_vec"]["a"][1]) in row.args
+    assert ("scratch", g2.info["scratch_base"] + g2.info["x3_vec"]["a"][1]) in g1.args
+    assert "tj_tf32_hi" in row.source and "tj_tf32_hi" in g1.source
+    # the hi -> lo distance in the stores equals the consumer's layout
+    a_hi, a_lo = g1.info["x3_vec"]["a"][1:]
+    assert f"+ {(a_lo - a_hi) // 4}L" in row.source
+    # a program output is never forwarded: the plan with x_ln also returned keeps its split
+    from mlir_gpu_kernel_compiler_b200.codegen import _split_forwarding
+
+    first = generate(plan)
+    fwd, skip = _split_forwarding(plan, first)
+    xln = plan.kernels[0].outputs[0]
+    assert xln.id in fwd and skip == {1: {"a"}, 2: {"a"}}
+    plan.outputs.append(xln)
+    fwd2, skip2 = _split_forwarding(plan, first)
+    assert xln.id not in fwd2 and 1 not in skip2
