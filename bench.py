@@ -437,7 +437,7 @@ def measure_side_config(cfg: str, a, dev) -> dict:
 
 def rows_on_root_step(plan, prog, ins, outs, total_rows: int, steps: int, dev, barrier) -> dict:
     """The step with its output gathered on rank 0 without a collective: every rank's program
-    (built with plain-store epilogues) is launched with its rows of rank 0's full-size y as the
+    (built with staged plain-store epilogues) is launched with its rows of rank 0's full-size y as the
     output, a CUDA IPC mapping on the other ranks, so the down projection's epilogue stores its
     tiles into rank 0's HBM over NVLink while the GEMM runs.  Timed in alternation with the
     ordinary step (local y), three rounds each (events, barrier + synchronize on both sides,
@@ -498,7 +498,7 @@ def rows_on_root_step(plan, prog, ins, outs, total_rows: int, steps: int, dev, b
                 "rounds_ms": {"local": local_ms, "rows_on_root": peer_ms},
                 "bytes_to_rank0": nbytes * (world - 1) // world, "rows_identical": bool(same.item()),
                 "how": "step whose last GEMM stores its rows into rank 0's y over NVLink (CUDA IPC mapping, "
-                       f"plain-store epilogue), alternating with the ordinary step, 3 rounds x {steps} steps, "
+                       f"staged plain-store epilogue), alternating with the ordinary step, 3 rounds x {steps} steps, "
                        "max over ranks, median round; rows_identical: rank 0's copy of every rank's rows has "
                        "the checksums of that rank's locally stored y (rank 0's: bit for bit)"}
     finally:

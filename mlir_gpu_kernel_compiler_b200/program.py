@@ -102,7 +102,8 @@ class B200Program:
         # checked build: every global access bounds-checked, violations reported as TJ_STATUS_BOUNDS
         self.checked = (os.environ.get("TENSORJIT_B200_CHECKED") == "1") if checked is None else bool(checked)
         # peer_outputs: the caller may bind outputs to another GPU's memory (rows stored over
-        # NVLink into a peer's buffer, ``distributed.RowsOnRoot``), so epilogues use plain stores
+        # NVLink into a peer's buffer, ``distributed.RowsOnRoot``), so epilogues stage their tiles in
+        # shared memory and write them with plain coalesced stores (no TMA store into peer memory)
         self.peer_outputs = bool(peer_outputs)
         self.kernel_sources = generate(self.xplan, tiles=tiles, checked=self.checked,
                                        tma_store=not self.peer_outputs)
