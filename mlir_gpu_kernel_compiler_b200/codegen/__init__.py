@@ -12,6 +12,8 @@ pre-pass; see ``gemm.gemm_form``); ``attention`` (the matmul -> softmax -> matmu
 """
 from __future__ import annotations
 
+import os
+
 from ..plan import PProgram
 from .attention import gen_attention
 from .common import KernelSource, checked_build, split_forwarding, store_mode
@@ -35,6 +37,8 @@ def _generate(plan: PProgram, tiles: dict | None, prefix: str) -> list[KernelSou
     lays out every matmul's workspace, the second has the producers of forwarded operands
     write the hi / lo copies there and drops those operands from the split launches."""
     first = _generate_pass(plan, tiles, prefix, {})
+    if os.environ.get("TENSORJIT_B200_FORWARD") == "0":
+        return first
     fwd, skip = _split_forwarding(plan, first)
     if not fwd:
         return first

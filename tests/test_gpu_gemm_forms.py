@@ -10,6 +10,7 @@ per product), 2e-2 for bf16/f16 (the output is rounded to the half type).
 import pytest
 import torch
 
+from oracle import fixtures as FX
 from oracle.plan_oracle import evaluate, normwise_error
 
 pytestmark = pytest.mark.gpu
@@ -92,3 +93,27 @@ def test_matmul_with_empty_k_is_its_epilogue():
     prog.check()
     ref = torch.nn.functional.gelu(c).expand(6, 5)
     assert normwise_error(y, ref) <= 1e-4
+
+
+@pytest.mark.parametrize("case", ["cfg1", "cuda_mlp__f32", "transformer_block__f32", "block_tail__f32"])
+def test_forwarded_3xtf32_operands_are_bit_identical(case, monkeypatch):
+    """Producers that write a 3xTF32 GEMM's hi / lo operand copies themselves compute the same
+    split as the split launch, so the program's outputs are the same bits with forwarding off
+    (``TENSORJIT_B200_FORWARD=0``) and on."""
+    from mlir_gpu_kernel_compiler_b200 import B200Program
+    from mlir_gpu_kernel_compiler_b200 import workloads as W
+
+    if case == "cfg1":
+        plan, ins = FX.load_plan("cfg1"), [t.cuda() for t in W.make_inputs(W.WORKLOADS["cfg1"])]
+    else:
+        plan, ins = FX.load_plan(case), [t.cuda() for t in FX.case_inputs(case)]
+    outs = {}
+    for flag in ("0", "1"):
+        monkeypatch.setenv("TENSORJIT_B200_FORWARD", flag)
+        prog = B200Program(plan, device="cuda")
+        assert any(k.info.get("forwarded_outputs") for k in prog.kernel_sources) == (flag == "1")
+        outs[flag] = prog(*ins)
+        torch.cuda.synchronize()
+        prog.check()
+    for a, b in zip(outs["0"], outs["1"]):
+        assert torch.equal(a, b), case
