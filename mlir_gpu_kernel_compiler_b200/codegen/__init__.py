@@ -33,11 +33,13 @@ def generate(plan: PProgram, tiles: dict | None = None, prefix: str = "tj", chec
 
 
 def _generate(plan: PProgram, tiles: dict | None, prefix: str) -> list[KernelSource]:
-    """Two passes when 3xTF32 operands can be forwarded (``_split_forwarding``): the first
-    lays out every matmul's workspace, the second has the producers of forwarded operands
-    write the hi / lo copies there and drops those operands from the split launches."""
+    """With ``TENSORJIT_B200_FORWARD=1``, two passes when 3xTF32 operands can be forwarded
+    (``_split_forwarding``): the first lays out every matmul's workspace, the second has the
+    producers of forwarded operands write the hi / lo copies there and drops those operands from
+    the split launches.  Off by default: on cfg1 the GEMM epilogue that then writes both copies
+    costs more (its f32 stores are row-strided) than the split launch's activation pass saves."""
     first = _generate_pass(plan, tiles, prefix, {})
-    if os.environ.get("TENSORJIT_B200_FORWARD") == "0":
+    if os.environ.get("TENSORJIT_B200_FORWARD", "0") != "1":   # off by default: measured slower
         return first
     fwd, skip = _split_forwarding(plan, first)
     if not fwd:

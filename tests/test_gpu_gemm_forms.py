@@ -99,7 +99,7 @@ def test_matmul_with_empty_k_is_its_epilogue():
 def test_forwarded_3xtf32_operands_are_bit_identical(case, monkeypatch):
     """Producers that write a 3xTF32 GEMM's hi / lo operand copies themselves compute the same
     split as the split launch, so the program's outputs are the same bits with forwarding off
-    (``TENSORJIT_B200_FORWARD=0``) and on."""
+    (the default) and on (``TENSORJIT_B200_FORWARD=1``)."""
     from mlir_gpu_kernel_compiler_b200 import B200Program
     from mlir_gpu_kernel_compiler_b200 import workloads as W
 

@@ -540,12 +540,14 @@ def test_peer_output_programs_store_without_tma():
         prog.run_into([], [1 << 40])
 
 
-def test_3xtf32_operand_forwarding():
+def test_3xtf32_operand_forwarding(monkeypatch):
     """cfg1: the LayerNorm writes its output as the first GEMM's TF32 hi / lo A operand, and the
     first GEMM's GELU epilogue writes h as the second GEMM's; the split launches keep only the
     weights (program inputs, split before the wait).  Forwarding stops where the operand has
     another reader or is a program output."""
     plan = FX.load_plan("cfg1")
+    assert not any(k.info.get("forwarded_outputs") for k in generate(plan))     # off by default
+    monkeypatch.setenv("TENSORJIT_B200_FORWARD", "1")
     ks = generate(plan)
     row, sp1, g1, sp2, g2 = ks[:5]
     assert [k.family for k in ks] == ["row", "split", "gemm_tc", "split", "gemm_tc", "ewise"]
