@@ -604,6 +604,29 @@ class Epilogue:
         outs = self.k.outputs
         return len(outs) == 1 and outs[0].dtype in ("bf16", "f16") and self.N % 8 == 0 and self.vec_ok()
 
+    def stage_last_ok(self) -> bool:
+        """The last-tile staged path for one f32 output (16-byte pieces of 4 columns; the
+        vector operand path of ``epilogue_vals``)."""
+        outs = self.k.outputs
+        return len(outs) == 1 and outs[0].dtype == "f32" and self.N % 8 == 0 and self.vec_ok() and not self.fwd
+
+    def store4_function(self) -> str:
+        """``store4(prm, b, i, j, v)``: 4 f32 output values at (batch b, row i, columns j..j+3),
+        nothing outside the output (the last-tile staged path)."""
+        o = self.k.outputs[0]
+        oi = self.out_index[o.id]
+        L = ["  template <class P>",
+             "  static __device__ __forceinline__ void store4(const P& prm, long b, long i, long j, const float4& v) {",
+             f"    if (i >= {self.M}L || j >= {self.N}L) return;"]
+        L += ["    " + x for x in self._status_lines()]
+        L.append("    " + ptr_decl(f"out{oi}", "float", oi, o.numel, False, self.kernel_id))
+        bl, bidx = self.batch_index_lines("b")
+        L += ["    " + x for x in bl]
+        L.append(f"    tj_st16(out{oi} + ({self.out_offset(bidx, 'i', 'j')}), make_uint4(__float_as_uint(v.x), "
+                 "__float_as_uint(v.y), __float_as_uint(v.z), __float_as_uint(v.w)));")
+        L.append("  }")
+        return "\n".join(L)
+
     def store16_function(self) -> str:
         """``store16(prm, b, i, j, v)``: 8 packed output elements at (batch b, row i, column j),
         nothing outside the output (the staged store path)."""
@@ -700,6 +723,27 @@ class Epilogue:
 # ---------------------------------------------------------------------------
 # tcgen05 kernel
 # ---------------------------------------------------------------------------
+def partial_stage_functions(M: int, N: int, part_idx: int, numel: int = 0, kernel_id: int = 0,
+                            status_idx: int = 0) -> str:
+    """``epilogue_vals`` (the raw accumulator) and ``store4`` (into partial-sum slice b) of a
+    split-K GEMM, for the last-tile staged path (N % 4 == 0)."""
+    return "\n".join([
+        "  template <class P>",
+        "  static __device__ __forceinline__ void epilogue_vals(const P&, long, long, long, const float (&acc)[32], "
+        "float (&out)[32]) {",
+        "    #pragma unroll",
+        "    for (int c = 0; c < 32; ++c) out[c] = acc[c];",
+        "  }",
+        "  template <class P>",
+        "  static __device__ __forceinline__ void store4(const P& prm, long b, long i, long j, const float4& v) {",
+        f"    if (i >= {M}L || j >= {N}L) return;",
+        *(["    " + status_decl(status_idx)] if checked() else []),
+        "    " + ptr_decl("part", "float", part_idx, numel, False, kernel_id),
+        f"    tj_st16(part + ((b * {M}L + i) * {N}L + j), make_uint4(__float_as_uint(v.x), __float_as_uint(v.y), "
+        "__float_as_uint(v.z), __float_as_uint(v.w)));",
+        "  }"])
+
+
 def partial_store_function(M: int, N: int, part_idx: int, numel: int = 0, kernel_id: int = 0,
                            status_idx: int = 0) -> str:
     """``epilogue(prm, b, i, j0, acc[32])`` of a split-K GEMM: the raw f32 accumulator row
@@ -783,6 +827,11 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     # outputs that may be a peer GPU's memory: staged in shared memory like the TMA-store path,
     # then written with plain coalesced 16-byte stores (whole row segments per instruction)
     staged = not tma_store and not tma_store_allowed() and epi.staged_store_ok() and not x3 and ksplit == 1
+    # f32 outputs and split-K partial sums: the CTA's last tile staged in the idle pipeline memory
+    # (single-CTA kernel; not for outputs that may be a peer GPU's memory)
+    stage_last = (not tma_store and not staged and not pair and tma_store_allowed()
+                  and os.environ.get("TENSORJIT_B200_STAGE_LAST") != "0"
+                  and (N % 4 == 0 if ksplit > 1 else epi.stage_last_ok()))
     L = [HEADER, '#include "gemm_sm100_pair.cuh"' if pair else '#include "gemm_sm100.cuh"',
          params_struct(nptr, 4 if x3 else (3 if tma_store else 2))]
     L.append("struct Cfg {")
@@ -798,6 +847,7 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     L.append(f"  static constexpr bool TF32X3 = {'true' if x3 else 'false'};")
     L.append(f"  static constexpr bool TMA_STORE = {'true' if tma_store else 'false'};")
     L.append(f"  static constexpr bool STAGED_STORE = {'true' if staged else 'false'};")
+    L.append(f"  static constexpr bool STAGE_LAST = {'true' if stage_last else 'false'};")
     L.append(f"  using OutT = {CTYPE[outs[0].dtype] if (tma_store or staged) else 'float'};")
     L.append(f"  static constexpr long BATCH = {batch}L, A_MATS = {a_mats}L, B_MATS = {b_mats}L;")
     L.append(f"  static constexpr bool BF16 = {'true' if a.dtype == 'bf16' else 'false'}, B_MN_MAJOR = {'true' if b_mn else 'false'};")
@@ -808,6 +858,12 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     L.append("  }")
     if ksplit > 1:
         L.append(partial_store_function(M, N, nptr - 1, ksplit * batch * M * N, kernel_id, status_idx))
+        if stage_last:
+            L.append(partial_stage_functions(M, N, nptr - 1, ksplit * batch * M * N, kernel_id, status_idx))
+    elif stage_last:
+        L.append(epi.chunk32_function())
+        L.append(epi.vals32_function())
+        L.append(epi.store4_function())
     elif staged:
         L.append(epi.vals32_function())
         L.append(epi.store16_function())
@@ -867,7 +923,8 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     ks = KernelSource(symbol, "gemm_tc", "\n".join(L), (grid, 1, 1), (threads, 1, 1), args, smem=smem,
                       tmaps=tmaps, cluster=(2, 1, 1) if pair else (1, 1, 1),
                       info={"M": M, "N": N, "K": K, "batch": batch, "BN": BN, "stages": STAGES,
-                            "tma_store": tma_store, "staged_store": staged, "epi_warps": epi_warps, "pair": pair,
+                            "tma_store": tma_store, "staged_store": staged, "stage_last": stage_last,
+                            "epi_warps": epi_warps, "pair": pair,
                             "tf32x3": x3,
                             "ksplit": ksplit, "packed": [x for x, f in (("a", pk_a), ("b", pk_b)) if f],
                             "flops": 2.0 * batch * M * N * K, "tiles": num_tiles,
@@ -906,7 +963,7 @@ def gen_gemm_multi(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = 
     L.append(f"  static constexpr int BN = {BN}, STAGES = {STAGES}, M = {M}, N = {N}, K = {K}, GROUP_M = {GROUP_M};")
     L.append(f"  static constexpr int GROUP_N = {int((tile or {}).get('GROUP_N', 0))};")
     L.append(f"  static constexpr int EPI_WARPS = 8, KSPLIT = 1, NSEG = {len(parts)};")
-    L.append("  static constexpr bool TF32X3 = false, TMA_STORE = false, STAGED_STORE = false;")
+    L.append("  static constexpr bool TF32X3 = false, TMA_STORE = false, STAGED_STORE = false, STAGE_LAST = false;")
     L.append("  using OutT = float;")
     L.append("  static constexpr long BATCH = 1L, A_MATS = 1L, B_MATS = 1L;")
     L.append(f"  static constexpr bool BF16 = {'true' if dt == 'bf16' else 'false'}, B_MN_MAJOR = false;")

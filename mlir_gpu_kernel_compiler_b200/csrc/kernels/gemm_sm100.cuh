@@ -268,14 +268,16 @@ TJ_DEV void staged_store_rows(const P& prm, const uint8_t* stage, uint32_t out_s
 // Cfg provides:
 //   static constexpr int BN, STAGES, M, N, K, GROUP_M, GROUP_N, EPI_WARPS, KSPLIT, NSEG; static constexpr long BATCH;
 //   (NSEG > 1: static __device__ int segment(int nt), seg_tile0(int g) map a column tile to its B operand)
-//   static constexpr bool BF16, B_MN_MAJOR, TMA_STORE, STAGED_STORE;  using OutT = <output element type>;
+//   static constexpr bool BF16, B_MN_MAJOR, TMA_STORE, STAGED_STORE, STAGE_LAST;  using OutT = <output type>;
 //   static __device__ void batch_map(long b, long& a_batch, long& b_batch);
 //   template <class P> static __device__ void epilogue(const P& prm, long b, long i, long j0, const float (&acc)[32]);
 //     (direct 16-byte stores), or with TMA_STORE:
 //   template <class P> static __device__ void epilogue_vals(const P& prm, long b, long i, long j0,
 //                                                           const float (&acc)[32], float (&out)[32]);
 //     (values only; the kernel stages them in shared memory and stores 32 x 32 tiles with TMA),
-//   or with STAGED_STORE: epilogue_vals and store16 (staged, then plain coalesced stores)
+//   or with STAGED_STORE: epilogue_vals and store16 (staged, then plain coalesced stores);
+//   STAGE_LAST (f32 outputs, partial sums): also epilogue_vals and store4(prm, b, i, j, float4),
+//   used on the CTA's last tile (staged in the idle pipeline memory), epilogue on the others
 template <class Cfg, class P>
 __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel_id) {
   // 3xTF32 mode (f32 operands): the stage holds hi and lo copies of A and B (written by the
@@ -317,6 +319,12 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
   constexpr bool STAGED = Cfg::STAGED_STORE;
   static_assert(!(STAGED && (Cfg::TMA_STORE || X3)), "one store path");
   constexpr uint32_t OUT_STAGE = (Cfg::TMA_STORE || STAGED) ? 32 * 32 * 2 : 0;
+  // f32 outputs (and split-K partial sums): on the CTA's last tile the pipeline's stage memory is
+  // idle once the tile's MMAs have completed, so the epilogue stages its 32 x EPI_COLS block
+  // there and writes whole row segments instead of 16 bytes into each of 32 rows per store
+  constexpr bool STAGE_LAST = Cfg::STAGE_LAST;
+  static_assert(!STAGE_LAST || (!Cfg::TMA_STORE && !STAGED), "one store path");
+  static_assert(!STAGE_LAST || EPI_WARPS * 32 * EPI_COLS * 4 <= STAGES * STAGE_BYTES, "staging fits the stages");
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + EPI_WARPS * 2 * OUT_STAGE);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
@@ -520,6 +528,39 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
       const long i = static_cast<long>(mt) * BM + q * 32 + lane;
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN + col0);
+      if constexpr (STAGE_LAST) {
+        if (w + gridDim.x >= num_tiles) {
+          // this CTA's last tile: no further loads or MMAs will touch the stage memory
+          float* st = reinterpret_cast<float*>(smem) + (warp - 2) * 32 * EPI_COLS;
+          constexpr int PR = EPI_COLS / 4;  // 16-byte pieces per staged row (swizzle: piece ^ (row & 7))
+#pragma unroll 1
+          for (int c = 0; c < EPI_COLS / 32; ++c) {
+            TJ_CHECKED_ONLY(if (!tj_check(buf * BN + col0 + c * 32 + 32 <= static_cast<int>(TMEM_COLS), status,
+                                          kernel_id * 16 + 15, -2, c)) break;)
+            float acc[32];
+            tmem_ld32(tbase + c * 32, acc);
+            float vals[32];
+            Cfg::epilogue_vals(prm, b, i, static_cast<long>(nt) * BN + col0 + c * 32, acc, vals);
+#pragma unroll
+            for (int cc = 0; cc < 8; ++cc)
+              *reinterpret_cast<float4*>(st + lane * EPI_COLS + (((c * 8 + cc) ^ (lane & 7)) << 2)) =
+                  make_float4(vals[4 * cc], vals[4 * cc + 1], vals[4 * cc + 2], vals[4 * cc + 3]);
+          }
+          __syncwarp();
+          const long row_base = static_cast<long>(mt) * BM + q * 32;
+          const long col_base = static_cast<long>(nt) * BN + col0;
+#pragma unroll 4
+          for (int it = 0; it < PR; ++it) {  // one 16-byte piece per lane: PR iterations cover 32 rows
+            const int idx = it * 32 + lane;
+            const int row = idx / PR, p = idx % PR;
+            const float4 v = *reinterpret_cast<const float4*>(st + row * EPI_COLS + ((p ^ (row & 7)) << 2));
+            Cfg::store4(prm, b, row_base + row, col_base + p * 4, v);
+          }
+          tc_fence_before();
+          mbar_arrive(smem_u32(&tempty[buf]));
+          continue;
+        }
+      }
 #pragma unroll 1
       for (int c = 0; c < EPI_COLS / 32; ++c) {
         // checked build: the accumulator columns read lie inside this CTA's TMEM allocation

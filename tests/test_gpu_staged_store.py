@@ -1,11 +1,14 @@
-"""The plain-store epilogue of programs built for peer outputs (``peer_outputs=True``, used when
+"""Staged epilogue stores against the per-row stores, on one GPU.
+
+First, the plain-store epilogue of programs built for peer outputs (``peer_outputs=True``, used when
 a row shard's output is another GPU's memory) against the ordinary program on one GPU.
 
 Those GEMMs stage each warp's 32-row block in shared memory, as the TMA-store path does, and
 write it back with plain coalesced 16-byte stores (two 32-column chunks as 128-byte row
 segments, a lone chunk as 64-byte ones).  The stored values are the same, so the output must be
 the same bits, for ragged row counts, column counts that end inside a chunk, batched and
-broadcast GEMMs, single-CTA and CTA-pair tiles.
+broadcast GEMMs, single-CTA and CTA-pair tiles.  Second, the last-tile staging of f32 outputs and
+split-K partial sums through the idle pipeline memory.
 """
 import pytest
 import torch
@@ -68,3 +71,32 @@ def test_staged_plain_stores_cfg5_shard():
     peer.check()
     assert torch.equal(y0, y1)
     assert FX.check_against_golden(y1, FX.case_expected("cfg5_m1024")[0], 2e-2) <= 2e-2
+
+
+F32_CASES = ["block_tail__f32", "bmm_broadcast__f32", "cuda_mlp__f32", "gemm_tc_aligned__f32",
+             "gemm_tc_batched_tb__f32", "gemm_tc_nn_batched__f32", "linear_tb__f32", "matmul_epi_64x64x64__f32",
+             "transformer_block__f32", "cfg1"]
+
+
+@pytest.mark.parametrize("case", F32_CASES)
+def test_last_tile_staged_f32_stores_are_bit_identical(case, monkeypatch):
+    """f32 outputs and split-K partial sums of a CTA's last tile go through the idle pipeline
+    memory and out as whole row segments; the values are the same, so the outputs must be the
+    same bits as with the per-row stores (``TENSORJIT_B200_STAGE_LAST=0``)."""
+    from mlir_gpu_kernel_compiler_b200 import B200Program
+    from mlir_gpu_kernel_compiler_b200 import workloads as W
+
+    if case == "cfg1":
+        plan, ins = FX.load_plan("cfg1"), [t.cuda() for t in W.make_inputs(W.WORKLOADS["cfg1"])]
+    else:
+        plan, ins = FX.load_plan(case), [t.cuda() for t in FX.case_inputs(case)]
+    outs = {}
+    for flag in ("0", "1"):
+        monkeypatch.setenv("TENSORJIT_B200_STAGE_LAST", flag)
+        prog = B200Program(plan, device="cuda")
+        assert any(k.info.get("stage_last") for k in prog.kernel_sources) == (flag == "1")
+        outs[flag] = prog(*ins)
+        torch.cuda.synchronize()
+        prog.check()
+    for a, b in zip(outs["0"], outs["1"]):
+        assert torch.equal(a, b), case
