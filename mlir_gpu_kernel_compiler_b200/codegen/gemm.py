@@ -827,11 +827,13 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     # outputs that may be a peer GPU's memory: staged in shared memory like the TMA-store path,
     # then written with plain coalesced 16-byte stores (whole row segments per instruction)
     staged = not tma_store and not tma_store_allowed() and epi.staged_store_ok() and not x3 and ksplit == 1
-    # f32 outputs and split-K partial sums: the CTA's last tile staged in the idle pipeline memory
-    # (single-CTA kernel; not for outputs that may be a peer GPU's memory)
-    stage_last = (not tma_store and not staged and not pair and tma_store_allowed()
-                  and os.environ.get("TENSORJIT_B200_STAGE_LAST") != "0"
-                  and (N % 4 == 0 if ksplit > 1 else epi.stage_last_ok()))
+    # split-K partial sums: the CTA's last tile staged in the idle pipeline memory and written as
+    # whole row segments (single-CTA kernel).  TENSORJIT_B200_STAGE_LAST=all also stages f32
+    # outputs with an epilogue; measured slower there (cfg1's GELU GEMM: 25.4 -> 29.1 us), the
+    # partial sums faster (cfg1's second GEMM: 20.5 -> 18.5 us).
+    mode = os.environ.get("TENSORJIT_B200_STAGE_LAST", "1")
+    stage_last = (not tma_store and not staged and not pair and tma_store_allowed() and mode != "0"
+                  and (N % 4 == 0 if ksplit > 1 else (mode == "all" and epi.stage_last_ok())))
     L = [HEADER, '#include "gemm_sm100_pair.cuh"' if pair else '#include "gemm_sm100.cuh"',
          params_struct(nptr, 4 if x3 else (3 if tma_store else 2))]
     L.append("struct Cfg {")

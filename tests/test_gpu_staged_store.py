@@ -82,7 +82,8 @@ F32_CASES = ["block_tail__f32", "bmm_broadcast__f32", "cuda_mlp__f32", "gemm_tc_
 def test_last_tile_staged_f32_stores_are_bit_identical(case, monkeypatch):
     """f32 outputs and split-K partial sums of a CTA's last tile go through the idle pipeline
     memory and out as whole row segments; the values are the same, so the outputs must be the
-    same bits as with the per-row stores (``TENSORJIT_B200_STAGE_LAST=0``)."""
+    same bits as with the per-row stores (``TENSORJIT_B200_STAGE_LAST=0``).  By default only the
+    partial sums are staged; ``all`` stages the f32 outputs with an epilogue as well."""
     from mlir_gpu_kernel_compiler_b200 import B200Program
     from mlir_gpu_kernel_compiler_b200 import workloads as W
 
@@ -91,12 +92,16 @@ def test_last_tile_staged_f32_stores_are_bit_identical(case, monkeypatch):
     else:
         plan, ins = FX.load_plan(case), [t.cuda() for t in FX.case_inputs(case)]
     outs = {}
-    for flag in ("0", "1"):
+    for flag in ("0", "1", "all"):
         monkeypatch.setenv("TENSORJIT_B200_STAGE_LAST", flag)
         prog = B200Program(plan, device="cuda")
-        assert any(k.info.get("stage_last") for k in prog.kernel_sources) == (flag == "1")
+        staged = [k for k in prog.kernel_sources if k.info.get("stage_last")]
+        assert (not staged) if flag == "0" else all(k.info["ksplit"] > 1 or flag == "all" for k in staged)
+        if flag == "all":
+            assert staged
         outs[flag] = prog(*ins)
         torch.cuda.synchronize()
         prog.check()
-    for a, b in zip(outs["0"], outs["1"]):
-        assert torch.equal(a, b), case
+    for flag in ("1", "all"):
+        for a, b in zip(outs["0"], outs[flag]):
+            assert torch.equal(a, b), (case, flag)
