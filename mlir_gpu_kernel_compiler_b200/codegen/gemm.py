@@ -459,6 +459,30 @@ def gen_ksplit_finalize(k: PKernel, symbol: str, args: list, ksplit: int, kernel
          f'extern "C" __global__ void __launch_bounds__(256) {symbol}(const __grid_constant__ Params prm) {{', PDL]
     L += ["  " + x for x in epi._ptr_lines()]
     L.append("  " + ptr_decl("part", "float", part_idx, ksplit * total, True, kernel_id))
+    if epi.vec_ok():
+        # 8 consecutive columns per thread: two 16-byte loads per K slice, the GEMM's 8-wide epilogue
+        groups = total // 8
+        L.append(f"  for (long g = (long)blockIdx.x * 256 + threadIdx.x; g < {groups}L; g += (long)gridDim.x * 256) {{")
+        L.append(f"    const long row = g / {N // 8}L, j = (g - row * {N // 8}L) * 8, i = row % {M}L, b = row / {M}L;")
+        L.append("    float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};")
+        L.append("    #pragma unroll")
+        L.append(f"    for (int s = 0; s < {ksplit}; ++s) {{")
+        L.append("      float p8[8];")
+        L.append(f"      tj_load_vec(part + (s * {total}L + row * {N}L + j), p8);")
+        L.append(f"      tj_load_vec(part + (s * {total}L + row * {N}L + j) + 4, p8 + 4);")
+        L.append("      #pragma unroll")
+        L.append("      for (int u = 0; u < 8; ++u) s8[u] += p8[u];")
+        L.append("    }")
+        bl, bidx = epi.batch_index_lines("b")
+        L += ["    " + x for x in bl]
+        L += ["    " + x for x in epi.vec8_lines(bidx, "s8[u]")]
+        L.append("  }")
+        L.append("}")
+        grid = max(1, min((groups + 255) // 256, NUM_SMS * 8))
+        ks = KernelSource(symbol, "ewise", "\n".join(L), (grid, 1, 1), (256, 1, 1), list(args),
+                          info={"bytes": total * 4 * (ksplit + 1), "numel": total, "ksplit": ksplit, "vec": 8})
+        ks.finalize_params()
+        return ks
     L.append(f"  for (long e = (long)blockIdx.x * 256 + threadIdx.x; e < {total}L; e += (long)gridDim.x * 256) {{")
     L.append(f"    const long j = e % {N}L, row = e / {N}L, i = row % {M}L, b = row / {M}L;")
     L.append("    float acc = 0.0f;")
@@ -546,40 +570,7 @@ class Epilogue:
             L.append("    for (int c = 0; c < 32; c += 8) {")
             L.append("      const long j = j0 + c;")
             L.append(f"      if (j >= {self.N}L) break;")
-            val = {}
-            for n in self.epi_inputs:
-                st = self.strides[n.id]
-                idx = self.in_index[n.id]
-                off = self.offset(n, bidx, "i", "j")
-                if st[-1] == 1:
-                    if n.dtype == "f32":   # 8 f32 = two 16-byte loads
-                        L.append(f"      float x{n.id}[8]; tj_load_vec(in{idx} + ({off}), x{n.id}); "
-                                 f"tj_load_vec(in{idx} + ({off}) + 4, x{n.id} + 4);")
-                    else:
-                        L.append(f"      float x{n.id}[8]; tj_load_vec(in{idx} + ({off}), x{n.id});")
-                    val[n.id] = f"x{n.id}[u]"
-                else:
-                    L.append(f"      const float x{n.id} = tj_f32(in{idx}[{off}]);")
-                    val[n.id] = f"x{n.id}"
-            outs = self.k.outputs
-            for j, o in enumerate(outs):
-                L.append(f"      float o{j}[8];")
-            L.append("      #pragma unroll")
-            L.append("      for (int u = 0; u < 8; ++u) {")
-            comp, m = self.compute_lines("acc[c + u]", val)
-            L += ["        " + s for s in comp]
-            for j, o in enumerate(outs):
-                L.append(f"        o{j}[u] = {m[o.id]};")
-            L.append("      }")
-            off = self.out_offset(bidx, "i", "j")
-            for j, o in enumerate(outs):
-                oi = self.out_index[o.id]
-                if o.id in self.fwd:
-                    L += ["      " + x for x in split_store_lines(f"out{oi}", off, f"o{j}", 8, self.fwd[o.id])]
-                elif o.dtype == "f32":
-                    L.append(f"      tj_store_vec(out{oi} + ({off}), o{j}); tj_store_vec(out{oi} + ({off}) + 4, o{j} + 4);")
-                else:
-                    L.append(f"      tj_store_vec(out{oi} + ({off}), o{j});")
+            L += ["      " + x for x in self.vec8_lines(bidx, "acc[c + u]")]
             L.append("    }")
         else:
             L.append("    #pragma unroll 4")
@@ -590,6 +581,45 @@ class Epilogue:
             L.append("    }")
         L.append("  }")
         return "\n".join(L)
+
+    def vec8_lines(self, bidx: list[str], acc: str) -> list[str]:
+        """Epilogue of the 8 columns j..j+7 of row i (vector path): load the operands, evaluate
+        the DAG on the accumulator values ``acc`` (an expression of ``u``), store the outputs."""
+        L, val = [], {}
+        for n in self.epi_inputs:
+            st = self.strides[n.id]
+            idx = self.in_index[n.id]
+            off = self.offset(n, bidx, "i", "j")
+            if st[-1] == 1:
+                if n.dtype == "f32":   # 8 f32 = two 16-byte loads
+                    L.append(f"float x{n.id}[8]; tj_load_vec(in{idx} + ({off}), x{n.id}); "
+                             f"tj_load_vec(in{idx} + ({off}) + 4, x{n.id} + 4);")
+                else:
+                    L.append(f"float x{n.id}[8]; tj_load_vec(in{idx} + ({off}), x{n.id});")
+                val[n.id] = f"x{n.id}[u]"
+            else:
+                L.append(f"const float x{n.id} = tj_f32(in{idx}[{off}]);")
+                val[n.id] = f"x{n.id}"
+        outs = self.k.outputs
+        for j, o in enumerate(outs):
+            L.append(f"float o{j}[8];")
+        L.append("#pragma unroll")
+        L.append("for (int u = 0; u < 8; ++u) {")
+        comp, m = self.compute_lines(acc, val)
+        L += ["  " + s for s in comp]
+        for j, o in enumerate(outs):
+            L.append(f"  o{j}[u] = {m[o.id]};")
+        L.append("}")
+        off = self.out_offset(bidx, "i", "j")
+        for j, o in enumerate(outs):
+            oi = self.out_index[o.id]
+            if o.id in self.fwd:
+                L += split_store_lines(f"out{oi}", off, f"o{j}", 8, self.fwd[o.id])
+            elif o.dtype == "f32":
+                L.append(f"tj_store_vec(out{oi} + ({off}), o{j}); tj_store_vec(out{oi} + ({off}) + 4, o{j} + 4);")
+            else:
+                L.append(f"tj_store_vec(out{oi} + ({off}), o{j});")
+        return L
 
     def tma_store_ok(self) -> bool:
         """One half-precision output written by 32 x 32 TMA stores: needs a 16-byte row
