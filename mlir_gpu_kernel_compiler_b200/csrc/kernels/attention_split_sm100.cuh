@@ -105,7 +105,6 @@ __device__ __forceinline__ void attention_split_sm100(const P& prm, typename Cfg
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  tj_pdl_launch_dependents();
   tj_pdl_wait();  // the previous kernel of the program is complete and its writes are visible
 
   bool q_pending = false;
@@ -352,6 +351,10 @@ __device__ __forceinline__ void attention_split_sm100(const P& prm, typename Cfg
       mbar_wait(smem_u32(&v_full[s]), ph, &no_abort, status, kernel_id * 16 + 10, 200000000ull);
     }
   }
+  // the next kernel of the program may launch once every CTA is here (it still waits for this
+  // grid's completion before touching memory); triggered at the end, not at the start, so a
+  // persistent kernel does not hold a launched dependent for its whole run
+  tj_pdl_launch_dependents();
   if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
 }
 

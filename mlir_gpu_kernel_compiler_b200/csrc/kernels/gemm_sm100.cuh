@@ -363,7 +363,6 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  tj_pdl_launch_dependents();
   tj_pdl_wait();  // the previous kernel of the program is complete and its writes are visible
 
   // stages the producer filled (and the phase it filled them in): on an abort, the
@@ -629,6 +628,10 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
         mbar_wait(smem_u32(&full[s]), issued_phase[s], &no_abort, status, kernel_id * 16 + 5, 200000000ull);
       }
   }
+  // the next kernel of the program may launch once every CTA is here (it still waits for this
+  // grid's completion before touching memory); triggered at the end, not at the start, so a
+  // persistent kernel does not hold a launched dependent for its whole run
+  tj_pdl_launch_dependents();
   if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
 }
 

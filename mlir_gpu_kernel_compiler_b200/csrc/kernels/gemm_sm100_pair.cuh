@@ -193,7 +193,6 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
   cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any remote access
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  tj_pdl_launch_dependents();
   tj_pdl_wait();  // the previous kernel of the program is complete and its writes are visible
 
   if (warp == 0) {
@@ -393,6 +392,10 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
     while (tj_globaltimer() - t0 < 2000000ull) __nanosleep(1000);
   }
   __syncthreads();
+  // the next kernel of the program may launch once every CTA is here (it still waits for this
+  // grid's completion before touching memory); triggered at the end, not at the start, so a
+  // persistent kernel does not hold a launched dependent for its whole run
+  tj_pdl_launch_dependents();
   if (warp == 1) tmem_dealloc_pair(tmem_base, TMEM_COLS);
 }
 
