@@ -140,6 +140,14 @@ TJ_API int tj_b200_time_kernels(void* program, const void* const* inputs, void* 
  * that ran out, or a checked-build bounds violation); the words are cleared. */
 TJ_API int tj_b200_check_status(void* program, int32_t* code, int32_t* where);
 
+/* Programmatic dependent launch between the program's kernels (enable != 0; the default unless
+ * the environment sets TENSORJIT_B200_PDL=0): each kernel after the first may be scheduled while
+ * the previous one finishes and waits (griddepcontrol.wait) before touching memory.  Saves launch
+ * gaps in latency-bound programs; measured to cost clock under the power cap in programs of long
+ * persistent GEMMs, so the Python front end enables it per program.  No counterpart in the
+ * reference (its driver launches kernels in plain stream order, `cuda_driver.py:115-124`). */
+TJ_API int tj_b200_set_pdl(void* program, int32_t enable);
+
 TJ_API int tj_b200_program_info(void* program, tj_program_info* info);
 
 TJ_API int tj_b200_destroy(void* program);

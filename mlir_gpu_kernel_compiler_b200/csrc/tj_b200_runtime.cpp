@@ -607,6 +607,23 @@ int tj_b200_set_graph(void* program, int32_t enable) {
   return TJ_OK;
 }
 
+int tj_b200_set_pdl(void* program, int32_t enable) {
+  if (!program) return fail(TJ_ERR_INVALID, "program is NULL");
+  Program& p = *static_cast<Program*>(program);
+  std::lock_guard<std::mutex> lock(p.mu);
+  const bool on = enable != 0;
+  if (on == p.pdl) return TJ_OK;
+  p.pdl = on;
+  if (p.exec || p.graph) {  // rebuilt with (or without) programmatic edges at the next run
+    CtxGuard guard(p.ctx);
+    if (p.exec) drv().cuGraphExecDestroy(p.exec);
+    if (p.graph) drv().cuGraphDestroy(p.graph);
+    p.exec = nullptr;
+    p.graph = nullptr;
+  }
+  return TJ_OK;
+}
+
 int tj_b200_check_status(void* program, int32_t* code, int32_t* where) {
   if (!program) return fail(TJ_ERR_INVALID, "program is NULL");
   Program& p = *static_cast<Program*>(program);

@@ -79,12 +79,17 @@ def _trace(*a):
         print("[b200]", *a, file=sys.stderr, flush=True)
 
 
+# programs estimated to run longer than this (ms) launch their kernels without programmatic
+# dependent launch
+PDL_MAX_MS = 2.0
+
+
 class B200Program:
     backend = "b200"
 
     def __init__(self, program, device: str | torch.device = "cuda", use_graph: Optional[bool] = None,
                  tune: bool = True, tiles: dict | None = None, nvcc_flags: tuple = (), fuse_kernels: bool = True,
-                 checked: Optional[bool] = None, peer_outputs: bool = False):
+                 checked: Optional[bool] = None, peer_outputs: bool = False, pdl: Optional[bool] = None):
         self.program = program
         self.pplan: PProgram = as_plan(program)
         self.device = torch.device(device)
@@ -113,6 +118,12 @@ class B200Program:
         self.cubins = compile_cubins([(ks.symbol, ks.source) for ks in self.kernel_sources], flags)
         _trace("compiled")
         self.use_graph = (os.environ.get("TENSORJIT_B200_GRAPH", "1") == "1") if use_graph is None else use_graph
+        # programmatic dependent launch: TENSORJIT_B200_PDL=0/1 forces it; by default only programs
+        # whose estimated run time is short (launch gaps matter) use it.  In a program of long
+        # persistent GEMMs it saved nothing and cost clock under the power cap (cfg5: ~4 %).
+        env_pdl = os.environ.get("TENSORJIT_B200_PDL")
+        self.pdl = (env_pdl != "0") if env_pdl in ("0", "1") else (
+            bool(pdl) if pdl is not None else self.estimated_ms() < PDL_MAX_MS)
         g = self.xplan
         self._in_index = {n.id: i for i, n in enumerate(g.inputs)}
         escaping = {g.resolve(o).id for o in g.outputs}
@@ -167,6 +178,14 @@ class B200Program:
                              "num_tmaps": len(ks.tmaps)})
         return launches, args, tmaps
 
+    def estimated_ms(self) -> float:
+        """Roofline estimate of one run: every launch's algorithmic FLOPs at the dense bf16 rate
+        plus its bytes at the HBM rate (nominal B200 figures)."""
+        t = 0.0
+        for ks in self.kernel_sources:
+            t += ks.info.get("flops", 0.0) / 2.25e15 + ks.info.get("bytes", 0.0) / 7.7e12
+        return t * 1e3
+
     @property
     def launches(self) -> list[dict]:
         return self._launches
@@ -195,6 +214,7 @@ class B200Program:
             self._native = rt.NativeProgram(self.cubins, self._launches, self._args, self._tmaps,
                                             self.arena_bytes, len(self.pplan.inputs), len(self._out_nodes), idx)
             self._native.set_graph(self.use_graph)
+            self._native.set_pdl(self.pdl)
         return self._native
 
     @property

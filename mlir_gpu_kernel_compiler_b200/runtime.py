@@ -25,6 +25,7 @@ EXPORTS = (
     "tj_b200_program_info", "tj_b200_destroy", "tj_b200_last_error", "tj_b200_abi_version",
     "tj_b200_driver_available", "tj_b200_time_kernels", "tj_b200_linear_f32_noalloc",
     "tj_b200_linear_f32_noalloc_status", "tj_b200_ipc_export", "tj_b200_ipc_open", "tj_b200_ipc_close",
+    "tj_b200_set_pdl",
 )
 
 
@@ -106,6 +107,8 @@ def library(path: str | Path | None = None) -> ctypes.CDLL:
         lib.tj_b200_ipc_open.restype = ctypes.c_int
         lib.tj_b200_ipc_close.argtypes = [vp, u64, i32]
         lib.tj_b200_ipc_close.restype = ctypes.c_int
+        lib.tj_b200_set_pdl.argtypes = [vp, i32]
+        lib.tj_b200_set_pdl.restype = ctypes.c_int
         lib.tj_b200_set_graph.argtypes = [vp, i32]
         lib.tj_b200_set_graph.restype = ctypes.c_int
         lib.tj_b200_check_status.argtypes = [vp, ctypes.POINTER(i32), ctypes.POINTER(i32)]
@@ -204,6 +207,9 @@ class NativeProgram:
         self.num_inputs, self.num_outputs = num_inputs, num_outputs
         self._in = (ctypes.c_void_p * max(num_inputs, 1))()
         self._out = (ctypes.c_void_p * max(num_outputs, 1))()
+
+    def set_pdl(self, enable: bool) -> None:
+        check(self._lib.tj_b200_set_pdl(self.handle, 1 if enable else 0), "tj_b200_set_pdl")
 
     def set_graph(self, enable: bool) -> None:
         check(self._lib.tj_b200_set_graph(self.handle, 1 if enable else 0), "tj_b200_set_graph")

@@ -89,6 +89,25 @@ def test_graph_rebinds_caller_buffers_without_copies():
     assert st["graph_replays"] == 4 and st["graph_node_updates"] >= 3
 
 
+def test_pdl_switch_rebuilds_the_graph_with_the_same_results():
+    """Turning programmatic dependent launch off and on again (tj_b200_set_pdl) re-instantiates
+    the whole-program graph with or without programmatic edges; results are the same bits."""
+    case = "transformer_block__bf16"
+    from mlir_gpu_kernel_compiler_b200 import B200Program
+
+    plan = FX.load_plan(case)
+    ins = [t.cuda() for t in FX.case_inputs(case)]
+    prog = B200Program(plan, use_graph=True, pdl=True)
+    ys = [prog(*ins)[0].clone()]
+    for on in (False, True):
+        prog.native.set_pdl(on)
+        ys.append(prog(*ins)[0].clone())
+    torch.cuda.synchronize()
+    prog.check()
+    assert all(torch.equal(ys[0], y) for y in ys[1:])
+    assert prog.native.info()["graph_instantiations"] == 3
+
+
 def test_output_buffers_reused_only_when_dropped():
     """tests/test_backends.py:190-206 semantics for caller-visible outputs."""
     case = "unary_gelu__f32"

@@ -572,3 +572,21 @@ def test_3xtf32_operand_forwarding(monkeypatch):
     plan.outputs.append(xln)
     fwd2, skip2 = _split_forwarding(plan, first)
     assert xln.id not in fwd2 and 1 not in skip2
+
+
+def test_pdl_chosen_per_program(monkeypatch):
+    """Programmatic dependent launch: on for latency-bound programs (short estimated run time),
+    off for programs of long persistent GEMMs, where it cost clock under the power cap;
+    TENSORJIT_B200_PDL forces either way, and the constructor argument overrides the estimate."""
+    from mlir_gpu_kernel_compiler_b200 import B200Program
+
+    monkeypatch.delenv("TENSORJIT_B200_PDL", raising=False)
+    assert B200Program(FX.load_plan("cfg4"), device="cuda").pdl
+    assert B200Program(FX.load_plan("cfg1"), device="cuda").pdl
+    big = B200Program(FX.load_plan("cfg5_m131072"), device="cuda")
+    assert not big.pdl and big.estimated_ms() > 10
+    assert B200Program(FX.load_plan("cfg5_m131072"), device="cuda", pdl=True).pdl
+    monkeypatch.setenv("TENSORJIT_B200_PDL", "1")
+    assert B200Program(FX.load_plan("cfg5_m131072"), device="cuda").pdl
+    monkeypatch.setenv("TENSORJIT_B200_PDL", "0")
+    assert not B200Program(FX.load_plan("cfg4"), device="cuda").pdl
