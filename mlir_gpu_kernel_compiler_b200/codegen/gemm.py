@@ -515,7 +515,8 @@ class Epilogue:
         self.mm, self.M, self.N, self.out_shape = mm, M, N, out_shape
         self.batch_shape = out_shape[:-2]
         self.epi_nodes = [n for n in k.nodes if n is not mm]
-        self.epi_inputs = [n for n in k.inputs if n is not a and n is not b]
+        a_src = (k.attrs.get("a_strided") or {}).get("src")     # A read from a transpose's source
+        self.epi_inputs = [n for n in k.inputs if n is not a and n is not b and n is not a_src]
         self.in_index, self.out_index = in_index, out_index
         self.strides = {}
         for n in self.epi_inputs:
@@ -819,6 +820,35 @@ def choose_tile(M: int, N: int, batch: int, b_mn_major: bool, override: dict | N
     return BN, STAGES, 16
 
 
+def _a_map_order(sa: dict) -> tuple[list[str], list[int]]:
+    """Roles of the folded-transpose A dims (K0 [K1] M0 [M1] [B], as ``strided_a_layout`` lists
+    them) and the order of those dims in the tensor map: sorted by stride, as the attention
+    kernel's maps are, so the map's strides never decrease.  Only K0 (unit stride, always first)
+    and M0 have box extents above 1, so the tile lands in shared memory as 128 rows of 64."""
+    roles = (["k0", "k1"][: sa["k_dims"]] + ["m0", "m1"][: sa["m_dims"]] + ["b"] * sa["batch_dims"])
+    order = sorted(range(len(roles)), key=lambda i: sa["dims"][i][1])
+    return roles, order
+
+
+def _a_coords_function(sa: dict) -> list[str]:
+    """``a_coords(ab, m0, k0, c)``: tensor-map coordinates of the A tile at row m0, column k0 of
+    A matrix ab when A is read from a folded transpose's source."""
+    dims = sa["dims"]
+    roles, order = _a_map_order(sa)
+    k0_size = dims[roles.index("k0")][0]
+    m0_size = dims[roles.index("m0")][0]
+    value = {"k0": f"k0 % {k0_size}" if "k1" in roles else "k0", "k1": f"k0 / {k0_size}",
+             "m0": f"m0 % {m0_size}" if "m1" in roles else "m0", "m1": f"m0 / {m0_size}",
+             "b": "static_cast<int>(ab)"}
+    L = ["  static __device__ __forceinline__ void a_coords(long ab, int m0, int k0, int (&c)[5]) {"]
+    if "b" not in roles:
+        L.append("    (void)ab;")
+    for pos, i in enumerate(order):
+        L.append(f"    c[{pos}] = {value[roles[i]]};")
+    L.append("  }")
+    return L
+
+
 def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = None,
                 x3_scratch: tuple | None = None, ksplit: int = 1, partial_scratch: int = 0,
                 packed: dict | None = None) -> KernelSource:
@@ -847,7 +877,9 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     BN, STAGES, GROUP_M = choose_tile(M, N, batch, b_mn, tile)
     if x3:
         STAGES = min(STAGES, max(2, (200 * 1024) // (2 * (128 * 128 + BN * 128))))
-    pair = bool(tile and tile.get("PAIR")) and not b_mn and BN in (128, 256) and not x3
+    sa = k.attrs.get("a_strided")       # A read from a folded transpose's source (fuse.py)
+    assert sa is None or not (x3 or pk_a), "a folded transpose needs the plain 16-bit A path"
+    pair = bool(tile and tile.get("PAIR")) and not b_mn and BN in (128, 256) and not x3 and not sa
     a_bs = _batch_strides(a, batch_shape)
     b_bs = _batch_strides(b, batch_shape)
     a_mats = prod(a.shape[:-2])
@@ -880,6 +912,9 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     L.append(f"  static constexpr bool TMA_STORE = {'true' if tma_store else 'false'};")
     L.append(f"  static constexpr bool STAGED_STORE = {'true' if staged else 'false'};")
     L.append(f"  static constexpr bool STAGE_LAST = {'true' if stage_last else 'false'};")
+    L.append(f"  static constexpr int A_RANK = {len(sa['dims']) if sa else 2};")
+    if sa:
+        L += _a_coords_function(sa)
     L.append(f"  using OutT = {CTYPE[outs[0].dtype] if (tma_store or staged) else 'float'};")
     L.append(f"  static constexpr long BATCH = {batch}L, A_MATS = {a_mats}L, B_MATS = {b_mats}L;")
     L.append(f"  static constexpr bool BF16 = {'true' if a.dtype == 'bf16' else 'false'}, B_MN_MAJOR = {'true' if b_mn else 'false'};")
@@ -922,9 +957,16 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     a_pitch = pitch if (x3 or pk_a) else K
     b_pitch = pitch if (x3 or pk_b) else K
     pk_arg = status_idx + 1
-    a_arg = status_idx + 1 if x3 else (pk_arg if pk_a else in_index[a.id])
+    a_arg = status_idx + 1 if x3 else (pk_arg if pk_a else in_index[(sa["src"] if sa else a).id])
     b_arg = status_idx + 2 if x3 else (pk_arg + int(pk_a) if pk_b else in_index[b.id])
-    tmA = TMapSpec(arg=a_arg, dtype=op_dt, dims=[K, a_mats * M], strides=[a_pitch * esz], box=[bk, 128], swizzle=3)
+    if sa:
+        roles, order = _a_map_order(sa)
+        box = [bk if roles[i] == "k0" else (128 if roles[i] == "m0" else 1) for i in order]
+        tmA = TMapSpec(arg=a_arg, dtype=op_dt, dims=[sa["dims"][i][0] for i in order],
+                       strides=[sa["dims"][i][1] * esz for i in order[1:]], box=box, swizzle=3)
+    else:
+        tmA = TMapSpec(arg=a_arg, dtype=op_dt, dims=[K, a_mats * M], strides=[a_pitch * esz], box=[bk, 128],
+                       swizzle=3)
     if not b_mn:
         tmB = TMapSpec(arg=b_arg, dtype=op_dt, dims=[K, b_mats * N], strides=[b_pitch * esz],
                        box=[bk, BN // 2 if pair else BN], swizzle=3)
@@ -956,6 +998,7 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
                       tmaps=tmaps, cluster=(2, 1, 1) if pair else (1, 1, 1),
                       info={"M": M, "N": N, "K": K, "batch": batch, "BN": BN, "stages": STAGES,
                             "tma_store": tma_store, "staged_store": staged, "stage_last": stage_last,
+                            "a_strided": bool(sa),
                             "epi_warps": epi_warps, "pair": pair,
                             "tf32x3": x3,
                             "ksplit": ksplit, "packed": [x for x, f in (("a", pk_a), ("b", pk_b)) if f],
@@ -996,6 +1039,7 @@ def gen_gemm_multi(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = 
     L.append(f"  static constexpr int GROUP_N = {int((tile or {}).get('GROUP_N', 0))};")
     L.append(f"  static constexpr int EPI_WARPS = 8, KSPLIT = 1, NSEG = {len(parts)};")
     L.append("  static constexpr bool TF32X3 = false, TMA_STORE = false, STAGED_STORE = false, STAGE_LAST = false;")
+    L.append("  static constexpr int A_RANK = 2;")
     L.append("  using OutT = float;")
     L.append("  static constexpr long BATCH = 1L, A_MATS = 1L, B_MATS = 1L;")
     L.append(f"  static constexpr bool BF16 = {'true' if dt == 'bf16' else 'false'}, B_MN_MAJOR = false;")

@@ -42,30 +42,6 @@
 namespace tja {
 using namespace tjg;
 
-TJ_DEV void tma_load_4d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int c1, int c2, int c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(
-          dst),
-      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-      : "memory");
-}
-TJ_DEV void tma_load_5d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int c1, int c2, int c3, int c4) {
-  asm volatile(
-      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], "
-      "[%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
-      : "memory");
-}
-// Tiled load of a rank-R tensor map at coordinates c[0..R-1].
-template <int R>
-TJ_DEV void tma_load_nd(uint32_t dst, const CUtensorMap* m, uint32_t bar, const int (&c)[5]) {
-  static_assert(R >= 2 && R <= 5, "tensor map rank");
-  if constexpr (R == 2) tma_load_2d(dst, m, bar, c[0], c[1]);
-  if constexpr (R == 3) tma_load_3d(dst, m, bar, c[0], c[1], c[2]);
-  if constexpr (R == 4) tma_load_4d(dst, m, bar, c[0], c[1], c[2], c[3]);
-  if constexpr (R == 5) tma_load_5d(dst, m, bar, c[0], c[1], c[2], c[3], c[4]);
-}
-
 // 2^x on the MUFU unit (PTX ex2.approx.ftz.f32; 2^-inf = 0).
 TJ_DEV float ex2_approx(float x) {
   float y;

@@ -235,6 +235,30 @@ TJ_DEV void tile_coords(long t, int m_tiles, int n_tiles, int group_m, int group
   nt = n_first + in_g / gsize;
 }
 
+TJ_DEV void tma_load_4d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+TJ_DEV void tma_load_5d(uint32_t dst, const CUtensorMap* m, uint32_t bar, int c0, int c1, int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], "
+      "[%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+// Tiled load of a rank-R tensor map at coordinates c[0..R-1].
+template <int R>
+TJ_DEV void tma_load_nd(uint32_t dst, const CUtensorMap* m, uint32_t bar, const int (&c)[5]) {
+  static_assert(R >= 2 && R <= 5, "tensor map rank");
+  if constexpr (R == 2) tma_load_2d(dst, m, bar, c[0], c[1]);
+  if constexpr (R == 3) tma_load_3d(dst, m, bar, c[0], c[1], c[2]);
+  if constexpr (R == 4) tma_load_4d(dst, m, bar, c[0], c[1], c[2], c[3]);
+  if constexpr (R == 5) tma_load_5d(dst, m, bar, c[0], c[1], c[2], c[3], c[4]);
+}
+
 // Plain coalesced stores of one epilogue warp's staged block: 32 rows x (32 * nch) columns of
 // 16-bit outputs, chunk c of the block in stage buffer c (32 rows x 64 bytes each, 16-byte
 // pieces swizzled as the TMA-store path writes them: piece ^= (row >> 1) & 3).  With two chunks
@@ -269,6 +293,8 @@ TJ_DEV void staged_store_rows(const P& prm, const uint8_t* stage, uint32_t out_s
 //   static constexpr int BN, STAGES, M, N, K, GROUP_M, GROUP_N, EPI_WARPS, KSPLIT, NSEG; static constexpr long BATCH;
 //   (NSEG > 1: static __device__ int segment(int nt), seg_tile0(int g) map a column tile to its B operand)
 //   static constexpr bool BF16, B_MN_MAJOR, TMA_STORE, STAGED_STORE, STAGE_LAST;  using OutT = <output type>;
+//   static constexpr int A_RANK (2: A through a 2-D map [K, mats * M]; 3..5: A read from a
+//   transpose's source, with static __device__ void a_coords(long ab, int m0, int k0, int (&c)[5]));
 //   static __device__ void batch_map(long b, long& a_batch, long& b_batch);
 //   template <class P> static __device__ void epilogue(const P& prm, long b, long i, long j0, const float (&acc)[32]);
 //     (direct 16-byte stores), or with TMA_STORE:
@@ -292,6 +318,7 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
   constexpr uint32_t B_BYTES = BN * 128;
   constexpr uint32_t STAGE_BYTES = OPC * (A_BYTES + B_BYTES);
   static_assert(!X3 || (!Cfg::B_MN_MAJOR && !Cfg::TMA_STORE), "3xTF32 mode: K-major B, direct stores");
+  static_assert(!X3 || Cfg::A_RANK == 2, "3xTF32 mode reads its A copies through a 2-D map");
   constexpr int m_tiles = (Cfg::M + BM - 1) / BM;
   constexpr int n_tiles = (Cfg::N + BN - 1) / BN;
   constexpr int k_blocks = (Cfg::K + BK - 1) / BK;
@@ -432,7 +459,14 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
           mbar_expect_tx(fb, STAGE_BYTES);
           uint8_t* a_st = sA + stage * OPC * A_BYTES;
           uint8_t* b_st = sB + stage * OPC * B_BYTES;
-          tma_load_2d(smem_u32(a_st), tmA, fb, kb * BK, a_row);
+          if constexpr (Cfg::A_RANK > 2) {
+            // A read in place from a transpose's source: rank-3..5 map, coordinates from the Cfg
+            int ac[5] = {0, 0, 0, 0, 0};
+            Cfg::a_coords(ab, mt * BM, kb * BK, ac);
+            tma_load_nd<Cfg::A_RANK>(smem_u32(a_st), tmA, fb, ac);
+          } else {
+            tma_load_2d(smem_u32(a_st), tmA, fb, kb * BK, a_row);
+          }
           if constexpr (!Cfg::B_MN_MAJOR) {
             tma_load_2d(smem_u32(b_st), tb, fb, kb * BK, static_cast<int>(bb * Cfg::N + n0));
           } else {

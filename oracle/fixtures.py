@@ -161,3 +161,23 @@ def allowed_error(case: str, out_index: int, tol: float) -> float:
     """The bound an output of ``case`` must meet against the f32 reference."""
     ent = BF16_STORAGE_EXCEPTIONS.get((case, out_index))
     return ent[1] if ent else tol
+
+
+def merge_heads_plan(batch: int, heads: int, seq: int, dh: int, n: int, dtype: str = "bf16"):
+    """The reference's plan of linear(reshape(permute(x, 0, 2, 1, 3), (batch*seq, heads*dh)), w, b)
+    (fixture merge_heads_linear) with other sizes: a transpose copy kernel, then the GEMM."""
+    from mlir_gpu_kernel_compiler_b200.plan import PProgram
+
+    d = load_plan("merge_heads_linear__bf16").to_dict()
+    shapes = {0: [batch, heads, seq, dh], 1: [n, heads * dh], 2: [n], 3: [batch, seq, heads, dh],
+              4: [batch * seq, heads * dh], 5: [batch * seq, n], 6: [batch * seq, n]}
+    for nd in d["nodes"]:
+        nd["shape"] = shapes[nd["id"]]
+        nd["dtype"] = dtype
+        if nd["op"] == "reshape":
+            nd["attrs"]["shape"] = shapes[4]
+    d["kernels"][0]["iter_shape"] = shapes[3]
+    d["kernels"][1]["iter_shape"] = shapes[5]
+    d["aliases"] = {"4": [3, shapes[4]]}
+    d["meta"] = dict(d.get("meta", {}), dtype=dtype)
+    return PProgram.from_dict(d)

@@ -151,6 +151,14 @@ def cases(tj):
 
     add("attention_heads", mha, [(512, 128), (256, 128), (256, 128), (256, 128), (128, 256)], dtypes=(BF16,))
 
+    # a transpose kernel feeding a plain GEMM's A operand (folded into the GEMM's operand
+    # addressing): the head merge before an output projection, and a batch-dim transpose
+    # before a batched matmul with an N-major B
+    add("merge_heads_linear", lambda x, w, b: tj.linear(tj.reshape(tj.permute(x, 0, 2, 1, 3), (512, 256)), w, b),
+        [(2, 4, 256, 64), (128, 256), (128,)], dtypes=(BF16, F16, F32))
+    add("transpose_bmm", lambda x, w: tj.gelu(tj.matmul(tj.permute(x, 1, 0, 2), w)),
+        [(256, 4, 128), (4, 128, 192)], dtypes=(BF16,))
+
     # a pre-norm block's tail: the residual add after the MLP is planned as its own elementwise
     # kernel (x1 also feeds the LayerNorm), which the B200 backend folds into the GEMM epilogue
     def block_tail(x, r, wo, g, w1, b1, w2, b2):

@@ -590,3 +590,34 @@ def test_pdl_chosen_per_program(monkeypatch):
     assert B200Program(FX.load_plan("cfg5_m131072"), device="cuda").pdl
     monkeypatch.setenv("TENSORJIT_B200_PDL", "0")
     assert not B200Program(FX.load_plan("cfg4"), device="cuda").pdl
+
+
+def test_transpose_copy_folded_into_gemm_operand():
+    """A transpose copy kernel that only feeds a bf16/f16 GEMM's A operand disappears: the GEMM
+    reads A from the transpose's source through a tensor map whose dims are ordered by stride,
+    with the 64-column k-block and the 128-row tile as the only box extents above 1."""
+    from mlir_gpu_kernel_compiler_b200.fuse import fuse, strided_a_layout
+
+    f = fuse(FX.load_plan("merge_heads_linear__bf16"))
+    assert [k.kind for k in f.kernels] == ["matmul"] and f.meta["folded_copies"] == 1
+    (g,) = generate(f)
+    assert g.info["a_strided"] and not g.info["pair"] and "A_RANK = 4" in g.source
+    tm = g.tmaps[0]
+    assert tm.dims == [64, 256, 4, 2] and tm.box == [64, 128, 1, 1]        # d, s, h, b of x[2, 4, 256, 64]
+    assert tm.strides == sorted(tm.strides) == [64 * 2, 256 * 64 * 2, 4 * 256 * 64 * 2]
+    assert g.args[tm.arg][1].op == "input"                                  # the source x, not the transpose
+    # batch-dim transpose before a batched matmul: rank 3, the batch coordinate from the GEMM's batch
+    (g2,) = generate(fuse(FX.load_plan("transpose_bmm__bf16")))
+    assert g2.tmaps[0].dims == [128, 4, 256] and g2.tmaps[0].box == [64, 1, 128] and "A_RANK = 3" in g2.source
+    # kept as a copy: f32 (3xTF32 reads split copies), a 128-row tile that would straddle two
+    # batch elements (seq 200), a K block that would straddle two heads (head dim 32)
+    assert [k.kind for k in fuse(FX.load_plan("merge_heads_linear__f32")).kernels] == ["copy", "matmul"]
+    for shape in ((2, 4, 200, 64, 128), (2, 8, 256, 32, 128)):
+        p = FX.merge_heads_plan(*shape)
+        assert [k.kind for k in fuse(p).kernels] == ["copy", "matmul"], shape
+    ok = FX.merge_heads_plan(8, 16, 2048, 64, 1024)                            # the transformer config's merge
+    assert strided_a_layout(ok, ok.kernels[1], set()) is not None
+    # the transpose is also a program output: kept
+    esc = FX.load_plan("merge_heads_linear__bf16")
+    esc.outputs.append(esc.kernels[0].outputs[0])
+    assert [k.kind for k in fuse(esc).kernels] == ["copy", "matmul"]
