@@ -880,6 +880,11 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     sa = k.attrs.get("a_strided")       # A read from a folded transpose's source (fuse.py)
     assert sa is None or not (x3 or pk_a), "a folded transpose needs the plain 16-bit A path"
     pair = bool(tile and tile.get("PAIR")) and not b_mn and BN in (128, 256) and not x3 and not sa
+    if tile and tile.get("PAIR") and not pair:
+        # a CTA-pair tile run on one CTA (e.g. A read from a folded transpose): each stage then
+        # holds the whole B tile, so keep only as many stages as fit beside the epilogue staging
+        per_stage = (2 if x3 else 1) * (128 * 128 + BN * 128)
+        STAGES = min(STAGES, max(2, (232448 - 1024 - 8 * 2 * 32 * 32 * 2 - 512) // per_stage))
     a_bs = _batch_strides(a, batch_shape)
     b_bs = _batch_strides(b, batch_shape)
     a_mats = prod(a.shape[:-2])

@@ -621,3 +621,13 @@ def test_transpose_copy_folded_into_gemm_operand():
     esc = FX.load_plan("merge_heads_linear__bf16")
     esc.outputs.append(esc.kernels[0].outputs[0])
     assert [k.kind for k in fuse(esc).kernels] == ["copy", "matmul"]
+
+
+def test_folded_transpose_gemm_fits_on_one_cta():
+    """The transformer config's head merge + output projection: its tuned tile is a CTA pair,
+    which a folded transpose cannot use; the single-CTA kernel then keeps the stages that fit."""
+    from mlir_gpu_kernel_compiler_b200 import B200Program
+
+    p = B200Program(FX.merge_heads_plan(8, 16, 2048, 64, 1024), device="cuda")
+    (k,) = p.kernel_sources
+    assert k.info["a_strided"] and not k.info["pair"] and k.smem <= 232448 and k.info["stages"] >= 2
