@@ -515,8 +515,9 @@ class Epilogue:
         self.mm, self.M, self.N, self.out_shape = mm, M, N, out_shape
         self.batch_shape = out_shape[:-2]
         self.epi_nodes = [n for n in k.nodes if n is not mm]
-        a_src = (k.attrs.get("a_strided") or {}).get("src")     # A read from a transpose's source
-        self.epi_inputs = [n for n in k.inputs if n is not a and n is not b and n is not a_src]
+        # operands read from a folded transpose's source
+        srcs = [(k.attrs.get(f) or {}).get("src") for f in ("a_strided", "b_strided")]
+        self.epi_inputs = [n for n in k.inputs if n is not a and n is not b and all(n is not x for x in srcs)]
         self.in_index, self.out_index = in_index, out_index
         self.strides = {}
         for n in self.epi_inputs:
@@ -820,29 +821,31 @@ def choose_tile(M: int, N: int, batch: int, b_mn_major: bool, override: dict | N
     return BN, STAGES, 16
 
 
-def _a_map_order(sa: dict) -> tuple[list[str], list[int]]:
-    """Roles of the folded-transpose A dims (K0 [K1] M0 [M1] [B], as ``strided_a_layout`` lists
-    them) and the order of those dims in the tensor map: sorted by stride, as the attention
-    kernel's maps are, so the map's strides never decrease.  Only K0 (unit stride, always first)
-    and M0 have box extents above 1, so the tile lands in shared memory as 128 rows of 64."""
-    roles = (["k0", "k1"][: sa["k_dims"]] + ["m0", "m1"][: sa["m_dims"]] + ["b"] * sa["batch_dims"])
-    order = sorted(range(len(roles)), key=lambda i: sa["dims"][i][1])
+def _operand_map_order(sd: dict) -> tuple[list[str], list[int]]:
+    """Roles of a folded-transpose operand's dims (K0 [K1] R0 [R1] [B0 [B1]], as
+    ``fuse.strided_operand_layout`` lists them; R = rows, M for A, N for B) and the order of those
+    dims in the tensor map: sorted by stride, as the attention kernel's maps are, so the map's
+    strides never decrease.  Only K0 (unit stride, always first) and R0 have box extents above
+    1, so a tile lands in shared memory as rows of one 64-element k-block."""
+    roles = ["k0", "k1"][: sd["k_dims"]] + ["r0", "r1"][: sd["r_dims"]] + ["b0", "b1"][: sd["batch_dims"]]
+    order = sorted(range(len(roles)), key=lambda i: sd["dims"][i][1])
     return roles, order
 
 
-def _a_coords_function(sa: dict) -> list[str]:
-    """``a_coords(ab, m0, k0, c)``: tensor-map coordinates of the A tile at row m0, column k0 of
-    A matrix ab when A is read from a folded transpose's source."""
-    dims = sa["dims"]
-    roles, order = _a_map_order(sa)
-    k0_size = dims[roles.index("k0")][0]
-    m0_size = dims[roles.index("m0")][0]
-    value = {"k0": f"k0 % {k0_size}" if "k1" in roles else "k0", "k1": f"k0 / {k0_size}",
-             "m0": f"m0 % {m0_size}" if "m1" in roles else "m0", "m1": f"m0 / {m0_size}",
-             "b": "static_cast<int>(ab)"}
-    L = ["  static __device__ __forceinline__ void a_coords(long ab, int m0, int k0, int (&c)[5]) {"]
-    if "b" not in roles:
-        L.append("    (void)ab;")
+def _operand_coords_function(sd: dict, name: str, rvar: str, bvar: str) -> list[str]:
+    """``<name>(batch, r0, k0, c)``: tensor-map coordinates of the operand tile at row r0 (of M
+    for A, N for B), column k0 of operand matrix ``batch`` when the operand is read from a folded
+    transpose's source.  Two batch dims split the batch index (inner dim first)."""
+    dims = sd["dims"]
+    roles, order = _operand_map_order(sd)
+    size = {r: dims[i][0] for i, r in enumerate(roles)}
+    value = {"k0": f"k0 % {size['k0']}" if "k1" in roles else "k0", "k1": f"k0 / {size['k0']}",
+             "r0": f"{rvar} % {size['r0']}" if "r1" in roles else rvar, "r1": f"{rvar} / {size['r0']}",
+             "b0": f"static_cast<int>({bvar} % {size['b0']}L)" if "b1" in roles else f"static_cast<int>({bvar})",
+             "b1": f"static_cast<int>({bvar} / {size.get('b0', 1)}L)"}
+    L = [f"  static __device__ __forceinline__ void {name}(long {bvar}, int {rvar}, int k0, int (&c)[5]) {{"]
+    if "b0" not in roles:
+        L.append(f"    (void){bvar};")
     for pos, i in enumerate(order):
         L.append(f"    c[{pos}] = {value[roles[i]]};")
     L.append("  }")
@@ -878,8 +881,11 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     if x3:
         STAGES = min(STAGES, max(2, (200 * 1024) // (2 * (128 * 128 + BN * 128))))
     sa = k.attrs.get("a_strided")       # A read from a folded transpose's source (fuse.py)
-    assert sa is None or not (x3 or pk_a), "a folded transpose needs the plain 16-bit A path"
-    pair = bool(tile and tile.get("PAIR")) and not b_mn and BN in (128, 256) and not x3 and not sa
+    sb = k.attrs.get("b_strided")       # K-major B read from a folded transpose's source
+    assert not sa or not (x3 or pk_a), "a folded transpose needs the plain 16-bit A path"
+    assert not sb or not (x3 or pk_b or b_mn), "a folded transpose needs the plain 16-bit K-major B path"
+    pair = (bool(tile and tile.get("PAIR")) and not b_mn and BN in (128, 256) and not x3 and not sa
+            and not sb)
     if tile and tile.get("PAIR") and not pair:
         # a CTA-pair tile run on one CTA (e.g. A read from a folded transpose): each stage then
         # holds the whole B tile, so keep only as many stages as fit beside the epilogue staging
@@ -918,8 +924,11 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     L.append(f"  static constexpr bool STAGED_STORE = {'true' if staged else 'false'};")
     L.append(f"  static constexpr bool STAGE_LAST = {'true' if stage_last else 'false'};")
     L.append(f"  static constexpr int A_RANK = {len(sa['dims']) if sa else 2};")
+    L.append(f"  static constexpr int B_RANK = {len(sb['dims']) if sb else 2};")
     if sa:
-        L += _a_coords_function(sa)
+        L += _operand_coords_function(sa, "a_coords", "m0", "ab")
+    if sb:
+        L += _operand_coords_function(sb, "b_coords", "n0", "bb")
     L.append(f"  using OutT = {CTYPE[outs[0].dtype] if (tma_store or staged) else 'float'};")
     L.append(f"  static constexpr long BATCH = {batch}L, A_MATS = {a_mats}L, B_MATS = {b_mats}L;")
     L.append(f"  static constexpr bool BF16 = {'true' if a.dtype == 'bf16' else 'false'}, B_MN_MAJOR = {'true' if b_mn else 'false'};")
@@ -963,16 +972,21 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     b_pitch = pitch if (x3 or pk_b) else K
     pk_arg = status_idx + 1
     a_arg = status_idx + 1 if x3 else (pk_arg if pk_a else in_index[(sa["src"] if sa else a).id])
-    b_arg = status_idx + 2 if x3 else (pk_arg + int(pk_a) if pk_b else in_index[b.id])
+    b_arg = status_idx + 2 if x3 else (pk_arg + int(pk_a) if pk_b else in_index[(sb["src"] if sb else b).id])
     if sa:
-        roles, order = _a_map_order(sa)
-        box = [bk if roles[i] == "k0" else (128 if roles[i] == "m0" else 1) for i in order]
+        roles, order = _operand_map_order(sa)
+        box = [bk if roles[i] == "k0" else (128 if roles[i] == "r0" else 1) for i in order]
         tmA = TMapSpec(arg=a_arg, dtype=op_dt, dims=[sa["dims"][i][0] for i in order],
                        strides=[sa["dims"][i][1] * esz for i in order[1:]], box=box, swizzle=3)
     else:
         tmA = TMapSpec(arg=a_arg, dtype=op_dt, dims=[K, a_mats * M], strides=[a_pitch * esz], box=[bk, 128],
                        swizzle=3)
-    if not b_mn:
+    if sb:
+        roles, order = _operand_map_order(sb)
+        box = [bk if roles[i] == "k0" else (BN if roles[i] == "r0" else 1) for i in order]
+        tmB = TMapSpec(arg=b_arg, dtype=op_dt, dims=[sb["dims"][i][0] for i in order],
+                       strides=[sb["dims"][i][1] * esz for i in order[1:]], box=box, swizzle=3)
+    elif not b_mn:
         tmB = TMapSpec(arg=b_arg, dtype=op_dt, dims=[K, b_mats * N], strides=[b_pitch * esz],
                        box=[bk, BN // 2 if pair else BN], swizzle=3)
     else:
@@ -1003,7 +1017,7 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
                       tmaps=tmaps, cluster=(2, 1, 1) if pair else (1, 1, 1),
                       info={"M": M, "N": N, "K": K, "batch": batch, "BN": BN, "stages": STAGES,
                             "tma_store": tma_store, "staged_store": staged, "stage_last": stage_last,
-                            "a_strided": bool(sa),
+                            "a_strided": bool(sa), "b_strided": bool(sb),
                             "epi_warps": epi_warps, "pair": pair,
                             "tf32x3": x3,
                             "ksplit": ksplit, "packed": [x for x, f in (("a", pk_a), ("b", pk_b)) if f],
@@ -1044,7 +1058,7 @@ def gen_gemm_multi(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = 
     L.append(f"  static constexpr int GROUP_N = {int((tile or {}).get('GROUP_N', 0))};")
     L.append(f"  static constexpr int EPI_WARPS = 8, KSPLIT = 1, NSEG = {len(parts)};")
     L.append("  static constexpr bool TF32X3 = false, TMA_STORE = false, STAGED_STORE = false, STAGE_LAST = false;")
-    L.append("  static constexpr int A_RANK = 2;")
+    L.append("  static constexpr int A_RANK = 2, B_RANK = 2;")
     L.append("  using OutT = float;")
     L.append("  static constexpr long BATCH = 1L, A_MATS = 1L, B_MATS = 1L;")
     L.append(f"  static constexpr bool BF16 = {'true' if dt == 'bf16' else 'false'}, B_MN_MAJOR = false;")

@@ -231,112 +231,125 @@ def _subdims(sizes_strides: list[tuple[int, int]]) -> list[tuple[int, int]]:
     return out
 
 
-def strided_a_layout(plan: PProgram, k: PKernel, escaping: set[int]) -> Optional[dict]:
-    """How a bf16/f16 matmul kernel's A operand could be read straight from the source of the
-    ``copy`` kernel (a transpose) that materialises it, instead of from the copy's output.
+def strided_operand_layout(plan: PProgram, k: PKernel, which: int, escaping: set[int],
+                           taken: frozenset = frozenset()) -> Optional[dict]:
+    """How operand ``which`` (0 = A, 1 = the K-major B of a ``trans_b`` matmul) of a bf16/f16
+    matmul kernel could be read straight from the source of the ``copy`` kernel (a transpose)
+    that materialises it, instead of from the copy's output.
 
-    A[batch.., m, k] is the transpose T of a source X (optionally reshaped): each logical dim of
-    A is a run of T's dims, and T's dim i has X's stride for dim perm[i].  The GEMM reads A by
-    TMA through one tensor map over X whose dims are, innermost first, K0 [K1] M0 [M1] [batch]:
-    K0 is unit-stride (a multiple of the 64-element k-block when K1 exists), a 128-row tile never
-    straddles M1 (M0 a multiple of 128), at most one batch dim, rank <= 5, 16-byte strides.
-    Returns {"src", "copy", "dims": [(size, stride) innermost first], "k_dims", "m_dims",
-    "batch_dims"} or None."""
+    The operand O[batch.., rows, k] (rows = M for A, N for B) is the transpose T of a source X,
+    optionally reshaped: each logical dim of O is a run of T's dims, and T's dim i has X's stride
+    for dim perm[i].  The GEMM reads O by TMA through one tensor map over X whose dims are K0 [K1]
+    R0 [R1] [B0 [B1]] (innermost first within each part): K0 unit-stride (a multiple of the
+    64-element k-block when K1 exists), a row tile never straddles R1 (R0 a multiple of 128 for
+    A, of 256 for B), at most two batch dims, rank <= 5, 16-byte strides; X not read elsewhere in
+    the kernel, T read only here and not a program output.  ``taken``: copy kernels already
+    folded into the other operand.  Returns {"src", "copy", "dims": [(size, stride)], "k_dims",
+    "r_dims", "batch_dims"} or None."""
     mm = k.anchor
-    if k.kind != "matmul" or mm is None or mm.op != "matmul" or k.attrs.get("a_strided"):
+    if k.kind != "matmul" or mm is None or mm.op != "matmul":
+        return None
+    if which == 1 and not mm.attrs.get("trans_b"):
         return None
     a, b = mm.inputs
-    t = plan.resolve(a)
+    o = mm.inputs[which]
+    t = plan.resolve(o)
     if (t.op != "transpose" or a.dtype not in ("bf16", "f16") or b.dtype != a.dtype or t.id in escaping
-            or a.id in escaping):
+            or o.id in escaping):
         return None
     copy_i = next((i for i, c in enumerate(plan.kernels) if c.kind == "copy" and len(c.nodes) == 1
                    and c.nodes[0] is t and c.outputs == [t]), None)
-    if copy_i is None:
+    if copy_i is None or copy_i in taken:
         return None
-    # T (and the alias A) is read by this matmul alone, once, as its A operand
-    ids = {t.id, a.id}
-    readers = [j for j, c in enumerate(plan.kernels) if j != copy_i
-               and any(n.id in ids or plan.resolve(n).id == t.id for n in c.inputs)]
-    if readers != [plan.kernels.index(k)]:
-        return None
-    if sum(1 for n in k.nodes for i in n.inputs if i.id in ids or plan.resolve(i).id == t.id) != 1:
+    # T (and the alias O) is read by this matmul alone, once, as this operand
+    ids = {t.id, o.id}
+    reads = lambda n: n.id in ids or plan.resolve(n).id == t.id  # noqa: E731
+    readers = [j for j, c in enumerate(plan.kernels) if j != copy_i and any(reads(n) for n in c.inputs)]
+    if readers != [plan.kernels.index(k)] or sum(1 for n in k.nodes for i in n.inputs if reads(i)) != 1:
         return None
     x = t.inputs[0]
-    if any(n is x for n in k.inputs):       # X also read directly (e.g. by the epilogue): keep the copy
+    if any(n is x or plan.resolve(n) is plan.resolve(x) for n in k.inputs):   # X also read directly
         return None
     perm = t.attrs["perm"]
     cs = contiguous_strides(x.shape)
     tdims = [(int(t.shape[i]), int(cs[perm[i]])) for i in range(len(t.shape))]
-    # each logical dim of A = a run of consecutive T dims (a reshape that only merges)
+    # each logical dim of O = a run of consecutive T dims (a reshape that only merges)
     groups, j = [], 0
-    for size in a.shape:
+    for size in o.shape:
         run, prod_ = [], 1
-        while prod_ < size or (size == 1 and not run and j < len(tdims) and tdims[j][0] == 1):
+        while prod_ < size:
             if j >= len(tdims):
                 return None
             run.append(tdims[j])
             prod_ *= tdims[j][0]
             j += 1
-            if size == 1:
-                break
         if prod_ != size:
             return None
         groups.append(run)
     if any(tdims[q][0] != 1 for q in range(j, len(tdims))):
         return None
     k_dims = _subdims(groups[-1])[::-1]                 # innermost first
-    m_dims = _subdims(groups[-2])[::-1]
+    r_dims = _subdims(groups[-2])[::-1]
     batch_dims = _subdims([d for g in groups[:-2] for d in g])[::-1]
-    K = int(a.shape[-1])
-    if not k_dims or k_dims[0][1] != 1 or len(k_dims) > 2 or len(m_dims) > 2 or len(batch_dims) > 1:
+    K = int(o.shape[-1])
+    if not k_dims or k_dims[0][1] != 1 or len(k_dims) > 2 or len(r_dims) > 2 or len(batch_dims) > 2:
         return None
-    if len(k_dims) == 2 and k_dims[0][0] % 64:
+    if (len(k_dims) == 2 and k_dims[0][0] % 64) or (len(k_dims) == 1 and K % 8):
         return None
-    if len(k_dims) == 1 and K % 8:
+    if len(r_dims) == 2 and r_dims[0][0] % (128 if which == 0 else 256):
         return None
-    if len(m_dims) == 2 and m_dims[0][0] % 128:
-        return None
-    dims = k_dims + m_dims + batch_dims
+    dims = k_dims + r_dims + batch_dims
     if len(dims) < 3 or len(dims) > 5 or any((st * 2) % 16 for _, st in dims[1:]):
         return None
-    return {"src": x, "copy": copy_i, "dims": dims, "k_dims": len(k_dims), "m_dims": len(m_dims),
+    return {"src": x, "copy": copy_i, "dims": dims, "k_dims": len(k_dims), "r_dims": len(r_dims),
             "batch_dims": len(batch_dims)}
 
 
-def fold_copies_into_gemm_a(plan: PProgram) -> PProgram:
-    """A transpose ``copy`` kernel whose output only feeds a bf16/f16 GEMM's A operand is removed:
-    the GEMM reads A from the transpose's source through a permuted-stride tensor map
-    (``strided_a_layout``), saving the copy's HBM round trip.  Outputs are unchanged."""
+def strided_a_layout(plan: PProgram, k: PKernel, escaping: set[int]) -> Optional[dict]:
+    """``strided_operand_layout`` of the A operand."""
+    return strided_operand_layout(plan, k, 0, escaping)
+
+
+def fold_copies_into_gemm(plan: PProgram) -> PProgram:
+    """A transpose ``copy`` kernel whose output only feeds a bf16/f16 GEMM's A operand, or the
+    K-major B of a ``trans_b`` GEMM, is removed: the GEMM reads that operand from the transpose's
+    source through a permuted-stride tensor map (``strided_operand_layout``), saving the copy's
+    HBM round trip.  Outputs are unchanged."""
     from .codegen.gemm import gemm_form
 
     escaping = {plan.resolve(o).id for o in plan.outputs}
     drop, replace = set(), {}
     for i, k in enumerate(plan.kernels):
-        lay = strided_a_layout(plan, k, escaping)
-        if lay is None:
+        lay_a = strided_operand_layout(plan, k, 0, escaping)
+        lay_b = strided_operand_layout(plan, k, 1, escaping,
+                                       frozenset({lay_a["copy"]}) if lay_a else frozenset())
+        if lay_a is None and lay_b is None:
             continue
         f = gemm_form(k)
         if f.mode != "f16" or f.pack_a or f.pack_b:
             continue
-        a = k.anchor.inputs[0]
+        attrs, subst = dict(k.attrs), {}
+        for name, lay, node in (("a_strided", lay_a, k.anchor.inputs[0]), ("b_strided", lay_b, k.anchor.inputs[1])):
+            if lay is not None:
+                attrs[name] = {key: lay[key] for key in ("src", "dims", "k_dims", "r_dims", "batch_dims")}
+                subst[node.id] = lay["src"]
+                drop.add(lay["copy"])
         fk = PKernel(kind="matmul", nodes=list(k.nodes), anchor=k.anchor,
-                     inputs=[lay["src"] if n is a else n for n in k.inputs], outputs=list(k.outputs),
+                     inputs=[subst.get(n.id, n) for n in k.inputs], outputs=list(k.outputs),
                      iter_shape=tuple(k.iter_shape))
-        fk.attrs = dict(k.attrs, a_strided={key: lay[key] for key in ("src", "dims", "k_dims", "m_dims",
-                                                                      "batch_dims")})
+        fk.attrs = attrs
         replace[i] = fk
-        drop.add(lay["copy"])
     if not replace:
         return plan
     kernels = [replace.get(i, k) for i, k in enumerate(plan.kernels) if i not in drop]
     return PProgram(name=plan.name, nodes=plan.nodes, inputs=plan.inputs, outputs=plan.outputs, kernels=kernels,
-                    aliases=plan.aliases, meta=dict(plan.meta, folded_copies=len(replace)))
+                    aliases=plan.aliases, meta=dict(plan.meta, folded_copies=len(drop)))
 
 
 def _plain_shared_a_matmul(k: PKernel):
     """(A, B, N) of a kernel that is a bare bf16/f16 ``A @ Bᵀ`` (2-D, no epilogue), else None."""
-    if k.kind != "matmul" or len(k.nodes) != 1 or k.outputs != [k.anchor] or k.attrs.get("a_strided"):
+    if (k.kind != "matmul" or len(k.nodes) != 1 or k.outputs != [k.anchor] or k.attrs.get("a_strided")
+            or k.attrs.get("b_strided")):
         return None
     mm = k.anchor
     if mm.op != "matmul" or not mm.attrs.get("trans_b"):
@@ -437,8 +450,8 @@ def absorb_elementwise_epilogues(plan: PProgram) -> PProgram:
 
 def fuse(plan: PProgram) -> PProgram:
     """All backend rewrites (``TENSORJIT_B200_FUSE=0`` disables them): attention chains,
-    transposes folded into a GEMM's A operand, GEMMs that share their A operand, then elementwise
-    kernels absorbed into the GEMM before them."""
+    transposes folded into the GEMM operands that read them, GEMMs that share their A operand,
+    then elementwise kernels absorbed into the GEMM before them."""
     if os.environ.get("TENSORJIT_B200_FUSE", "1") == "0":
         return plan
-    return absorb_elementwise_epilogues(fuse_shared_a_gemms(fold_copies_into_gemm_a(fuse_attention(plan))))
+    return absorb_elementwise_epilogues(fuse_shared_a_gemms(fold_copies_into_gemm(fuse_attention(plan))))

@@ -159,6 +159,17 @@ def cases(tj):
     add("transpose_bmm", lambda x, w: tj.gelu(tj.matmul(tj.permute(x, 1, 0, 2), w)),
         [(256, 4, 128), (4, 128, 192)], dtypes=(BF16,))
 
+    # unfused attention scores (no softmax follows): both GEMM operands come from head-split
+    # transposes of projection outputs, A and the K-major B (trans_b) each with two batch dims
+    def heads_scores(x, wq, wk):
+        def heads(t):
+            return tj.permute(tj.reshape(t, (2, 256, 4, 64)), 0, 2, 1, 3)
+
+        q, k = heads(tj.linear(x, wq) * 0.0625), heads(tj.linear(x, wk) * 0.0625)
+        return tj.matmul(q, tj.transpose(k, -1, -2)) * 0.125
+
+    add("heads_scores", heads_scores, [(512, 256), (256, 256), (256, 256)], dtypes=(BF16,))
+
     # a pre-norm block's tail: the residual add after the MLP is planned as its own elementwise
     # kernel (x1 also feeds the LayerNorm), which the B200 backend folds into the GEMM epilogue
     def block_tail(x, r, wo, g, w1, b1, w2, b2):

@@ -609,6 +609,14 @@ def test_transpose_copy_folded_into_gemm_operand():
     # batch-dim transpose before a batched matmul: rank 3, the batch coordinate from the GEMM's batch
     (g2,) = generate(fuse(FX.load_plan("transpose_bmm__bf16")))
     assert g2.tmaps[0].dims == [128, 4, 256] and g2.tmaps[0].box == [64, 1, 128] and "A_RANK = 3" in g2.source
+    # unfused attention scores: A (q) and the K-major B (k) both read from the projection outputs,
+    # each through a rank-4 map with two batch dims (head, batch) split from the batch index
+    hs = fuse(FX.load_plan("heads_scores__bf16"))
+    assert [k.kind for k in hs.kernels] == ["matmul"] * 3 and hs.meta["folded_copies"] == 2
+    g3 = generate(hs)[-1]
+    assert g3.info["a_strided"] and g3.info["b_strided"] and "A_RANK = 4" in g3.source and "B_RANK = 4" in g3.source
+    assert g3.tmaps[0].dims == g3.tmaps[1].dims == [64, 4, 256, 2] and g3.tmaps[1].box[2] == g3.info["BN"]
+    assert "c[1] = static_cast<int>(ab % 4L);" in g3.source and "c[3] = static_cast<int>(bb / 4L);" in g3.source
     # kept as a copy: f32 (3xTF32 reads split copies), a 128-row tile that would straddle two
     # batch elements (seq 200), a K block that would straddle two heads (head dim 32)
     assert [k.kind for k in fuse(FX.load_plan("merge_heads_linear__f32")).kernels] == ["copy", "matmul"]
