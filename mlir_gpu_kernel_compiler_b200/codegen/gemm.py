@@ -826,8 +826,10 @@ def _operand_map_order(sd: dict) -> tuple[list[str], list[int]]:
     ``fuse.strided_operand_layout`` lists them; R = rows, M for A, N for B) and the order of those
     dims in the tensor map: sorted by stride, as the attention kernel's maps are, so the map's
     strides never decrease.  Only K0 (unit stride, always first) and R0 have box extents above
-    1, so a tile lands in shared memory as rows of one 64-element k-block."""
-    roles = ["k0", "k1"][: sd["k_dims"]] + ["r0", "r1"][: sd["r_dims"]] + ["b0", "b1"][: sd["batch_dims"]]
+    1, so a tile lands in shared memory as rows of one 64-element k-block (for an N-major B, R0
+    is unit-stride and first: 64 x 64 chunks as the N-major path loads them)."""
+    k_roles, r_roles = ["k0", "k1"][: sd["k_dims"]], ["r0", "r1"][: sd["r_dims"]]
+    roles = (r_roles + k_roles if sd.get("n_major") else k_roles + r_roles) + ["b0", "b1"][: sd["batch_dims"]]
     order = sorted(range(len(roles)), key=lambda i: sd["dims"][i][1])
     return roles, order
 
@@ -883,7 +885,7 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     sa = k.attrs.get("a_strided")       # A read from a folded transpose's source (fuse.py)
     sb = k.attrs.get("b_strided")       # K-major B read from a folded transpose's source
     assert not sa or not (x3 or pk_a), "a folded transpose needs the plain 16-bit A path"
-    assert not sb or not (x3 or pk_b or b_mn), "a folded transpose needs the plain 16-bit K-major B path"
+    assert not sb or not (x3 or pk_b or b_mn != bool(sb.get("n_major"))), "a folded B needs the plain 16-bit path"
     pair = (bool(tile and tile.get("PAIR")) and not b_mn and BN in (128, 256) and not x3 and not sa
             and not sb)
     if tile and tile.get("PAIR") and not pair:
@@ -924,7 +926,8 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
     L.append(f"  static constexpr bool STAGED_STORE = {'true' if staged else 'false'};")
     L.append(f"  static constexpr bool STAGE_LAST = {'true' if stage_last else 'false'};")
     L.append(f"  static constexpr int A_RANK = {len(sa['dims']) if sa else 2};")
-    L.append(f"  static constexpr int B_RANK = {len(sb['dims']) if sb else 2};")
+    L.append(f"  static constexpr int B_RANK = {len(sb['dims']) if sb else (3 if b_mn else 2)};")
+    L.append(f"  static constexpr bool B_FOLDED = {'true' if sb else 'false'};")
     if sa:
         L += _operand_coords_function(sa, "a_coords", "m0", "ab")
     if sb:
@@ -983,7 +986,10 @@ def gen_gemm_tc(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = Non
                        swizzle=3)
     if sb:
         roles, order = _operand_map_order(sb)
-        box = [bk if roles[i] == "k0" else (BN if roles[i] == "r0" else 1) for i in order]
+        if sb.get("n_major"):   # 64-column x 64-k chunks, as the N-major path loads them
+            box = [64 if roles[i] in ("r0", "k0") else 1 for i in order]
+        else:
+            box = [bk if roles[i] == "k0" else (BN if roles[i] == "r0" else 1) for i in order]
         tmB = TMapSpec(arg=b_arg, dtype=op_dt, dims=[sb["dims"][i][0] for i in order],
                        strides=[sb["dims"][i][1] * esz for i in order[1:]], box=box, swizzle=3)
     elif not b_mn:
@@ -1059,6 +1065,7 @@ def gen_gemm_multi(k: PKernel, symbol: str, kernel_id: int, tile: dict | None = 
     L.append(f"  static constexpr int EPI_WARPS = 8, KSPLIT = 1, NSEG = {len(parts)};")
     L.append("  static constexpr bool TF32X3 = false, TMA_STORE = false, STAGED_STORE = false, STAGE_LAST = false;")
     L.append("  static constexpr int A_RANK = 2, B_RANK = 2;")
+    L.append("  static constexpr bool B_FOLDED = false;")
     L.append("  using OutT = float;")
     L.append("  static constexpr long BATCH = 1L, A_MATS = 1L, B_MATS = 1L;")
     L.append(f"  static constexpr bool BF16 = {'true' if dt == 'bf16' else 'false'}, B_MN_MAJOR = false;")

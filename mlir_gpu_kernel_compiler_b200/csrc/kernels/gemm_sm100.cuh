@@ -295,7 +295,7 @@ TJ_DEV void staged_store_rows(const P& prm, const uint8_t* stage, uint32_t out_s
 //   static constexpr bool BF16, B_MN_MAJOR, TMA_STORE, STAGED_STORE, STAGE_LAST;  using OutT = <output type>;
 //   static constexpr int A_RANK, B_RANK (2: the operand through a 2-D map [K, mats * rows]; 3..5:
 //   read from a transpose's source, with static __device__ void a_coords(long ab, int m0, int k0,
-//   int (&c)[5]) / b_coords(long bb, int n0, int k0, int (&c)[5]); B then K-major);
+//   int (&c)[5]) / b_coords(long bb, int n0, int k0, int (&c)[5]); B_FOLDED marks the folded B);
 //   static __device__ void batch_map(long b, long& a_batch, long& b_batch);
 //   template <class P> static __device__ void epilogue(const P& prm, long b, long i, long j0, const float (&acc)[32]);
 //     (direct 16-byte stores), or with TMA_STORE:
@@ -319,8 +319,7 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
   constexpr uint32_t B_BYTES = BN * 128;
   constexpr uint32_t STAGE_BYTES = OPC * (A_BYTES + B_BYTES);
   static_assert(!X3 || (!Cfg::B_MN_MAJOR && !Cfg::TMA_STORE), "3xTF32 mode: K-major B, direct stores");
-  static_assert(!X3 || (Cfg::A_RANK == 2 && Cfg::B_RANK == 2), "3xTF32 mode reads its copies through 2-D maps");
-  static_assert(Cfg::B_RANK == 2 || !Cfg::B_MN_MAJOR, "a folded B operand is K-major");
+  static_assert(!X3 || (Cfg::A_RANK == 2 && !Cfg::B_FOLDED), "3xTF32 mode reads its copies through 2-D maps");
   constexpr int m_tiles = (Cfg::M + BM - 1) / BM;
   constexpr int n_tiles = (Cfg::N + BN - 1) / BN;
   constexpr int k_blocks = (Cfg::K + BK - 1) / BK;
@@ -469,13 +468,21 @@ __device__ __forceinline__ void gemm_sm100(const P& prm, int* status, int kernel
           } else {
             tma_load_2d(smem_u32(a_st), tmA, fb, kb * BK, a_row);
           }
-          if constexpr (Cfg::B_RANK > 2) {
+          if constexpr (Cfg::B_FOLDED && !Cfg::B_MN_MAJOR) {
             // K-major B read in place from a transpose's source
             int bc[5] = {0, 0, 0, 0, 0};
             Cfg::b_coords(bb, n0, kb * BK, bc);
             tma_load_nd<Cfg::B_RANK>(smem_u32(b_st), tb, fb, bc);
           } else if constexpr (!Cfg::B_MN_MAJOR) {
             tma_load_2d(smem_u32(b_st), tb, fb, kb * BK, static_cast<int>(bb * Cfg::N + n0));
+          } else if constexpr (Cfg::B_FOLDED) {
+            // N-major B read in place from a transpose's source: the same 64 x 64 chunks
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c) {
+              int bc[5] = {0, 0, 0, 0, 0};
+              Cfg::b_coords(bb, n0 + 64 * c, kb * BK, bc);
+              tma_load_nd<Cfg::B_RANK>(smem_u32(b_st + c * (BK * 128)), tmB, fb, bc);
+            }
           } else {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c)

@@ -149,7 +149,7 @@ __device__ __forceinline__ void gemm_sm100_pair(const P& prm, int* status, int k
   uint8_t* sOut = sB + STAGES * B_BYTES;
   constexpr bool STAGED = Cfg::STAGED_STORE;   // plain coalesced stores through the stage
   static_assert(!Cfg::STAGE_LAST, "last-tile staging is a single-CTA kernel path");
-  static_assert(Cfg::A_RANK == 2 && Cfg::B_RANK == 2, "operands read from a transpose's source: single-CTA path");
+  static_assert(Cfg::A_RANK == 2 && !Cfg::B_FOLDED, "operands read from a transpose's source: single-CTA path");
   static_assert(!(STAGED && Cfg::TMA_STORE), "one store path");
   constexpr uint32_t OUT_STAGE = (Cfg::TMA_STORE || STAGED) ? 32 * 32 * 2 : 0;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + EPI_WARPS * 2 * OUT_STAGE);

@@ -233,11 +233,12 @@ def _subdims(sizes_strides: list[tuple[int, int]]) -> list[tuple[int, int]]:
 
 def strided_operand_layout(plan: PProgram, k: PKernel, which: int, escaping: set[int],
                            taken: frozenset = frozenset()) -> Optional[dict]:
-    """How operand ``which`` (0 = A, 1 = the K-major B of a ``trans_b`` matmul) of a bf16/f16
-    matmul kernel could be read straight from the source of the ``copy`` kernel (a transpose)
-    that materialises it, instead of from the copy's output.
+    """How operand ``which`` (0 = A, 1 = B) of a bf16/f16 matmul kernel could be read straight
+    from the source of the ``copy`` kernel (a transpose) that materialises it, instead of from
+    the copy's output.
 
-    The operand O[batch.., rows, k] (rows = M for A, N for B) is the transpose T of a source X,
+    The operand O[batch.., rows, k] (rows = M for A, N for a ``trans_b`` B), or O[batch.., k, n]
+    for an N-major B (``n_major``: then its N dims come first, as rows), is the transpose T of X,
     optionally reshaped: each logical dim of O is a run of T's dims, and T's dim i has X's stride
     for dim perm[i].  The GEMM reads O by TMA through one tensor map over X whose dims are K0 [K1]
     R0 [R1] [B0 [B1]] (innermost first within each part): K0 unit-stride (a multiple of the
@@ -245,12 +246,11 @@ def strided_operand_layout(plan: PProgram, k: PKernel, which: int, escaping: set
     A, of 256 for B), at most two batch dims, rank <= 5, 16-byte strides; X not read elsewhere in
     the kernel, T read only here and not a program output.  ``taken``: copy kernels already
     folded into the other operand.  Returns {"src", "copy", "dims": [(size, stride)], "k_dims",
-    "r_dims", "batch_dims"} or None."""
+    "r_dims", "batch_dims", "n_major"} or None."""
     mm = k.anchor
     if k.kind != "matmul" or mm is None or mm.op != "matmul":
         return None
-    if which == 1 and not mm.attrs.get("trans_b"):
-        return None
+    n_major = which == 1 and not mm.attrs.get("trans_b")
     a, b = mm.inputs
     o = mm.inputs[which]
     t = plan.resolve(o)
@@ -288,21 +288,24 @@ def strided_operand_layout(plan: PProgram, k: PKernel, which: int, escaping: set
         groups.append(run)
     if any(tdims[q][0] != 1 for q in range(j, len(tdims))):
         return None
-    k_dims = _subdims(groups[-1])[::-1]                 # innermost first
-    r_dims = _subdims(groups[-2])[::-1]
+    inner, outer = _subdims(groups[-1])[::-1], _subdims(groups[-2])[::-1]     # innermost first
+    k_dims, r_dims = (outer, inner) if n_major else (inner, outer)
     batch_dims = _subdims([d for g in groups[:-2] for d in g])[::-1]
-    K = int(o.shape[-1])
-    if not k_dims or k_dims[0][1] != 1 or len(k_dims) > 2 or len(r_dims) > 2 or len(batch_dims) > 2:
+    if not inner or inner[0][1] != 1 or len(k_dims) > 2 or len(r_dims) > 2 or len(batch_dims) > 2:
         return None
-    if (len(k_dims) == 2 and k_dims[0][0] % 64) or (len(k_dims) == 1 and K % 8):
+    if len(inner) == 1 and int(o.shape[-1]) % 8:
+        return None
+    # a k-block (64) never straddles two K sub-dims; a row tile (128 rows of A, a 256-wide B tile,
+    # 64-column chunks of an N-major B) never straddles two row sub-dims
+    if len(k_dims) == 2 and k_dims[0][0] % 64:
         return None
     if len(r_dims) == 2 and r_dims[0][0] % (128 if which == 0 else 256):
         return None
-    dims = k_dims + r_dims + batch_dims
+    dims = (r_dims + k_dims if n_major else k_dims + r_dims) + batch_dims
     if len(dims) < 3 or len(dims) > 5 or any((st * 2) % 16 for _, st in dims[1:]):
         return None
     return {"src": x, "copy": copy_i, "dims": dims, "k_dims": len(k_dims), "r_dims": len(r_dims),
-            "batch_dims": len(batch_dims)}
+            "batch_dims": len(batch_dims), "n_major": n_major}
 
 
 def strided_a_layout(plan: PProgram, k: PKernel, escaping: set[int]) -> Optional[dict]:
@@ -311,8 +314,8 @@ def strided_a_layout(plan: PProgram, k: PKernel, escaping: set[int]) -> Optional
 
 
 def fold_copies_into_gemm(plan: PProgram) -> PProgram:
-    """A transpose ``copy`` kernel whose output only feeds a bf16/f16 GEMM's A operand, or the
-    K-major B of a ``trans_b`` GEMM, is removed: the GEMM reads that operand from the transpose's
+    """A transpose ``copy`` kernel whose output only feeds a bf16/f16 GEMM's A or B operand is
+    removed: the GEMM reads that operand from the transpose's
     source through a permuted-stride tensor map (``strided_operand_layout``), saving the copy's
     HBM round trip.  Outputs are unchanged."""
     from .codegen.gemm import gemm_form
@@ -331,7 +334,8 @@ def fold_copies_into_gemm(plan: PProgram) -> PProgram:
         attrs, subst = dict(k.attrs), {}
         for name, lay, node in (("a_strided", lay_a, k.anchor.inputs[0]), ("b_strided", lay_b, k.anchor.inputs[1])):
             if lay is not None:
-                attrs[name] = {key: lay[key] for key in ("src", "dims", "k_dims", "r_dims", "batch_dims")}
+                attrs[name] = {key: lay[key] for key in ("src", "dims", "k_dims", "r_dims", "batch_dims",
+                                                         "n_major")}
                 subst[node.id] = lay["src"]
                 drop.add(lay["copy"])
         fk = PKernel(kind="matmul", nodes=list(k.nodes), anchor=k.anchor,

@@ -170,6 +170,21 @@ def cases(tj):
 
     add("heads_scores", heads_scores, [(512, 256), (256, 256), (256, 256)], dtypes=(BF16,))
 
+    # an attention whose probabilities are also returned (so it is not fused): the q / k / v head
+    # splits, the N-major v of P·V and the head merge before the output projection are all copies
+    # that the GEMMs reading them fold away
+    def heads_attention_probs(x, wq, wk, wv, wo):
+        def heads(t):
+            return tj.permute(tj.reshape(t, (2, 256, 4, 64)), 0, 2, 1, 3)
+
+        q, k, v = (heads(tj.linear(x, w) * 0.0625) for w in (wq, wk, wv))
+        p_ = tj.softmax(tj.matmul(q, tj.transpose(k, -1, -2)) * 0.125)
+        o = tj.linear(tj.reshape(tj.permute(tj.matmul(p_, v), 0, 2, 1, 3), (512, 256)), wo) * 0.0625
+        return o, p_
+
+    add("heads_attention_probs", heads_attention_probs,
+        [(512, 256), (256, 256), (256, 256), (256, 256), (256, 256)], dtypes=(BF16,))
+
     # a pre-norm block's tail: the residual add after the MLP is planned as its own elementwise
     # kernel (x1 also feeds the LayerNorm), which the B200 backend folds into the GEMM epilogue
     def block_tail(x, r, wo, g, w1, b1, w2, b2):

@@ -1,6 +1,7 @@
 """A transpose copy kernel folded into the GEMM that reads it (``fuse.fold_copies_into_gemm``),
 on the GPU: the GEMM reads its A operand, or its K-major B, from the transpose's source through a
-rank-3..5 tensor map (``heads_scores``: both, each with two batch dims).
+rank-3..5 tensor map (``heads_scores``: both, each with two batch dims; ``heads_attention_probs``:
+also an N-major B).
 
 Against the unfused program (copy kernel, then the GEMM on the copy) and, at the transformer
 config's head-merge size, against a PyTorch fp32 reference.  The fused and unfused GEMMs read the
@@ -25,7 +26,7 @@ def _compare(plan, ins):
     assert "copy" not in fams and all(f == "gemm_tc" for f in fams)
     assert any(k.info["a_strided"] or k.info["b_strided"] for k in fused.kernel_sources)
     assert "copy" in [k.family for k in plain.kernel_sources]
-    y1, y0 = fused(*ins)[0], plain(*ins)[0]
+    y1, y0 = fused(*ins), plain(*ins)
     torch.cuda.synchronize()
     fused.check()
     plain.check()
@@ -34,14 +35,16 @@ def _compare(plan, ins):
 
 
 @pytest.mark.parametrize("case", ["merge_heads_linear__bf16", "merge_heads_linear__f16", "transpose_bmm__bf16",
-                                  "heads_scores__bf16"])
+                                  "heads_scores__bf16", "heads_attention_probs__bf16"])
 def test_folded_copy_matches_unfused_program(case):
+    """``heads_attention_probs``: an attention whose probabilities are returned too, so it is not
+    fused; its q / k / v head splits (v as the N-major B of P·V) and its head merge are folded."""
     plan = FX.load_plan(case)
     ins = [t.cuda() for t in FX.case_inputs(case)]
-    y1, y0, same_kernel = _compare(plan, ins)
-    assert torch.equal(y1, y0) if same_kernel else normwise_error(y1, y0) <= 1e-3
-    exp = FX.case_expected(case)[0]
-    assert FX.check_against_golden(y1, exp, 2e-2) <= 2e-2
+    ys1, ys0, same_kernel = _compare(plan, ins)
+    for y1, y0, exp in zip(ys1, ys0, FX.case_expected(case)):
+        assert torch.equal(y1, y0) if same_kernel else normwise_error(y1, y0) <= 1e-3
+        assert FX.check_against_golden(y1, exp, 2e-2) <= 2e-2
 
 
 @pytest.mark.parametrize("shape", [(8, 16, 2048, 64, 1024), (3, 4, 384, 64, 256)])
@@ -54,7 +57,8 @@ def test_folded_head_merge_at_size(shape):
     x = torch.randn((B, H, S, D), generator=g, device="cuda").to(torch.bfloat16)
     w = (torch.randn((N, H * D), generator=g, device="cuda") * 0.03).to(torch.bfloat16)
     b = (torch.randn((N,), generator=g, device="cuda") * 0.1).to(torch.bfloat16)
-    y1, y0, same_kernel = _compare(plan, [x, w, b])
+    ys1, ys0, same_kernel = _compare(plan, [x, w, b])
+    y1, y0 = ys1[0], ys0[0]
     assert torch.equal(y1, y0) if same_kernel else normwise_error(y1, y0) <= 1e-3
     ref = x.float().permute(0, 2, 1, 3).reshape(B * S, H * D) @ w.float().t() + b.float()
     assert normwise_error(y1, ref) <= 2e-2

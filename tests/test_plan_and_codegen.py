@@ -617,6 +617,13 @@ def test_transpose_copy_folded_into_gemm_operand():
     assert g3.info["a_strided"] and g3.info["b_strided"] and "A_RANK = 4" in g3.source and "B_RANK = 4" in g3.source
     assert g3.tmaps[0].dims == g3.tmaps[1].dims == [64, 4, 256, 2] and g3.tmaps[1].box[2] == g3.info["BN"]
     assert "c[1] = static_cast<int>(ab % 4L);" in g3.source and "c[3] = static_cast<int>(bb / 4L);" in g3.source
+    # an unfused attention (probabilities returned): all four copies folded, v as the N-major B of
+    # P·V read in 64 x 64 chunks (n first) from the v projection's output
+    ha = fuse(FX.load_plan("heads_attention_probs__bf16"))
+    assert [k.kind for k in ha.kernels] == ["matmul"] * 4 + ["row", "matmul", "matmul"]
+    assert ha.meta["folded_copies"] == 4
+    pv = [g for g in generate(ha) if g.family == "gemm_tc"][-2]
+    assert pv.info["b_strided"] and "B_FOLDED = true" in pv.source and pv.tmaps[1].box == [64, 1, 64, 1]
     # kept as a copy: f32 (3xTF32 reads split copies), a 128-row tile that would straddle two
     # batch elements (seq 200), a K block that would straddle two heads (head dim 32)
     assert [k.kind for k in fuse(FX.load_plan("merge_heads_linear__f32")).kernels] == ["copy", "matmul"]
