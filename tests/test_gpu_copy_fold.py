@@ -23,7 +23,7 @@ def _compare(plan, ins):
     fused = B200Program(plan, device="cuda")
     plain = B200Program(plan, device="cuda", fuse_kernels=False)
     fams = [k.family for k in fused.kernel_sources]
-    assert "copy" not in fams and all(f == "gemm_tc" for f in fams)
+    assert "copy" not in fams
     assert any(k.info["a_strided"] or k.info["b_strided"] for k in fused.kernel_sources)
     assert "copy" in [k.family for k in plain.kernel_sources]
     y1, y0 = fused(*ins), plain(*ins)
