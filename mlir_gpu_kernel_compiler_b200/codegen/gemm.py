@@ -27,7 +27,7 @@ from __future__ import annotations
 import os
 
 from ..plan import PKernel, PNode, access_strides, contiguous_strides, first_consumer
-from .common import (PDL, BOUNDS_SITE, CTYPE, HEADER, ITEM, NUM_SMS, TMAP_DTYPE, KernelSource, TMapSpec, checked,
+from .common import (PDL, BOUNDS_SITE, CTYPE, HEADER, ITEM, NUM_SMS, KernelSource, TMapSpec, checked,
                      decompose_stmts, expr, fast_math_for, offset_expr, params_struct, prod, ptr_decl, split_out,
                      split_skip, split_store_lines, status_decl, tma_store_allowed)
 

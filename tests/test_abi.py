@@ -6,8 +6,6 @@ import re
 import subprocess
 from pathlib import Path
 
-import pytest
-
 from mlir_gpu_kernel_compiler_b200 import runtime as rt
 from mlir_gpu_kernel_compiler_b200 import toolchain
 

@@ -6,7 +6,6 @@ the b200 backend and executed on the GPU; every output must agree with
 within max-abs-relative (normwise) error 1e-4 for f32 and 2e-2 for bf16/f16
 (the tolerances the north star states).
 """
-import numpy as np
 import pytest
 import torch
 

@@ -1,7 +1,6 @@
 """Host-side logic without a GPU: plan serialisation, the arena planner against
 the reference planner's offsets, code generation and sm_100a compilation,
 launch geometry, and the tensorjit registration hook."""
-import json
 import math
 
 import numpy as np
