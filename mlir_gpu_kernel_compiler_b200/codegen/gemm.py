@@ -174,14 +174,15 @@ def _pack_loop(segments: list[dict], tiles: list[int], idx: list[int]) -> list[s
         L.append(f"      u -= {acc}L;")
         L.append(f"      const long kt = u % {kt}L, rt = (u / {kt}L) % {rt}L, mat = u / {kt * rt}L;")
         L.append("      for (int y = ty; y < 32; y += 8) {")
+        g = sg.get("gather")
         if sg["k_major"]:
+            off = _gather_offset(g, "mat", "r", "kk") if g else f"mat * {R * K}L + r * {K}L + kk"
             L.append("        const long r = rt * 32 + y, kk = kt * 32 + tx;")
-            L.append(f"        tile[y][tx] = (r < {R}L && kk < {K}L) ? tj_f32(src{j}[mat * {R * K}L + r * {K}L + kk]) "
-                     ": 0.0f;")
+            L.append(f"        tile[y][tx] = (r < {R}L && kk < {K}L) ? tj_f32(src{j}[{off}]) : 0.0f;")
         else:   # source [K, rows]: consecutive threads read consecutive rows
+            off = _gather_offset(g, "mat", "r", "kk") if g else f"mat * {R * K}L + kk * {R}L + r"
             L.append("        const long kk = kt * 32 + y, r = rt * 32 + tx;")
-            L.append(f"        tile[tx][y] = (r < {R}L && kk < {K}L) ? tj_f32(src{j}[mat * {R * K}L + kk * {R}L + r]) "
-                     ": 0.0f;")
+            L.append(f"        tile[tx][y] = (r < {R}L && kk < {K}L) ? tj_f32(src{j}[{off}]) : 0.0f;")
         L.append("      }")
         L.append("      __syncthreads();")
         L.append("      for (int y = ty; y < 32; y += 8) {")
@@ -234,9 +235,28 @@ def gen_epilogue_only(k: PKernel, symbol: str, kernel_id: int = 0) -> KernelSour
 
 
 def _operand_segment(node: PNode, rows: int, K: int, pitch: int, k_major: bool, split: bool, dst_dtype: str,
-                     hi: int, lo: int) -> dict:
-    return {"src": ("node", node), "src_dtype": node.dtype, "mats": prod(node.shape[:-2]), "rows": rows, "K": K,
-            "pitch": pitch, "k_major": k_major, "split": split, "dst_dtype": dst_dtype, "hi": hi, "lo": lo}
+                     hi: int, lo: int, gather: dict | None = None) -> dict:
+    """``gather``: the operand is read from a folded transpose's source (``fuse.py``): its
+    {"src", "k", "r", "b"} sub-dims give each element's offset there."""
+    src = gather["src"] if gather else node
+    return {"src": ("node", src), "src_dtype": node.dtype, "mats": prod(node.shape[:-2]), "rows": rows, "K": K,
+            "pitch": pitch, "k_major": k_major, "split": split, "dst_dtype": dst_dtype, "hi": hi, "lo": lo,
+            "gather": gather}
+
+
+def _gather_offset(g: dict, mat: str, r: str, kk: str) -> str:
+    """Offset in a folded transpose's source of operand element (mat, r, kk): each index split
+    over its sub-dims (innermost first, mixed radix) times their strides."""
+    terms = []
+    for var, dims in ((kk, g["k"]), (r, g["r"]), (mat, g["b"])):
+        div = 1
+        for q, (size, stride) in enumerate(dims):
+            v = var if div == 1 else f"({var} / {div}L)"
+            if q < len(dims) - 1:
+                v = f"({v} % {size}L)"
+            terms.append(v if stride == 1 else f"{v} * {stride}L")
+            div *= size
+    return " + ".join(terms) if terms else "0L"
 
 
 def gen_matmul(k: PKernel, symbol: str, kernel_id: int, tile: dict | None) -> list[KernelSource]:
@@ -256,9 +276,9 @@ def gen_matmul(k: PKernel, symbol: str, kernel_id: int, tile: dict | None) -> li
     ws = b_off + (_align(prod(b.shape[:-2]) * N * P * ITEM[b.dtype]) if form.pack_b else 0)
     segs = []
     if form.pack_a:
-        segs.append(_operand_segment(a, M, K, P, True, False, a.dtype, a_off, a_off))
+        segs.append(_operand_segment(a, M, K, P, True, False, a.dtype, a_off, a_off, k.attrs.get("a_gather")))
     if form.pack_b:
-        segs.append(_operand_segment(b, N, K, P, tb, False, b.dtype, b_off, b_off))
+        segs.append(_operand_segment(b, N, K, P, tb, False, b.dtype, b_off, b_off, k.attrs.get("b_gather")))
     pk = gen_pack_operands(f"{symbol}_pack", segs, kernel_id)
     g = gen_gemm_tc(k, symbol, kernel_id, tile, packed={"a": a_off if form.pack_a else None,
                                                         "b": b_off if form.pack_b else None, "pitch": P})
@@ -418,7 +438,8 @@ def gen_matmul_tc_x3(k: PKernel, symbol: str, kernel_id: int, tile: dict | None)
     BN, ksplit = x3_tile(M, N, K, batch, tile)
     tile = dict(tile or {"STAGES": 4, "GROUP_M": 16}, BN=BN)
     ws = part + (_align(ksplit * batch * M * N * 4) if ksplit > 1 else 0)
-    vec_split = a.dtype == b.dtype == "f32" and tb and K % 4 == 0
+    ga, gb = k.attrs.get("a_gather"), k.attrs.get("b_gather")      # folded transposes (fuse.py)
+    vec_split = a.dtype == b.dtype == "f32" and tb and K % 4 == 0 and not ga and not gb
     skip = split_skip(kernel_id) if vec_split else set()
     if vec_split:
         # both operands already K-major f32 with a 16-byte pitch: the vectorised split, minus the
@@ -427,8 +448,8 @@ def gen_matmul_tc_x3(k: PKernel, symbol: str, kernel_id: int, tile: dict | None)
                                       ("b", (b.numel, ("node", b), b_hi, b_lo))) if role not in skip]
         sp = gen_split_tf32(f"{symbol}_split", segs, kernel_id) if segs else None
     else:
-        sp = gen_pack_operands(f"{symbol}_split", [_operand_segment(a, M, K, P, True, True, "f32", a_hi, a_lo),
-                                                   _operand_segment(b, N, K, P, tb, True, "f32", b_hi, b_lo)],
+        sp = gen_pack_operands(f"{symbol}_split", [_operand_segment(a, M, K, P, True, True, "f32", a_hi, a_lo, ga),
+                                                   _operand_segment(b, N, K, P, tb, True, "f32", b_hi, b_lo, gb)],
                                kernel_id)
     g = gen_gemm_tc(k, symbol, kernel_id, tile, x3_scratch=(a_hi, b_hi, a_lo, b_lo),
                     ksplit=ksplit, partial_scratch=part)
@@ -516,7 +537,7 @@ class Epilogue:
         self.batch_shape = out_shape[:-2]
         self.epi_nodes = [n for n in k.nodes if n is not mm]
         # operands read from a folded transpose's source
-        srcs = [(k.attrs.get(f) or {}).get("src") for f in ("a_strided", "b_strided")]
+        srcs = [(k.attrs.get(f) or {}).get("src") for f in ("a_strided", "b_strided", "a_gather", "b_gather")]
         self.epi_inputs = [n for n in k.inputs if n is not a and n is not b and all(n is not x for x in srcs)]
         self.in_index, self.out_index = in_index, out_index
         self.strides = {}

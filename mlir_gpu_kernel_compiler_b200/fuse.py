@@ -232,7 +232,7 @@ def _subdims(sizes_strides: list[tuple[int, int]]) -> list[tuple[int, int]]:
 
 
 def strided_operand_layout(plan: PProgram, k: PKernel, which: int, escaping: set[int],
-                           taken: frozenset = frozenset()) -> Optional[dict]:
+                           taken: frozenset = frozenset(), gather: bool = False) -> Optional[dict]:
     """How operand ``which`` (0 = A, 1 = B) of a bf16/f16 matmul kernel could be read straight
     from the source of the ``copy`` kernel (a transpose) that materialises it, instead of from
     the copy's output.
@@ -246,7 +246,11 @@ def strided_operand_layout(plan: PProgram, k: PKernel, which: int, escaping: set
     A, of 256 for B), at most two batch dims, rank <= 5, 16-byte strides; X not read elsewhere in
     the kernel, T read only here and not a program output.  ``taken``: copy kernels already
     folded into the other operand.  Returns {"src", "copy", "dims": [(size, stride)], "k_dims",
-    "r_dims", "batch_dims", "n_major"} or None."""
+    "r_dims", "batch_dims", "n_major"} or None.
+
+    ``gather``: the operand goes through the GEMM's pack / split pre-pass, which computes each
+    element's offset in X itself: any dtype, any number of sub-dims, none of the tensor-map
+    conditions; returns {"src", "copy", "k", "r", "b": [(size, stride)] innermost first}."""
     mm = k.anchor
     if k.kind != "matmul" or mm is None or mm.op != "matmul":
         return None
@@ -254,8 +258,8 @@ def strided_operand_layout(plan: PProgram, k: PKernel, which: int, escaping: set
     a, b = mm.inputs
     o = mm.inputs[which]
     t = plan.resolve(o)
-    if (t.op != "transpose" or a.dtype not in ("bf16", "f16") or b.dtype != a.dtype or t.id in escaping
-            or o.id in escaping):
+    if (t.op != "transpose" or (not gather and (a.dtype not in ("bf16", "f16") or b.dtype != a.dtype))
+            or t.id in escaping or o.id in escaping):
         return None
     copy_i = next((i for i, c in enumerate(plan.kernels) if c.kind == "copy" and len(c.nodes) == 1
                    and c.nodes[0] is t and c.outputs == [t]), None)
@@ -291,6 +295,8 @@ def strided_operand_layout(plan: PProgram, k: PKernel, which: int, escaping: set
     inner, outer = _subdims(groups[-1])[::-1], _subdims(groups[-2])[::-1]     # innermost first
     k_dims, r_dims = (outer, inner) if n_major else (inner, outer)
     batch_dims = _subdims([d for g in groups[:-2] for d in g])[::-1]
+    if gather:
+        return {"src": x, "copy": copy_i, "k": k_dims, "r": r_dims, "b": batch_dims}
     if not inner or inner[0][1] != 1 or len(k_dims) > 2 or len(r_dims) > 2 or len(batch_dims) > 2:
         return None
     if len(inner) == 1 and int(o.shape[-1]) % 8:
@@ -314,22 +320,45 @@ def strided_a_layout(plan: PProgram, k: PKernel, escaping: set[int]) -> Optional
 
 
 def fold_copies_into_gemm(plan: PProgram) -> PProgram:
-    """A transpose ``copy`` kernel whose output only feeds a bf16/f16 GEMM's A or B operand is
-    removed: the GEMM reads that operand from the transpose's
-    source through a permuted-stride tensor map (``strided_operand_layout``), saving the copy's
-    HBM round trip.  Outputs are unchanged."""
+    """A transpose ``copy`` kernel whose output only feeds a GEMM operand is removed, saving its
+    HBM round trip: a bf16/f16 GEMM reads that operand from the transpose's source through a
+    permuted-stride tensor map (``strided_operand_layout``); a GEMM whose operands go through a
+    pack / split pre-pass (f32 3xTF32, odd pitches) has that launch gather them from the source
+    instead.  Outputs are unchanged."""
     from .codegen.gemm import gemm_form
 
     escaping = {plan.resolve(o).id for o in plan.outputs}
     drop, replace = set(), {}
     for i, k in enumerate(plan.kernels):
+        if k.kind != "matmul" or k.anchor is None or k.anchor.op != "matmul":
+            continue
         lay_a = strided_operand_layout(plan, k, 0, escaping)
         lay_b = strided_operand_layout(plan, k, 1, escaping,
                                        frozenset({lay_a["copy"]}) if lay_a else frozenset())
-        if lay_a is None and lay_b is None:
-            continue
         f = gemm_form(k)
         if f.mode != "f16" or f.pack_a or f.pack_b:
+            lay_a = lay_b = None
+        if lay_a is None and lay_b is None:
+            # operands copied by the GEMM's pack / split pre-pass: that launch gathers them from
+            # the transpose's source instead (3xTF32 splits both operands; a pack, those it packs)
+            if f.mode not in ("x3", "f16"):
+                continue
+            ga = strided_operand_layout(plan, k, 0, escaping, gather=True) if f.mode == "x3" or f.pack_a else None
+            gb = (strided_operand_layout(plan, k, 1, escaping, frozenset({ga["copy"]}) if ga else frozenset(),
+                                         gather=True) if f.mode == "x3" or f.pack_b else None)
+            if ga is None and gb is None:
+                continue
+            attrs, subst = dict(k.attrs), {}
+            for name, lay, node in (("a_gather", ga, k.anchor.inputs[0]), ("b_gather", gb, k.anchor.inputs[1])):
+                if lay is not None:
+                    attrs[name] = {key: lay[key] for key in ("src", "k", "r", "b")}
+                    subst[node.id] = lay["src"]
+                    drop.add(lay["copy"])
+            fk = PKernel(kind="matmul", nodes=list(k.nodes), anchor=k.anchor,
+                         inputs=[subst.get(n.id, n) for n in k.inputs], outputs=list(k.outputs),
+                         iter_shape=tuple(k.iter_shape))
+            fk.attrs = attrs
+            replace[i] = fk
             continue
         attrs, subst = dict(k.attrs), {}
         for name, lay, node in (("a_strided", lay_a, k.anchor.inputs[0]), ("b_strided", lay_b, k.anchor.inputs[1])):
@@ -352,8 +381,8 @@ def fold_copies_into_gemm(plan: PProgram) -> PProgram:
 
 def _plain_shared_a_matmul(k: PKernel):
     """(A, B, N) of a kernel that is a bare bf16/f16 ``A @ Bᵀ`` (2-D, no epilogue), else None."""
-    if (k.kind != "matmul" or len(k.nodes) != 1 or k.outputs != [k.anchor] or k.attrs.get("a_strided")
-            or k.attrs.get("b_strided")):
+    if (k.kind != "matmul" or len(k.nodes) != 1 or k.outputs != [k.anchor]
+            or any(k.attrs.get(f) for f in ("a_strided", "b_strided", "a_gather", "b_gather"))):
         return None
     mm = k.anchor
     if mm.op != "matmul" or not mm.attrs.get("trans_b"):

@@ -623,9 +623,14 @@ def test_transpose_copy_folded_into_gemm_operand():
     assert ha.meta["folded_copies"] == 4
     pv = [g for g in generate(ha) if g.family == "gemm_tc"][-2]
     assert pv.info["b_strided"] and "B_FOLDED = true" in pv.source and pv.tmaps[1].box == [64, 1, 64, 1]
-    # kept as a copy: f32 (3xTF32 reads split copies), a 128-row tile that would straddle two
-    # batch elements (seq 200), a K block that would straddle two heads (head dim 32)
-    assert [k.kind for k in fuse(FX.load_plan("merge_heads_linear__f32")).kernels] == ["copy", "matmul"]
+    # f32 (3xTF32): the split launch gathers A from the transpose's source instead of a tensor map
+    f32 = fuse(FX.load_plan("merge_heads_linear__f32"))
+    assert [k.kind for k in f32.kernels] == ["matmul"] and "a_gather" in f32.kernels[0].attrs
+    sp = generate(f32)[0]
+    assert sp.family == "split" and sp.args[0][1].op == "input"
+    assert "(kk % 64L) + (kk / 64L) * 16384L + (r % 256L) * 64L + (r / 256L) * 65536L" in sp.source
+    # kept as a copy: a 128-row tile that would straddle two batch elements (seq 200), a K block
+    # that would straddle two heads (head dim 32)
     for shape in ((2, 4, 200, 64, 128), (2, 8, 256, 32, 128)):
         p = FX.merge_heads_plan(*shape)
         assert [k.kind for k in fuse(p).kernels] == ["copy", "matmul"], shape
